@@ -1,0 +1,77 @@
+"""ctypes binding of libdrinkme_b200.so (the C ABI of include/drinkme_b200.h).
+
+The library is built in-tree (``python -m drinkme_b200.build``). There is no
+fallback: a missing library, or a call that fails, raises.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdrinkme_b200.so")
+
+DM_OK, DM_EINVAL, DM_ECUDA, DM_EDEVICE, DM_ENOMEM = 0, 1, 2, 3, 4
+DM_BF16, DM_F32 = 0, 1
+DM_MC_MAX = 8
+
+EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv", "dm_decode",
+           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check")
+
+
+class DrinkmeError(RuntimeError):
+    """A C-ABI call failed; .status is the DM_* code."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(msg)
+        self.status = status
+
+
+class TensorInfo(ct.Structure):
+    _fields_ = [("R", ct.c_int64), ("C", ct.c_int64), ("row_begin", ct.c_int64), ("rows", ct.c_int64),
+                ("block_size", ct.c_int32), ("nwidths", ct.c_int32), ("widths", ct.c_int32 * 8),
+                ("nblocks", ct.c_int64), ("payload_words", ct.c_int64), ("read_bytes", ct.c_int64),
+                ("resident_bytes", ct.c_int64), ("fast_path", ct.c_int32), ("device", ct.c_int32)]
+
+
+_LIB = None
+
+
+def lib():
+    """The loaded library; raises when it was not built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"drinkme_b200: the CUDA library is not built ({LIB_PATH}); "
+                              "run `python -m drinkme_b200.build`")
+        L = ct.CDLL(LIB_PATH)
+        p, i32, i64, sz = ct.c_void_p, ct.c_int32, ct.c_int64, ct.c_size_t
+        cp = ct.c_char_p
+        L.dm_version.argtypes = []
+        L.dm_tensor_create.argtypes = [p, sz, p, sz, p, sz, i64, i64, p, i32, i32, i64, i64, i32, ct.POINTER(p), cp, sz]
+        L.dm_tensor_clone.argtypes = [p, ct.POINTER(p), cp, sz]
+        L.dm_tensor_destroy.argtypes = [p]
+        L.dm_tensor_get_info.argtypes = [p, ct.POINTER(TensorInfo)]
+        L.dm_gemv.argtypes = [p, p, i32, i64, p, p, i32, p, cp, sz]
+        L.dm_decode.argtypes = [p, p, p, cp, sz]
+        L.dm_prepare_schedule.argtypes = [p, sz, p, i64, p, i32, i32, i64, p, p, cp, sz]
+        L.dm_gemv_raw.argtypes = [p, i64, i64, p, i32, i64, p, p, i32, p, cp, sz]
+        L.dm_pack_plan.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, ct.POINTER(ct.c_uint64), cp, sz]
+        L.dm_pack_encode.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, p, ct.c_uint64, cp, sz]
+        L.dm_tensor_check.argtypes = [p, ct.POINTER(ct.c_int32), cp, sz]
+        for name in EXPORTS:
+            getattr(L, name).restype = ct.c_int
+        _LIB = L
+    return _LIB
+
+
+def call(fn: str, *args) -> None:
+    """Call an entry point with the (err, err_len) tail appended; raise on a
+    nonzero status (ValueError for DM_EINVAL, DrinkmeError otherwise)."""
+    err = ct.create_string_buffer(1024)
+    rc = getattr(lib(), fn)(*args, err, 1024)
+    if rc != DM_OK:
+        msg = err.value.decode(errors="replace") or f"{fn} failed with status {rc}"
+        if rc == DM_EINVAL:
+            raise ValueError(msg)
+        raise DrinkmeError(rc, msg)

@@ -1,0 +1,278 @@
+// The extern "C" entry points of libdrinkme_b200.so (declared in
+// include/drinkme_b200.h): tensor load/free, the GEMV dispatch, decode, the
+// gulp schedule, the raw GEMV and the device error word.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "dm_internal.h"
+
+namespace dm {
+
+void set_error(char *err, size_t len, const std::string &msg) {
+    if (err && len) {
+        size_t n = std::min(len - 1, msg.size());
+        std::memcpy(err, msg.data(), n);
+        err[n] = 0;
+    }
+}
+
+}  // namespace dm
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int fail(char *err, size_t len, int code, const std::string &msg) {
+    dm::set_error(err, len, msg);
+    return code;
+}
+
+int cuda_fail(char *err, size_t len, cudaError_t e, const char *what) {
+    return fail(err, len, DM_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void free_tensor(dm_tensor *t) {
+    if (!t) return;
+    DeviceGuard g(t->device);
+    if (t->d_data) cudaFree(t->d_data);
+    if (t->d_unit16) cudaFree(t->d_unit16);
+    if (t->S.partials) cudaFree(t->S.partials);
+    if (t->S.counters) cudaFree(t->S.counters);
+    if (t->S.xsplit) cudaFree(t->S.xsplit);
+    if (t->S.err) cudaFree(t->S.err);
+    delete t;
+}
+
+}  // namespace
+
+extern "C" int dm_version(void) { return 100; }
+
+extern "C" int dm_tensor_create(const uint8_t *palette, size_t npalette, const uint32_t *offsets, size_t noffsets,
+                                const uint32_t *data, size_t nwords, int64_t R, int64_t C, const int32_t *widths,
+                                int32_t nwidths, int32_t block_size, int64_t row_begin, int64_t row_end,
+                                int32_t device, dm_tensor **out, char *err, size_t err_len) {
+    if (!out || !offsets || !data || !widths || (!palette && npalette))
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_create: null pointer");
+    *out = nullptr;
+    std::string msg;
+    if (nwidths < 2 || nwidths > 8)
+        return fail(err, err_len, DM_EINVAL, "radix needs 2..8 widths in 1..8, ending with the exponent width");
+    if (dm::validate_pack(palette, npalette, offsets, noffsets, nwords, R, C, widths, nwidths, block_size, msg))
+        return fail(err, err_len, DM_EINVAL, msg);
+    dm_tensor *t = new dm_tensor();
+    t->device = device;
+    std::string bytes, unit16;
+    if (dm::build_layout(palette, npalette, offsets, data, nwords, R, C, widths, nwidths, block_size, row_begin,
+                         row_end, t->L, bytes, unit16, msg)) {
+        delete t;
+        return fail(err, err_len, DM_EINVAL, msg);
+    }
+    DeviceGuard g(device);
+    cudaError_t e;
+    cudaDeviceGetAttribute(&t->sms, cudaDevAttrMultiProcessorCount, device);
+    if ((e = cudaMalloc(&t->d_data, bytes.size())) != cudaSuccess) {
+        free_tensor(t);
+        return cuda_fail(err, err_len, e, "cudaMalloc(layout)");
+    }
+    t->data_bytes = bytes.size();
+    if ((e = cudaMalloc(&t->d_unit16, unit16.size())) != cudaSuccess) {
+        free_tensor(t);
+        return cuda_fail(err, err_len, e, "cudaMalloc(unit directory)");
+    }
+    if ((e = cudaMemcpy(t->d_data, bytes.data(), bytes.size(), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(t->d_unit16, unit16.data(), unit16.size(), cudaMemcpyHostToDevice)) != cudaSuccess) {
+        free_tensor(t);
+        return cuda_fail(err, err_len, e, "cudaMemcpy(layout)");
+    }
+    t->resident_bytes = bytes.size() + unit16.size();
+    if ((e = cudaMalloc(&t->S.err, sizeof(int))) != cudaSuccess || (e = cudaMemset(t->S.err, 0, sizeof(int))) != cudaSuccess) {
+        free_tensor(t);
+        return cuda_fail(err, err_len, e, "cudaMalloc(error word)");
+    }
+    if (t->L.fast_sip) {
+        const int64_t workers = std::min<int64_t>((int64_t)t->sms * 8, t->L.units);
+        t->S.max_workers = (int32_t)workers;
+        const size_t pbytes = (size_t)workers * 2 * 64 * sizeof(float);
+        const size_t cbytes = (size_t)t->L.tiles * sizeof(int);
+        const size_t xbytes = (size_t)6 * (size_t)t->L.C * 2;
+        if ((e = cudaMalloc(&t->S.partials, pbytes)) != cudaSuccess ||
+            (e = cudaMalloc(&t->S.counters, cbytes)) != cudaSuccess ||
+            (e = cudaMemset(t->S.counters, 0, cbytes)) != cudaSuccess ||
+            (e = cudaMalloc(&t->S.xsplit, xbytes)) != cudaSuccess) {
+            free_tensor(t);
+            return cuda_fail(err, err_len, e, "cudaMalloc(scratch)");
+        }
+        t->resident_bytes += pbytes + cbytes + xbytes;
+    }
+    *out = t;
+    return DM_OK;
+}
+
+extern "C" int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err, size_t err_len) {
+    if (!src || !out) return fail(err, err_len, DM_EINVAL, "dm_tensor_clone: null pointer");
+    *out = nullptr;
+    DeviceGuard g(src->device);
+    dm_tensor *t = new dm_tensor();
+    t->device = src->device;
+    t->L = src->L;
+    t->sms = src->sms;
+    t->data_bytes = src->data_bytes;
+    t->S.max_workers = src->S.max_workers;
+    cudaError_t e;
+    const size_t ubytes = (size_t)(src->L.units + 1) * sizeof(uint32_t);
+    if ((e = cudaMalloc(&t->d_data, src->data_bytes)) != cudaSuccess ||
+        (e = cudaMemcpy(t->d_data, src->d_data, src->data_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess ||
+        (e = cudaMalloc(&t->d_unit16, ubytes)) != cudaSuccess ||
+        (e = cudaMemcpy(t->d_unit16, src->d_unit16, ubytes, cudaMemcpyDeviceToDevice)) != cudaSuccess ||
+        (e = cudaMalloc(&t->S.err, sizeof(int))) != cudaSuccess ||
+        (e = cudaMemset(t->S.err, 0, sizeof(int))) != cudaSuccess) {
+        free_tensor(t);
+        return cuda_fail(err, err_len, e, "dm_tensor_clone");
+    }
+    t->resident_bytes = src->data_bytes + ubytes;
+    if (src->L.fast_sip) {
+        const size_t pbytes = (size_t)t->S.max_workers * 2 * 64 * sizeof(float);
+        const size_t cbytes = (size_t)t->L.tiles * sizeof(int);
+        const size_t xbytes = (size_t)6 * (size_t)t->L.C * 2;
+        if ((e = cudaMalloc(&t->S.partials, pbytes)) != cudaSuccess ||
+            (e = cudaMalloc(&t->S.counters, cbytes)) != cudaSuccess ||
+            (e = cudaMemset(t->S.counters, 0, cbytes)) != cudaSuccess ||
+            (e = cudaMalloc(&t->S.xsplit, xbytes)) != cudaSuccess) {
+            free_tensor(t);
+            return cuda_fail(err, err_len, e, "dm_tensor_clone(scratch)");
+        }
+        t->resident_bytes += pbytes + cbytes + xbytes;
+    }
+    *out = t;
+    return DM_OK;
+}
+
+extern "C" int dm_tensor_destroy(dm_tensor *t) {
+    free_tensor(t);
+    return DM_OK;
+}
+
+extern "C" int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info) {
+    if (!t || !info) return DM_EINVAL;
+    std::memset(info, 0, sizeof(*info));
+    info->R = t->L.R;
+    info->C = t->L.C;
+    info->row_begin = t->L.row0;
+    info->rows = t->L.rows;
+    info->block_size = t->L.B;
+    info->nwidths = t->L.nw;
+    for (int i = 0; i < 8; ++i) info->widths[i] = t->L.widths[i];
+    info->nblocks = t->L.rows * t->L.NB;
+    info->payload_words = t->L.payload_words;
+    info->read_bytes = t->L.read_bytes;
+    info->resident_bytes = (int64_t)t->resident_bytes;
+    info->fast_path = t->L.fast_sip ? 1 : 0;
+    info->device = t->device;
+    return DM_OK;
+}
+
+extern "C" int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
+                       int32_t out_dtype, void *stream, char *err, size_t err_len) {
+    if (!t || !x || !out) return fail(err, err_len, DM_EINVAL, "dm_gemv: null pointer");
+    if (M < 1 || M > DM_MC_MAX)
+        return fail(err, err_len, DM_EINVAL,
+                    "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
+    if ((x_dtype != DM_BF16 && x_dtype != DM_F32) || (out_dtype != DM_BF16 && out_dtype != DM_F32))
+        return fail(err, err_len, DM_EINVAL, "dm_gemv: dtype must be DM_BF16 or DM_F32");
+    DeviceGuard g(t->device);
+    std::string msg;
+    const uint16_t *b16 = reinterpret_cast<const uint16_t *>(bias);
+    const int of32 = out_dtype == DM_F32;
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    int rc;
+    if (t->L.fast_sip && aligned) {
+        if (x_dtype == DM_BF16) {
+            rc = dm::launch_gemv_sip(t, reinterpret_cast<const uint16_t *>(x), t->L.C, (int)M, 1, (int)M, b16, out,
+                                     of32, stream, msg);
+        } else {
+            rc = DM_OK;
+            const size_t esz = of32 ? 4 : 2;
+            for (int64_t m0 = 0; m0 < M && rc == DM_OK; m0 += 2) {
+                const int64_t mm = std::min<int64_t>(2, M - m0);
+                rc = dm::launch_split_f32(reinterpret_cast<const float *>(x) + m0 * t->L.C, t->L.C, mm, t->S.xsplit,
+                                          stream, msg);
+                if (rc == DM_OK)
+                    rc = dm::launch_gemv_sip(t, t->S.xsplit, t->L.C, (int)(3 * mm), 3, (int)mm, b16,
+                                             reinterpret_cast<uint8_t *>(out) + (size_t)m0 * t->L.rows * esz, of32,
+                                             stream, msg);
+            }
+        }
+    } else {
+        rc = dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);
+    }
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *err, size_t err_len) {
+    if (!t || !out) return fail(err, err_len, DM_EINVAL, "dm_decode: null pointer");
+    DeviceGuard g(t->device);
+    std::string msg;
+    int rc = dm::launch_decode_generic(t, out, stream, msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *offsets, int64_t C,
+                                   const int32_t *widths, int32_t nwidths, int32_t block_size, int64_t nblocks,
+                                   uint16_t *out, void *stream, char *err, size_t err_len) {
+    if (!data || !offsets || !widths || !out) return fail(err, err_len, DM_EINVAL, "dm_prepare_schedule: null pointer");
+    if (nwidths < 2 || nwidths > 8 || block_size < 32 || block_size > 4096 || C <= 0)
+        return fail(err, err_len, DM_EINVAL, "dm_prepare_schedule: invalid parameters");
+    std::string msg;
+    int rc = dm::launch_prepare_schedule(data, nwords, offsets, C, widths, nwidths, block_size, nblocks, out, stream,
+                                         msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int32_t x_dtype, int64_t M,
+                           const void *bias, void *out, int32_t out_dtype, void *stream, char *err, size_t err_len) {
+    if (!w || !x || !out) return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: null pointer");
+    if (M < 1 || M > DM_MC_MAX)
+        return fail(err, err_len, DM_EINVAL,
+                    "gemv_narrow: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
+    if (R <= 0 || C <= 0) return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: empty weight");
+    if ((x_dtype != DM_BF16 && x_dtype != DM_F32) || (out_dtype != DM_BF16 && out_dtype != DM_F32))
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: dtype must be DM_BF16 or DM_F32");
+    const bool vec_ok = (C % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
+    if (!vec_ok && (C % 8 == 0))
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: weight and activations must be 16-byte aligned");
+    std::string msg;
+    int rc = dm::launch_gemv_raw(w, R, C, x, x_dtype == DM_F32, M, reinterpret_cast<const uint16_t *>(bias), out,
+                                 out_dtype == DM_F32, stream, msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_tensor_check(const dm_tensor *t, int32_t *device_error, char *err, size_t err_len) {
+    if (!t || !device_error) return fail(err, err_len, DM_EINVAL, "dm_tensor_check: null pointer");
+    DeviceGuard g(t->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaDeviceSynchronize");
+    int v = 0;
+    if ((e = cudaMemcpy(&v, t->S.err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(err, err_len, e, "cudaMemcpy(error word)");
+    if (v && (e = cudaMemset(t->S.err, 0, sizeof(int))) != cudaSuccess)
+        return cuda_fail(err, err_len, e, "cudaMemset(error word)");
+    *device_error = v;
+    return DM_OK;
+}

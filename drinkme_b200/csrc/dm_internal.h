@@ -1,0 +1,102 @@
+// Internal declarations shared by the host layout code, the kernels and the
+// C ABI of libdrinkme_b200.so.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/drinkme_b200.h"
+
+namespace dm {
+
+// Rows per unit: a unit is 8 consecutive rows x one block column, the work
+// item of the GEMV kernels and the granularity of the device layout. Eight
+// rows are the n = 8 side of one m16n8k16 MMA (the weights are its B
+// operand, the activations its A operand).
+constexpr int kUnitRows = 8;
+// Bytes of a unit's header: per row slot {u16 off16, u16 nesc, u16 sched,
+// u16 words}.
+constexpr int kUnitHeader = kUnitRows * 8;
+// Activations staged per unit: one 1024-weight block column of every
+// virtual activation row, row stride 2048 + 16 bytes (an odd number of
+// 16-byte slots, so the 8-lane phases of the B-fragment loads do not
+// collide on shared-memory banks).
+constexpr int kXRowStride = 2048 + 16;
+constexpr int kMaxVirtualRows = 8;
+
+struct RowEntry {
+    uint16_t off16;  // row-block stream start, in 16-byte units from the unit start
+    uint16_t nesc;   // sip fast path: escapes (tier-0 code 7) in the block; else 0
+    uint16_t sched;  // >= 3 tiers: the reference's per-block schedule (radix_pack.schedule_np)
+    uint16_t words;  // the block's word count in the pack (0: absent row)
+};
+static_assert(sizeof(RowEntry) == 8, "row entry is 8 bytes");
+
+struct TensorLayout {
+    int64_t R = 0, C = 0, row0 = 0, rows = 0;
+    int32_t B = 0, nw = 0, widths[8] = {0};
+    int32_t covered = 0;
+    uint8_t palette[256] = {0};
+    int64_t NB = 0, tiles = 0, units = 0;
+    int64_t payload_words = 0;  // NW of this shard
+    int64_t read_bytes = 0;
+    bool fast_sip = false;
+    int32_t max_unit_bytes = 0;
+    // padded palette words (radix_pack.padded_palette_words): nonterminal tiers,
+    // each (1 << w) - 1 bytes zero-padded to whole words
+    uint32_t pal_words[24] = {0};
+    int32_t npal_words = 0;
+    // per-tier word offset of each tier's table inside pal_words
+    int32_t tier_table[8] = {0};
+};
+
+struct Scratch {
+    float *partials = nullptr;   // [max_workers][2][8 rows][8 virtual rows]
+    int *counters = nullptr;     // [tiles] arrival counters, zero between calls
+    uint16_t *xsplit = nullptr;  // [6][C] bf16 hi/mid/lo rows of an fp32 activation pair
+    int *err = nullptr;          // device error word
+    int32_t max_workers = 0;
+};
+
+}  // namespace dm
+
+struct dm_tensor {
+    int32_t device = 0;
+    dm::TensorLayout L;
+    uint8_t *d_data = nullptr;     // unit-major layout + tail pad
+    size_t data_bytes = 0;
+    uint32_t *d_unit16 = nullptr;  // [units + 1] unit starts in 16-byte units
+    dm::Scratch S;
+    int32_t sms = 148;
+    size_t resident_bytes = 0;
+};
+
+namespace dm {
+
+void set_error(char *err, size_t len, const std::string &msg);
+
+// Host layout (layout.cpp)
+int validate_pack(const uint8_t *palette, size_t npal, const uint32_t *offsets, size_t noff, size_t nwords,
+                  int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, std::string &msg);
+int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, const uint32_t *data,
+                 size_t nwords, int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B,
+                 int64_t row0, int64_t row1, TensorLayout &L, std::string &bytes, std::string &unit16,
+                 std::string &msg);
+int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw);
+
+// Kernel launchers (kernels.cu)
+int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
+int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,
+                        int out_f32, void *stream, std::string &msg);
+int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
+                    const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg);
+int launch_split_f32(const float *x, int64_t C, int64_t M, uint16_t *out, void *stream, std::string &msg);
+int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *offsets, int64_t C,
+                            const int32_t *widths, int32_t nw, int32_t B, int64_t nblocks, uint16_t *out,
+                            void *stream, std::string &msg);
+int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
+                    void *out, int out_f32, void *stream, std::string &msg);
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *consumers);
+
+}  // namespace dm

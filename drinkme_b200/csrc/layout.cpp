@@ -1,0 +1,287 @@
+// Host side of the loader: descriptor validation and the B200 device layout.
+//
+// The pack stays pack format 1 on disk (src/drinkme/codec/radix_pack.py:9-21).
+// What changes is only where the bytes sit on the device: the reference keeps
+// the payload verbatim plus a zero pad (swap.to_device_radix,
+// src/drinkme/codec/swap.py:80-161); this loader regroups the same block
+// words into UNITS of 8 rows x 1 block column, each unit contiguous and
+// 16-byte aligned so one bulk copy stages it into shared memory:
+//
+//   unit  = [8 x RowEntry header][row-block streams, each 16-byte aligned]
+//           [sip fast path: per row, the escape index — the uint16 position
+//            of every tier-0 escape (code 7) in block order, 16-byte aligned]
+//           [sip fast path, ragged last tile only: one null block whose
+//            weights all decode to +0]
+//   units in tile-major order (tile = 8 rows; all block columns of a tile
+//   before the next tile), then a zero tail pad as long as the widest block
+//   (radix.block_word_bounds(B)[1] words), so no reader leaves the buffer.
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "dm_internal.h"
+
+namespace dm {
+
+static int64_t cw(int64_t count, int64_t width) { return (count * width + 31) / 32; }
+
+int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw) {
+    int64_t m = cw(n, 8);
+    for (int i = 0; i < nw - 1; ++i) m += cw(n, widths[i]);
+    return m + cw(n, 8);
+}
+
+static int64_t block_words_fewest(int64_t n, const int32_t *widths) { return cw(n, 8) + cw(n, widths[0]); }
+
+template <class F>
+static void parallel_for(int64_t n, F fn) {
+    unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    int64_t threads = std::min<int64_t>(hw, std::max<int64_t>(1, n / 256));
+    if (threads <= 1) {
+        for (int64_t i = 0; i < n; ++i) fn(i);
+        return;
+    }
+    std::atomic<int64_t> next(0);
+    std::vector<std::thread> pool;
+    for (int64_t t = 0; t < threads; ++t)
+        pool.emplace_back([&]() {
+            for (;;) {
+                int64_t s = next.fetch_add(1024);
+                if (s >= n) break;
+                int64_t e = std::min(n, s + 1024);
+                for (int64_t i = s; i < e; ++i) fn(i);
+            }
+        });
+    for (auto &th : pool) th.join();
+}
+
+// radix.py:174-238 (validate) with its messages, plus the widths rule of
+// radix.py:139-146.
+int validate_pack(const uint8_t *palette, size_t npal, const uint32_t *offsets, size_t noff, size_t nwords,
+                  int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, std::string &msg) {
+    if (R <= 0 || C <= 0) { msg = "invalid radix shape or raw flag"; return 1; }
+    if (B < 32 || B > 4096 || (B & (B - 1))) { msg = "invalid radix block size"; return 1; }
+    if (nw < 2 || nw > 8 || widths[nw - 1] != 8) {
+        msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
+        return 1;
+    }
+    int64_t covered = 0;
+    for (int i = 0; i < nw; ++i)
+        if (widths[i] < 1 || widths[i] > 8) {
+            msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
+            return 1;
+        }
+    for (int i = 0; i < nw - 1; ++i) covered += (1 << widths[i]) - 1;
+    if (covered > 256) { msg = "radix tiers exceed the exponent alphabet"; return 1; }
+    if ((int64_t)npal != covered) { msg = "invalid radix palette entries"; return 1; }
+    bool seen[256] = {false};
+    for (size_t i = 0; i < npal; ++i) {
+        if (seen[palette[i]]) { msg = "invalid radix palette entries"; return 1; }
+        seen[palette[i]] = true;
+    }
+    int64_t per_row = (C + B - 1) / B, nb = R * per_row;
+    if ((int64_t)noff != nb + 1 || offsets[0] != 0 || (int64_t)offsets[nb] != (int64_t)nwords) {
+        msg = "invalid radix block offsets";
+        return 1;
+    }
+    for (int64_t i = 0; i < nb; ++i) {
+        if (offsets[i + 1] <= offsets[i]) { msg = "invalid radix block offsets"; return 1; }
+    }
+    for (int64_t i = 0; i < nb; ++i) {
+        int64_t n = std::min<int64_t>(B, C - (i % per_row) * B);
+        int64_t len = (int64_t)offsets[i + 1] - (int64_t)offsets[i];
+        int64_t fewest = block_words_fewest(n, widths), most = block_words_most(n, widths, nw);
+        if (len < fewest) {
+            msg = "invalid radix block offsets: block " + std::to_string(i) + " holds " + std::to_string(len) +
+                  " word(s), fewer than the " + std::to_string(fewest) + " its literal plane and first tier take for " +
+                  std::to_string(n) + " weights";
+            return 1;
+        }
+        if (len > most) {
+            msg = "invalid radix block offsets: block " + std::to_string(i) + " holds " + std::to_string(len) +
+                  " words, more than the " + std::to_string(most) + " any block of " + std::to_string(n) +
+                  " weights can use";
+            return 1;
+        }
+    }
+    return 0;
+}
+
+static inline uint32_t field_at(const uint32_t *w, int64_t avail, int64_t index, int32_t width) {
+    int64_t bit = index * width;
+    int64_t wi = bit >> 5;
+    uint32_t lo = (uint32_t)(bit & 31);
+    uint64_t a = wi < avail ? w[wi] : 0, b = wi + 1 < avail ? w[wi + 1] : 0;
+    uint64_t v = (a >> lo) | (lo + width > 32 ? (b << (32 - lo)) : 0);
+    return (uint32_t)(v & ((1u << width) - 1));
+}
+
+// The sip escape positions of one full 1024-weight block: tier-0 codes
+// equal to 7, in block order. Counts only; positions written when out != 0.
+static int sip_escapes(const uint32_t *tier0, uint16_t *out) {
+    int count = 0;
+    for (int g = 0; g < 32; ++g) {  // 32 codes per 3 words
+        unsigned __int128 v = (unsigned __int128)tier0[3 * g] | ((unsigned __int128)tier0[3 * g + 1] << 32) |
+                              ((unsigned __int128)tier0[3 * g + 2] << 64);
+        unsigned __int128 f = v & (v >> 1) & (v >> 2);
+        uint32_t m = 0;
+        for (int j = 0; j < 32; ++j) m |= (uint32_t)((f >> (3 * j)) & 1) << j;
+        while (m) {
+            int j = __builtin_ctz(m);
+            m &= m - 1;
+            if (out) out[count] = (uint16_t)(32 * g + j);
+            ++count;
+        }
+    }
+    return count;
+}
+
+// radix_pack.py:376-411 (schedule_np) for one block: byte (k-1) = word
+// length of nonterminal tier k (k >= 1); reads past `avail` are zero.
+static uint16_t block_schedule(const uint32_t *blk, int64_t avail, int64_t n, const int32_t *widths, int32_t nw) {
+    if (nw <= 2) return 0;
+    int64_t pos = cw(n, 8), count = n;
+    uint32_t header = 0;
+    for (int t = 0; t < nw - 1; ++t) {
+        int32_t w = widths[t];
+        int64_t words = cw(count, w);
+        if (t > 0) header |= (uint32_t)words << ((t - 1) * 8);
+        if (t < nw - 2) {
+            uint32_t esc = (1u << w) - 1;
+            int64_t kept = 0;
+            for (int64_t i = 0; i < count; ++i)
+                if (field_at(blk + pos, avail - pos, i, w) == esc) ++kept;
+            count = kept;
+        }
+        pos += words;
+    }
+    return (uint16_t)header;
+}
+
+static inline int64_t a16(int64_t bytes) { return (bytes + 15) & ~int64_t(15); }
+
+int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, const uint32_t *data,
+                 size_t nwords, int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, int64_t row0,
+                 int64_t row1, TensorLayout &L, std::string &bytes, std::string &unit16, std::string &msg) {
+    if (row0 < 0 || row1 > R || row1 <= row0) { msg = "invalid row range"; return 1; }
+    L = TensorLayout();
+    L.R = R; L.C = C; L.row0 = row0; L.rows = row1 - row0; L.B = B; L.nw = nw;
+    for (int i = 0; i < nw; ++i) L.widths[i] = widths[i];
+    L.covered = (int32_t)npal;
+    std::memcpy(L.palette, palette, npal);
+    L.NB = (C + B - 1) / B;
+    L.tiles = (L.rows + kUnitRows - 1) / kUnitRows;
+    L.units = L.tiles * L.NB;
+    L.fast_sip = nw == 2 && widths[0] == 3 && B == 1024 && C % 1024 == 0;
+    {  // padded palette words (radix_pack.py:333-350)
+        int32_t wpos = 0, base = 0;
+        std::vector<uint8_t> t;
+        for (int i = 0; i < nw - 1; ++i) {
+            int32_t n = (1 << widths[i]) - 1, padded = ((n + 3) / 4) * 4;
+            L.tier_table[i] = wpos;
+            for (int k = 0; k < padded; ++k) t.push_back(k < n ? palette[base + k] : 0);
+            base += n;
+            wpos += padded / 4;
+        }
+        L.npal_words = wpos;
+        if (wpos > 24) { msg = "radix palette tables too large for the device kernels"; return 1; }
+        std::memcpy(L.pal_words, t.data(), t.size());
+    }
+    const int64_t NB = L.NB, rows = L.rows;
+    const int64_t first_blk = row0 * NB, nblk = rows * NB;
+    L.payload_words = (int64_t)offsets[first_blk + nblk] - (int64_t)offsets[first_blk];
+    L.read_bytes = L.payload_words * 4 + (nblk + 1) * 4 + (int64_t)L.npal_words * 4 + (nw > 2 ? nblk * 2 : 0);
+
+    // pass 1: per block, escapes (fast path) and the schedule
+    std::vector<uint16_t> nesc(nblk, 0), sched(nblk, 0);
+    const bool fast = L.fast_sip;
+    parallel_for(nblk, [&](int64_t i) {
+        int64_t gb = first_blk + i;
+        const uint32_t *blk = data + offsets[gb];
+        int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+        int64_t n = std::min<int64_t>(B, C - (i % NB) * B);
+        sched[i] = block_schedule(blk, (int64_t)nwords - (int64_t)offsets[gb], n, widths, nw);
+        if (fast) {
+            int e = sip_escapes(blk + 256, nullptr);
+            // a block short of its terminal stream (validate cannot see it)
+            // keeps every escape index inside its own words
+            int avail = (int)std::max<int64_t>(0, (words - 352) * 4);
+            nesc[i] = (uint16_t)std::min(e, avail);
+        }
+    });
+    // unit sizes
+    std::vector<int64_t> usize(L.units + 1, 0);
+    const bool ragged = rows % kUnitRows != 0;
+    for (int64_t u = 0; u < L.units; ++u) {
+        int64_t tile = u / NB, b = u % NB, sz = kUnitHeader;
+        bool absent = false;
+        for (int s = 0; s < kUnitRows; ++s) {
+            int64_t r = tile * kUnitRows + s;
+            if (r >= rows) { absent = true; continue; }
+            int64_t i = r * NB + b, gb = first_blk + i;
+            int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+            sz += a16(words * 4);
+            if (fast) sz += a16((int64_t)nesc[i] * 2);
+        }
+        if (fast && absent && ragged) sz += 1408;
+        usize[u] = sz;
+        L.max_unit_bytes = (int32_t)std::max<int64_t>(L.max_unit_bytes, sz);
+    }
+    std::vector<int64_t> ustart(L.units + 1, 0);
+    for (int64_t u = 0; u < L.units; ++u) ustart[u + 1] = ustart[u] + usize[u];
+    const int64_t pad = a16(block_words_most(B, widths, nw) * 4 + 64);
+    const int64_t total = ustart[L.units] + pad;
+    if (ustart[L.units] / 16 > (int64_t)UINT32_MAX) { msg = "radix tensor too large for the unit directory"; return 1; }
+    bytes.assign((size_t)total, '\0');
+    unit16.assign((size_t)(L.units + 1) * 4, '\0');
+    uint32_t *u16p = reinterpret_cast<uint32_t *>(&unit16[0]);
+    for (int64_t u = 0; u <= L.units; ++u) u16p[u] = (uint32_t)(ustart[u] / 16);
+    char *out = &bytes[0];
+    parallel_for(L.units, [&](int64_t u) {
+        int64_t tile = u / NB, b = u % NB;
+        char *base = out + ustart[u];
+        RowEntry *hdr = reinterpret_cast<RowEntry *>(base);
+        int64_t at = kUnitHeader;
+        int64_t null_at = -1;
+        for (int s = 0; s < kUnitRows; ++s) {
+            int64_t r = tile * kUnitRows + s;
+            if (r >= rows) continue;
+            int64_t i = r * NB + b, gb = first_blk + i;
+            int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+            hdr[s].off16 = (uint16_t)(at / 16);
+            hdr[s].words = (uint16_t)words;
+            hdr[s].sched = sched[i];
+            hdr[s].nesc = nesc[i];
+            std::memcpy(base + at, data + offsets[gb], (size_t)words * 4);
+            at += a16(words * 4);
+            if (fast) {
+                std::vector<uint16_t> pos(1024);
+                int e = sip_escapes(data + offsets[gb] + 256, pos.data());
+                int keep = std::min<int>(e, nesc[i]);
+                std::memcpy(base + at, pos.data(), (size_t)keep * 2);
+                at += a16((int64_t)nesc[i] * 2);
+            }
+        }
+        if (fast && ragged) {
+            for (int s = 0; s < kUnitRows; ++s) {
+                int64_t r = tile * kUnitRows + s;
+                if (r < rows) continue;
+                if (null_at < 0) {
+                    null_at = at;
+                    std::memset(base + at, 0, 1024);          // literals 0
+                    std::memset(base + at + 1024, 0xFF, 384);  // every tier-0 code is 7: every weight escapes
+                    at += 1408;
+                }
+                hdr[s].off16 = (uint16_t)(null_at / 16);
+                hdr[s].words = 0;
+                hdr[s].nesc = 0;
+                hdr[s].sched = 0;
+            }
+        }
+    });
+    return 0;
+}
+
+}  // namespace dm

@@ -1,0 +1,293 @@
+"""The operator boundary: packed Linears served by the sm_100a kernels — the
+drop-in for the reference's ``drinkme.codec.swap`` module classes and loader
+(src/drinkme/codec/swap.py):
+
+  to_device_radix(pack, device)   swap.py:80-161   the loader (here: the C
+                                                   library's unit-major B200
+                                                   layout, optionally one row
+                                                   shard of the tensor)
+  to_device_raw(pack, device)     swap.py:64-77
+  CompressedLinear                swap.py:228-392  routing by M, epilogue
+  RadixCompressedLinear           swap.py:395-456
+  RawLinear                       swap.py:459-497
+  NarrowLinear                    swap.py:530-626
+  make_module(pack, bias, device) swap.py:900-919
+  eligible                        swap.py:850-854
+
+Routing (swap.py:302-335): M == 1 -> "gemv"; 2 <= M <= MC_MAX -> "mc"
+unless DRINKME_PREFILL_DENSE_MIN says dense; M >= GEMM_MIN_ROWS (9) ->
+"dense" (decode the weight once, then one GEMM); "loop" when the dense arm
+is switched off. The epilogue rounds once: fp32 accumulate, plus the bias
+in fp32, one cast (swap.py:284-300). There is no CPU route: a CPU input
+raises (the reference's CPU route is the oracle here, oracle/oracle.py).
+"""
+from __future__ import annotations
+
+import os
+import warnings
+
+import numpy as np
+import torch
+
+from . import codec, radix_ops
+from .ops import MC_MAX
+from .radix_schedule import select as select_launch
+from .tensor import RadixTensor
+
+
+def _cuda_device(device) -> torch.device:
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError(f"drinkme_b200 serves CUDA devices only, not {dev} (no CPU route)")
+    return dev
+
+
+def to_device_raw(pack: dict, device="cuda") -> dict:
+    dev = _cuda_device(device)
+    R, C = int(pack["R"]), int(pack["C"])
+    bits = np.ascontiguousarray(pack["raw_bits"], dtype=np.uint16).reshape(R, C)
+    w = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+    return {"weight": w, "R": R, "C": C, "codec": "raw", "format_version": codec.FORMAT_VERSION, "layout": 0}
+
+
+def to_device_radix(pack: dict, device="cuda", row_begin: int = 0, row_end: int | None = None) -> dict:
+    """A radix tensor dict -> its runtime dict on a CUDA device, rows
+    [row_begin, row_end) of it (the whole tensor by default). The payload is
+    validated and laid out by the C library; the gulp schedule is computed
+    on the device over the pack's original layout (radix_ops.prepare_schedule)."""
+    dev = _cuda_device(device)
+    R, C = int(pack["R"]), int(pack["C"])
+    widths = tuple(int(w) for w in pack["widths"])
+    B = int(pack["block_size"])
+    r0, r1 = int(row_begin), R if row_end is None else int(row_end)
+    h = RadixTensor(pack, dev, r0, r1)
+    nb = (C + B - 1) // B
+    rows = r1 - r0
+    if len(widths) > 2:
+        off = np.ascontiguousarray(pack["rx_offsets"], dtype=np.uint32)[r0 * nb:r1 * nb + 1].astype(np.int64)
+        data = np.ascontiguousarray(pack["rx_data"], dtype=np.uint32)[int(off[0]):int(off[-1])]
+        d_data = torch.from_numpy(data.view(np.int32).copy()).to(dev)
+        d_off = torch.from_numpy((off - off[0]).astype(np.int32)).to(dev)
+        schedule = radix_ops.prepare_schedule(d_data, d_off, C, widths, B, rows * nb)
+        del d_data, d_off
+    else:
+        schedule = torch.empty(0, dtype=torch.uint16, device=dev)
+    pad = int(codec.block_word_bounds(B, codec.MANT, codec.EXP, widths)[1])
+    return {
+        **{k: v for k, v in pack.items() if k not in ("rx_palette", "rx_offsets", "rx_data")},
+        "rx_handle": h,
+        "rx_schedule": schedule,
+        "rx_palette_np": np.ascontiguousarray(pack["rx_palette"], dtype=np.uint8),
+        "rx_launch": select_launch(R, C, B, widths).as_dict(),
+        "NW": int(h.info.payload_words), "rx_pad_words": pad,
+        "R": rows, "C": C, "R_full": R, "row_begin": r0, "widths": widths, "block_size": B, "NBK": rows * nb,
+        "codec": "radix", "format_version": codec.FORMAT_VERSION, "layout": 0,
+    }
+
+
+def resident_bytes(runtime: dict) -> int:
+    """Device bytes a runtime dict holds (pack.resident_bytes, pack.py:1170)."""
+    n = sum(v.numel() * v.element_size() for v in runtime.values() if torch.is_tensor(v))
+    h = runtime.get("rx_handle")
+    return n + (int(h.info.resident_bytes) if h is not None else 0)
+
+
+_DENSE_MIN: int | None = None
+
+
+def _dense_min() -> int:
+    """DRINKME_PREFILL_DENSE_MIN if set, else GEMM_MIN_ROWS; <= 0 disables the
+    dense arm. Read once (swap.py:205-225)."""
+    global _DENSE_MIN
+    if _DENSE_MIN is None:
+        raw = os.environ.get("DRINKME_PREFILL_DENSE_MIN", "").strip()
+        try:
+            _DENSE_MIN = int(raw) if raw else CompressedLinear.GEMM_MIN_ROWS
+        except ValueError:
+            warnings.warn(f"DRINKME_PREFILL_DENSE_MIN={raw!r} is not an integer; using the measured default "
+                          f"{CompressedLinear.GEMM_MIN_ROWS}")
+            _DENSE_MIN = CompressedLinear.GEMM_MIN_ROWS
+    return _DENSE_MIN
+
+
+class CompressedLinear(torch.nn.Module):
+    """Routing by M and the round-once epilogue, shared by the radix and raw
+    modules."""
+
+    GEMM_MIN_ROWS = MC_MAX + 1
+
+    def __init__(self, runtime: dict, bias):
+        super().__init__()
+        self.p = runtime
+        self.bias = bias
+        self.R, self.C = int(runtime["R"]), int(runtime["C"])
+        self.tensor_codec = runtime.get("codec")
+        self.layout = int(runtime.get("layout", 0))
+
+    def _gemv_row(self, xi):
+        raise NotImplementedError
+
+    def _gemv_cols(self, xm):
+        raise NotImplementedError
+
+    def _dense_weight(self):
+        raise NotImplementedError
+
+    def _epilogue(self, y, x, shape):
+        if self.bias is not None:
+            y = y + self.bias
+        return y.to(x.dtype).reshape(*shape[:-1], self.R)
+
+    def _route(self, x) -> str:
+        if x.device.type != "cuda":
+            raise ValueError(f"drinkme_b200 serves CUDA tensors only; got an input on {x.device} "
+                             "(the CPU reference route is not part of this package)")
+        return self._route_rows(x.numel() // x.shape[-1])
+
+    def _route_rows(self, m: int) -> str:
+        if m == 1:
+            return "gemv"
+        dense_min = _dense_min()
+        if 0 < dense_min <= m:
+            return "dense"
+        if m <= MC_MAX:
+            return "mc"
+        return "loop"
+
+    def forward(self, x):
+        return self._forward(x, self._route(x))
+
+    def _forward(self, x, route: str):
+        shape = x.shape
+        xf = x.reshape(-1, self.C)
+        if route == "gemv":
+            return self._epilogue(self._gemv_row(xf[0].float().contiguous()), x, shape)
+        if route == "dense":
+            W = self._dense_weight()
+            out = torch.nn.functional.linear(xf, W, self.bias).reshape(*shape[:-1], self.R)
+            del W
+            return out
+        if route == "mc":
+            return self._epilogue(self._gemv_cols(xf.float().contiguous()), x, shape)
+        outs = torch.empty(xf.shape[0], self.R, device=x.device, dtype=torch.float32)
+        for i in range(xf.shape[0]):
+            outs[i] = self._gemv_row(xf[i].float().contiguous())
+        return self._epilogue(outs, x, shape)
+
+
+class RadixCompressedLinear(CompressedLinear):
+    """A radix-coded Linear served by the fused decode + GEMV kernels: the
+    gemv and mc routes read x in its own dtype (bf16 or fp32) and fuse the
+    bias and the one rounding in the kernel."""
+
+    def __init__(self, runtime: dict, bias):
+        if runtime.get("codec") != "radix" or "rx_handle" not in runtime:
+            raise ValueError("RadixCompressedLinear needs a to_device_radix runtime dict")
+        super().__init__(runtime, bias)
+        self.tensor_codec = "radix"
+
+    def _gemv_row(self, xi):
+        return radix_ops.gemv(self.p, xi)
+
+    def _gemv_cols(self, xm):
+        return radix_ops.gemv_mc(self.p, xm)
+
+    def _dense_weight(self):
+        return radix_ops.decode_weight(self.p)
+
+    def _forward(self, x, route: str):
+        if route in ("gemv", "mc") and x.dtype in (torch.bfloat16, torch.float32):
+            shape = x.shape
+            xf = x.reshape(-1, self.C)
+            if route == "gemv":
+                out = radix_ops.gemv_fused(self.p, xf[0], self.bias, x.dtype)
+            else:
+                out = radix_ops.gemv_mc_fused(self.p, xf, self.bias, x.dtype)
+            return out.reshape(*shape[:-1], self.R)
+        return super()._forward(x, route)
+
+
+class RawLinear(CompressedLinear):
+    """The raw fallback (bf16 bits verbatim): the raw GEMV for 1..MC_MAX rows,
+    cuBLAS (F.linear) above."""
+
+    def __init__(self, runtime: dict, bias):
+        if runtime.get("codec") != "raw":
+            raise ValueError("RawLinear needs a to_device_raw runtime dict")
+        super().__init__(runtime, bias)
+        self.tensor_codec = "raw"
+
+    def _dense_weight(self):
+        return self.p["weight"]
+
+    def forward(self, x):
+        self._route(x)
+        return stock_linear(x, self.p["weight"], self.bias)
+
+
+def stock_linear(x, weight, bias):
+    """A raw bf16 Linear's forward: up to MC_MAX rows through the raw GEMV
+    (fp32 accumulate, bias in fp32, one rounding), else F.linear."""
+    M = x.numel() // x.shape[-1]
+    if (x.device.type == "cuda" and 1 <= M <= MC_MAX and weight.dtype == torch.bfloat16
+            and x.dtype in (torch.bfloat16, torch.float32)):
+        y = radix_ops.gemv_raw(weight, x.reshape(M, -1), bias, x.dtype)
+        return y.reshape(*x.shape[:-1], weight.shape[0])
+    return torch.nn.functional.linear(x, weight, bias)
+
+
+class NarrowLinear(torch.nn.Linear):
+    """A raw bf16 Linear below the codec's row threshold served by the raw
+    GEMV for M <= MC_MAX (swap.py:530-626)."""
+
+    MAX_ROWS = 1024
+    MIN_COLS = 1024
+    BLOCK = 512
+    NUM_WARPS = 4
+
+    @classmethod
+    def wants(cls, mod) -> bool:
+        if type(mod) is not torch.nn.Linear or eligible(mod):
+            return False
+        w = mod.weight
+        return (w.dtype == torch.bfloat16 and w.device.type == "cuda" and w.shape[0] <= cls.MAX_ROWS
+                and w.shape[1] >= cls.MIN_COLS and w.shape[1] % 4 == 0)
+
+    @classmethod
+    def adopt(cls, lin: torch.nn.Linear) -> "NarrowLinear":
+        new = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, device="meta")
+        new.weight = lin.weight
+        new.bias = lin.bias
+        return new
+
+    def forward(self, x):
+        shape = x.shape
+        xm = x.reshape(-1, self.in_features)
+        M = xm.shape[0]
+        if M > MC_MAX or x.device.type != "cuda":
+            return torch.nn.functional.linear(x, self.weight, self.bias)
+        y = radix_ops.gemv_narrow(self.weight, xm, self.bias, self.BLOCK, self.NUM_WARPS)
+        return y.reshape(*shape[:-1], self.out_features)
+
+
+def eligible(child) -> bool:
+    if not isinstance(child, torch.nn.Linear):
+        return False
+    w = child.weight.data
+    return w.dtype == torch.bfloat16 and w.shape[1] % 4 == 0 and min(w.shape) >= 1024
+
+
+def make_module(pack: dict, bias, device="cuda", row_begin: int = 0, row_end: int | None = None):
+    """The loader's one constructor: a pack dict -> the resident module for
+    it, by the tensor's own kind (swap.py:900-919). With a row range, the
+    module holds that shard of the rows (and of the bias)."""
+    if pack.get("codec") == "radix":
+        rt = to_device_radix(pack, device, row_begin, row_end)
+        if bias is not None and row_end is not None:
+            bias = bias[row_begin:row_end]
+        return RadixCompressedLinear(rt, bias)
+    if pack.get("codec") == "raw":
+        rt = to_device_raw(pack, device)
+        return RawLinear(rt, bias)
+    raise ValueError(f"pack tensor declares codec {pack.get('codec')!r}: not a radix or raw tensor this build serves "
+                     "— refusing to build a module for it")

@@ -1,0 +1,141 @@
+/*
+ * drinkme_b200 — the C ABI of the B200-native radix decode + linear hot path.
+ *
+ * Every entry point returns 0 on success and a nonzero status on failure,
+ * writing a NUL-terminated message into (err, err_len) when err_len > 0 —
+ * the convention of the reference's one native entry point
+ * (src/drinkme/codec/radix_native.cpp:211-236, `radix_native(op, ...,
+ * char* error, uint64_t error_size)`). No entry point takes a torch type:
+ * pointers, sizes and a `void* stream` (a cudaStream_t; NULL = the legacy
+ * default stream).
+ *
+ * Pointer residency: arrays named `host_*` are host memory; every other
+ * array argument is device memory on the tensor's device. Calls that take a
+ * stream enqueue work on it and return without synchronising (CUDA-graph
+ * capturable), except where noted.
+ *
+ * Status codes: DM_OK 0, DM_EINVAL 1 (bad argument / malformed pack),
+ * DM_ECUDA 2 (a CUDA API error), DM_EDEVICE 3 (a kernel reported a device
+ * error, e.g. a bounded wait that gave up), DM_ENOMEM 4.
+ */
+#ifndef DRINKME_B200_H
+#define DRINKME_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DM_OK 0
+#define DM_EINVAL 1
+#define DM_ECUDA 2
+#define DM_EDEVICE 3
+#define DM_ENOMEM 4
+
+/* element types of activations and outputs */
+#define DM_BF16 0
+#define DM_F32 1
+
+/* The widest activation batch one GEMV call serves: the reference's
+ * MC_MAX (src/drinkme/codec/ops.py:19), the structural cap of the
+ * multi-column kernel (radix_ops.py:379-398 refuses M outside 1..8). */
+#define DM_MC_MAX 8
+
+typedef struct dm_tensor dm_tensor; /* opaque device-resident radix tensor */
+
+typedef struct dm_tensor_info {
+    int64_t R, C;              /* the full tensor's shape */
+    int64_t row_begin, rows;   /* the shard this handle holds: rows [row_begin, row_begin + rows) */
+    int32_t block_size, nwidths;
+    int32_t widths[8];
+    int64_t nblocks;           /* rows * ceil(C / block_size) */
+    int64_t payload_words;     /* NW: the pack payload words of this shard */
+    int64_t read_bytes;        /* radix_ops.read_bytes of this shard: NW*4 + directory + tables + schedule */
+    int64_t resident_bytes;    /* device bytes the handle holds (layout + scratch) */
+    int32_t fast_path;         /* 1 when the sm_100a sip kernel serves this tensor's GEMV */
+    int32_t device;
+} dm_tensor_info;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int dm_version(void);
+
+/* Load one pack-format-1 radix tensor onto `device`, rows [row_begin,
+ * row_end) of it (the whole tensor: 0, R). Replaces
+ * swap.to_device_radix (src/drinkme/codec/swap.py:80-161) for the device
+ * side: it validates the descriptors as radix.validate does
+ * (src/drinkme/codec/radix.py:174-238; same messages), then lays the
+ * shard's blocks out for the B200 kernels (unit-major, 16-byte aligned,
+ * per-unit headers, the gulp schedule and, for the sip fast path, an
+ * escape index) and copies it to the device. Host pointers: the pack's
+ * rx_palette (unpadded, `npalette` entries), rx_offsets (R*NB+1 entries),
+ * rx_data (`nwords`). Synchronous. */
+int dm_tensor_create(const uint8_t *host_palette, size_t npalette, const uint32_t *host_offsets,
+                     size_t noffsets, const uint32_t *host_data, size_t nwords, int64_t R, int64_t C,
+                     const int32_t *host_widths, int32_t nwidths, int32_t block_size, int64_t row_begin,
+                     int64_t row_end, int32_t device, dm_tensor **out, char *err, size_t err_len);
+
+int dm_tensor_destroy(dm_tensor *t);
+
+/* A second handle holding a device-side copy of `src` (same device, its own
+ * buffers and scratch): loads one packed tensor into several places in HBM
+ * without repeating the host layout. No reference counterpart (the
+ * reference builds every resident tensor from its pack: swap.py:80-161). */
+int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err, size_t err_len);
+
+int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info);
+
+/* y[M, rows] = x[M, C] @ W[rows, C]^T (+ bias), fp32 accumulate, the bias
+ * added in fp32 and ONE rounding to `out_dtype`. Replaces
+ * radix_ops.gemv_fused / gemv / gemv_mc (src/drinkme/codec/radix_ops.py:
+ * 351-398): x is bf16 or fp32 (`x_dtype`, row stride C), 1 <= M <= 8
+ * (DM_EINVAL outside, the ValueError of radix_ops.py:384-385), bias is a
+ * bf16 [rows] vector or NULL, out is [M, rows] row-major in `out_dtype`.
+ * Column m of an M-row call is bitwise the M=1 call on row m. Uses the
+ * tensor's own scratch: calls on one tensor must not overlap on the GPU. */
+int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
+            int32_t out_dtype, void *stream, char *err, size_t err_len);
+
+/* The shard's decoded bf16 bit patterns, uint16 [rows, C] — replaces
+ * radix_ops.decode_bits (src/drinkme/codec/radix_ops.py:418-427). */
+int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *err, size_t err_len);
+
+/* The gulp schedule over the ORIGINAL pack layout on the device: one
+ * uint16 per block whose byte (k-1) is the word length of nonterminal tier
+ * k's stream — replaces radix_ops.prepare_schedule
+ * (src/drinkme/codec/radix_ops.py:341-348). Words at or past `nwords` read
+ * as zero. */
+int dm_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *offsets, int64_t C,
+                        const int32_t *host_widths, int32_t nwidths, int32_t block_size, int64_t nblocks,
+                        uint16_t *out, void *stream, char *err, size_t err_len);
+
+/* y[M, R] = x[M, C] @ w[R, C]^T (+ bias) over a raw row-major bf16 weight
+ * — replaces radix_ops.gemv_narrow (src/drinkme/codec/radix_ops.py:
+ * 401-415) and serves the raw lm_head (swap.stock_linear, swap.py:
+ * 681-707). 1 <= M <= 8; fp32 accumulate, bias in fp32, one rounding. */
+int dm_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int32_t x_dtype, int64_t M,
+                const void *bias, void *out, int32_t out_dtype, void *stream, char *err, size_t err_len);
+
+/* The pack encoder (src/drinkme/codec/radix_native.cpp:57-166 `plan` +
+ * `encode`; radix.py:77-136 for any block size): uint16 [R, C] bf16 bits
+ * -> the pack arrays, byte-identical to the reference's. Two calls:
+ * dm_pack_plan fills host_palette (covered entries) and host_offsets
+ * (R*NB+1) and returns the payload word count in *nwords; dm_pack_encode
+ * then writes host_data[nwords]. `threads` <= 0 uses every host core. */
+int dm_pack_plan(const uint16_t *host_bits, int64_t R, int64_t C, const int32_t *host_widths, int32_t nwidths,
+                 int32_t block_size, int32_t threads, uint8_t *host_palette, uint32_t *host_offsets,
+                 uint64_t *nwords, char *err, size_t err_len);
+int dm_pack_encode(const uint16_t *host_bits, int64_t R, int64_t C, const int32_t *host_widths,
+                   int32_t nwidths, int32_t block_size, int32_t threads, const uint8_t *host_palette,
+                   const uint32_t *host_offsets, uint32_t *host_data, uint64_t nwords, char *err, size_t err_len);
+
+/* Reads and clears the tensor's device error word (a kernel's bounded
+ * wait that gave up writes it). Synchronises the tensor's device. */
+int dm_tensor_check(const dm_tensor *t, int32_t *device_error, char *err, size_t err_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRINKME_B200_H */

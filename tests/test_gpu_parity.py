@@ -1,0 +1,315 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI, against the CPU
+oracle (oracle/oracle.py) and against the reference's own outputs (the
+golden vectors: its encoder's packs, its decoders' bits, its Triton kernels'
+fp32 GEMVs).
+
+Gates, as the reference states them:
+  * decoded weights bit-exact (bench/radix_gemv_bitpin.py "bits");
+  * GEMV within |y - y64| <= 2e-6 * |x|.|W| + 1e-7 of float64
+    (bench/radix_gemv_bitpin.py:182, radix_mc_bitpin.py:104);
+  * linear outputs within 1e-3 max relative error, max|y - y_ref| /
+    max|y_ref|, of the reference's own kernels on the same inputs;
+  * fused bias: the bf16 output == (fp32 + bias).to(bf16) exactly;
+  * row m of an M-row call bitwise the M=1 call; bf16 x == its fp32
+    widening (tests/test_narrow_linear.py:101-123).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import all_patterns, pack_of, radix_names
+from drinkme_b200 import codec, radix_ops, swap
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _bits_t(U):
+    return torch.from_numpy(np.ascontiguousarray(U).view(np.int16)).view(torch.bfloat16)
+
+
+def _x_of(z, name, M=1):
+    xb = z[f"{name}/x_bf16"][:M]
+    return torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).to(DEV)
+
+
+def _f32(x):
+    return x.float().cpu().numpy()
+
+
+def _within_bound(y, x, bits):
+    y64, bound = oracle.gemv_bound(_f32(x), bits)
+    err = np.abs(y.astype(np.float64) - y64)
+    return bool(np.all(err <= bound)), float((err / bound).max())
+
+
+@pytest.fixture(scope="module")
+def runtimes(golden):
+    z, pins = golden
+    out = {}
+    for name in radix_names(pins):
+        out[name] = swap.to_device_radix(pack_of(z, pins, name), DEV)
+    return out
+
+
+def test_decode_every_golden_pack_bit_exact(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        got = radix_ops.decode_bits(rt).cpu().numpy()
+        assert np.array_equal(got.view(np.uint16), z[f"{name}/bits"]), name
+
+
+@pytest.mark.parametrize("profile", ["sip", "balanced", "gulp"])
+@pytest.mark.parametrize("block", [32, 1024])
+def test_all_65536_patterns_decode_exactly(profile, block):
+    ex = all_patterns()
+    pal, off, data = codec.encode_arrays(ex, codec.PROFILES[profile], block)
+    p = {"rx_palette": pal, "rx_offsets": off, "rx_data": data, "R": 512, "C": 513,
+         "widths": list(codec.PROFILES[profile]), "block_size": block, "codec": "radix", "profile": profile}
+    rt = swap.to_device_radix(p, DEV)
+    got = radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16)
+    assert np.array_equal(got, ex)
+    again = radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16)
+    assert np.array_equal(again, ex)
+
+
+def test_gulp_schedule_matches_the_reference(golden, runtimes):
+    z, pins = golden
+    n = 0
+    for name, rt in runtimes.items():
+        key = f"{name}/schedule"
+        if key in z.files:
+            got = rt["rx_schedule"].cpu().numpy().view(np.uint16)
+            assert np.array_equal(got, z[key]), name
+            n += 1
+    assert n >= 10
+
+
+def test_gemv_m1_bf16_within_float64_bound_and_reference(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        bits = z[f"{name}/bits"]
+        x = _x_of(z, name)
+        y = radix_ops.gemv(rt, x[0]).cpu().numpy()
+        ok, worst = _within_bound(y[None, :], x, bits)
+        assert ok, (name, worst, radix_ops.decoder_of(rt))
+        ref = z[f"{name}/gemv_bf16x"]
+        rel = np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30)
+        assert rel <= 1e-3, (name, rel)
+
+
+def test_fast_path_serves_the_sip_whole_block_tensors(runtimes):
+    kinds = {name: radix_ops.decoder_of(rt) for name, rt in runtimes.items()}
+    assert kinds["sip_normal_16x4096"] == radix_ops.DECODER_SIP_MMA
+    assert kinds["sip_tail_16x4096"] == radix_ops.DECODER_SIP_MMA
+    assert kinds["sip_normal_4x12288"] == radix_ops.DECODER_SIP_MMA
+    assert kinds["gulp_normal_16x4096"] == radix_ops.DECODER_GENERIC
+    assert kinds["sip_tail_3x1025"] == radix_ops.DECODER_GENERIC
+
+
+def test_gemv_fp32_x_within_bound(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        x32 = torch.from_numpy(z[f"{name}/x_f32"]).to(DEV)
+        y = radix_ops.gemv(rt, x32[0]).cpu().numpy()
+        ok, worst = _within_bound(y[None, :], x32, z[f"{name}/bits"])
+        assert ok, (name, worst)
+        ref = z[f"{name}/gemv_f32x"]
+        assert np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30) <= 1e-3, name
+
+
+def test_fused_bias_rounds_once(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        x = _x_of(z, name)
+        bias = torch.from_numpy(z[f"{name}/bias_bf16"].view(np.int16).copy()).view(torch.bfloat16).to(DEV)
+        y32 = radix_ops.gemv(rt, x[0])
+        fused = radix_ops.gemv_fused(rt, x[0], bias, torch.bfloat16)
+        assert torch.equal(fused[0], (y32 + bias.float()).to(torch.bfloat16)), name
+
+
+def test_mc_rows_bitwise_the_m1_call_and_within_bound(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        x = _x_of(z, name, 8)
+        ones = [radix_ops.gemv(rt, x[j]) for j in range(8)]
+        for M in range(1, 9):
+            ym = radix_ops.gemv_mc(rt, x[:M])
+            for j in range(M):
+                assert torch.equal(ym[j], ones[j]), (name, M, j)
+        y8 = radix_ops.gemv_mc(rt, x).cpu().numpy()
+        ok, worst = _within_bound(y8, x, z[f"{name}/bits"])
+        assert ok, (name, worst)
+        ref = z[f"{name}/mc8_bf16x"]
+        assert np.abs(y8 - ref).max() / max(np.abs(ref).max(), 1e-30) <= 1e-3, name
+
+
+def test_bf16_x_equals_its_fp32_widening(golden, runtimes):
+    z, pins = golden
+    for name, rt in runtimes.items():
+        x = _x_of(z, name, 3)
+        assert torch.equal(radix_ops.gemv_mc(rt, x), radix_ops.gemv_mc(rt, x.float())), name
+
+
+def test_mc_refuses_m_outside_one_to_eight(runtimes):
+    rt = runtimes["sip_normal_16x4096"]
+    for M in (0, 9):
+        with pytest.raises(ValueError, match="outside 1"):
+            radix_ops.gemv_mc(rt, torch.zeros(M, 4096, dtype=torch.bfloat16, device=DEV))
+
+
+def test_the_bias_cancellation_keeps_its_residual():
+    """tests/test_codec_bias_rounding.py: W columns 0, 1 = 1, x = (1, 1/256),
+    bias -1: one rounding keeps 2^-8 on every arm and every profile."""
+    R = C = 1024
+    w = torch.zeros(R, C, dtype=torch.bfloat16)
+    w[:, :2] = 1
+    b = torch.full((R,), -1.0, device=DEV, dtype=torch.bfloat16)
+    for prof in ("sip", "gulp"):
+        pk = codec.pack_weight_radix(w, prof)
+        assert pk["codec"] == "radix"
+        mod = swap.make_module(pk, b, DEV)
+        for n in (1, 3, 8, 9):
+            x = torch.zeros(n, C, device=DEV, dtype=torch.bfloat16)
+            x[:, 0] = 1
+            x[:, 1] = 1 / 256
+            y = mod(x)
+            assert torch.all(y == 0.00390625), (prof, n)
+
+
+def test_module_routes_match_the_arms(golden):
+    z, pins = golden
+    name = "sip_normal_16x4096"
+    p = pack_of(z, pins, name)
+    bias = torch.linspace(-0.1, 0.1, 16, device=DEV).to(torch.bfloat16)
+    mod = swap.make_module(p, bias, DEV)
+    W = _bits_t(z[f"{name}/bits"]).to(DEV)
+    x = _x_of(z, name, 8)
+    assert mod._route(x[:1]) == "gemv"
+    assert torch.equal(mod(x[:1])[0], radix_ops.gemv_fused(mod.p, x[0], bias, torch.bfloat16)[0])
+    assert mod._route(x[:5]) == "mc"
+    y5 = mod(x[:5])
+    assert torch.equal(y5, (radix_ops.gemv_mc(mod.p, x[:5]) + bias.float()).to(torch.bfloat16))
+    xd = torch.randn(9, 4096, device=DEV).to(torch.bfloat16)
+    assert mod._route(xd) == "dense"
+    assert torch.equal(mod(xd), torch.nn.functional.linear(xd, W, bias))
+
+
+@pytest.mark.parametrize("R", [13, 40, 1])
+def test_ragged_tiles_on_the_fast_path(R):
+    g = torch.Generator().manual_seed(R)
+    W = (torch.randn(R, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, "sip")
+    rt = swap.to_device_radix(p, DEV)
+    assert radix_ops.decoder_of(rt) == radix_ops.DECODER_SIP_MMA
+    bits = codec.bits_of(W)
+    assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits)
+    x = torch.randn(8, 4096, generator=g).to(torch.bfloat16).to(DEV)
+    for M in (1, 8):
+        y = radix_ops.gemv_mc(rt, x[:M]).cpu().numpy()
+        ok, worst = _within_bound(y, x[:M], bits)
+        assert ok, (R, M, worst)
+
+
+def test_row_shards_are_the_rows_of_the_whole():
+    g = torch.Generator().manual_seed(5)
+    R, C = 100, 8192
+    W = (torch.randn(R, C, generator=g) * 0.02).to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, "sip")
+    bits = codec.bits_of(W)
+    x = torch.randn(2, C, generator=g).to(torch.bfloat16).to(DEV)
+    for r0, r1 in ((0, 37), (37, 64), (64, 100), (0, 100)):
+        rt = swap.to_device_radix(p, DEV, r0, r1)
+        assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits[r0:r1])
+        y = radix_ops.gemv_mc(rt, x).cpu().numpy()
+        ok, worst = _within_bound(y, x, bits[r0:r1])
+        assert ok, (r0, r1, worst)
+
+
+def test_config1_down_proj_full_size():
+    """BASELINE configs[0] shapes on the GPU: 4096 x 12288 sip, seed 0, x seed 1:
+    decode bit-exact, y within the float64 bound and 1e-3 of the reference's
+    CPU route (bf16 output of F.linear over the decoded weight)."""
+    import json
+    import os
+
+    from conftest import GOLDEN
+
+    g = torch.Generator().manual_seed(0)
+    W = (torch.randn(4096, 12288, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(1, 12288, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    p = codec.pack_weight_served(W)
+    rt = swap.to_device_radix(p, DEV)
+    bits = codec.bits_of(W)
+    assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits)
+    xd = x.to(DEV)
+    y = radix_ops.gemv(rt, xd[0]).cpu().numpy()
+    ok, worst = _within_bound(y[None, :], xd, bits)
+    assert ok, worst
+    z = np.load(os.path.join(GOLDEN, "packs.npz"))
+    ref = z["config1/cpu_route_bf16"][0]
+    yb = radix_ops.gemv_fused(rt, xd[0], None, torch.bfloat16).float().cpu().numpy()[0]
+    assert np.abs(yb - ref).max() / np.abs(ref).max() <= 1e-2  # both bf16-rounded
+    assert np.abs(y - ref).max() / np.abs(ref).max() <= 5e-3
+    with open(os.path.join(GOLDEN, "pins.json")) as f:
+        assert radix_ops.read_bytes(rt) == json.load(f)["config1"]["sip"]["read_bytes"]
+
+
+@pytest.mark.parametrize("shape", [(48, 5120), (32, 4096), (256, 6656)])
+def test_raw_narrow_gemv(shape):
+    R, C = shape
+    torch.manual_seed(2)
+    w = (torch.randn(R, C) * 0.05).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(R) * 0.5).to(torch.bfloat16).to(DEV)
+    x = (torch.randn(8, C, device=DEV) * 0.5).to(torch.bfloat16)
+    ones = [radix_ops.gemv_narrow(w, x[j:j + 1], bias) for j in range(8)]
+    for M in range(1, 9):
+        ym = radix_ops.gemv_narrow(w, x[:M], bias)
+        for j in range(M):
+            assert torch.equal(ym[j:j + 1], ones[j]), (shape, M, j)
+    y32 = radix_ops.gemv_raw(w, x, None, torch.float32).cpu().numpy()
+    bits = w.cpu().view(torch.int16).numpy().view(np.uint16)
+    y64, bound = oracle.gemv_bound(_f32(x), bits)
+    assert np.all(np.abs(y32 - y64) <= bound)
+    assert torch.equal(radix_ops.gemv_narrow(w, x[:3], None).float(),
+                       radix_ops.gemv_narrow(w, x[:3].float(), None).to(torch.bfloat16).float())
+
+
+def test_raw_gemv_adds_the_bias_before_the_one_rounding():
+    lin = torch.zeros(2, 1024, dtype=torch.bfloat16, device=DEV)
+    lin[0, 0] = 1.0
+    lin[0, 1] = 1.0
+    bias = torch.zeros(2, dtype=torch.bfloat16, device=DEV)
+    bias[0] = -1.0
+    x = torch.zeros(1, 1024, dtype=torch.bfloat16, device=DEV)
+    x[0, 0] = 1.0
+    x[0, 1] = 2.0 ** -9
+    assert radix_ops.gemv_narrow(lin, x, bias)[0, 0].item() == 2.0 ** -9
+
+
+def test_prepare_schedule_on_the_original_layout(golden):
+    z, pins = golden
+    name = "gulp_tail_16x4096"
+    p = pack_of(z, pins, name)
+    data = torch.from_numpy(p["rx_data"].view(np.int32).copy()).to(DEV)
+    off = torch.from_numpy(p["rx_offsets"].view(np.int32).copy()).to(DEV)
+    s = radix_ops.prepare_schedule(data, off, p["C"], p["widths"], 1024, 16 * 4)
+    assert np.array_equal(s.cpu().numpy().view(np.uint16), z[f"{name}/schedule"])
+
+
+def test_repeated_calls_are_bitwise_deterministic(runtimes, golden):
+    z, _ = golden
+    for name in ("sip_normal_16x4096", "sip_normal_4x12288", "gulp_normal_16x4096"):
+        rt = runtimes[name]
+        x = _x_of(z, name, 4)
+        a = radix_ops.gemv_mc(rt, x)
+        for _ in range(3):
+            assert torch.equal(radix_ops.gemv_mc(rt, x), a)
+
+
+def test_no_device_errors_recorded(runtimes):
+    for name, rt in runtimes.items():
+        assert rt["rx_handle"].device_error() == 0, name

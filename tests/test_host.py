@@ -1,0 +1,181 @@
+"""Host logic with no GPU: the C ABI library loads and exports every entry
+point the header declares; the loader's validation refuses malformed packs
+with the reference's messages before touching the device; the launch
+schedule, registry, pack reader and routing keep the reference's contract."""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, pack_of
+from drinkme_b200 import _lib, codec, radix_schedule, registry
+
+
+def test_library_exports_every_declared_entry_point():
+    with open(os.path.join(ROOT, "include", "drinkme_b200.h")) as f:
+        header = f.read()
+    declared = set(re.findall(r"^int (dm_\w+)\(", header, flags=re.M))
+    assert declared == set(_lib.EXPORTS)
+    L = ct.CDLL(_lib.LIB_PATH)
+    for name in declared:
+        assert hasattr(L, name), name
+    assert _lib.lib().dm_version() >= 100
+
+
+def _create(p, row_begin=0, row_end=None):
+    """dm_tensor_create up to its validation (no device is touched before it
+    passes)."""
+    pal = np.ascontiguousarray(p["rx_palette"], dtype=np.uint8)
+    off = np.ascontiguousarray(p["rx_offsets"], dtype=np.uint32)
+    data = np.ascontiguousarray(p["rx_data"], dtype=np.uint32)
+    w = (ct.c_int32 * len(p["widths"]))(*[int(x) for x in p["widths"]])
+    h = ct.c_void_p()
+    R = int(p["R"])
+    _lib.call("dm_tensor_create", pal.ctypes.data_as(ct.c_void_p), pal.size, off.ctypes.data_as(ct.c_void_p),
+              off.size, data.ctypes.data_as(ct.c_void_p), data.size, R, int(p["C"]), w, len(p["widths"]),
+              int(p["block_size"]), row_begin, R if row_end is None else row_end, 0, ct.byref(h))
+    return h
+
+
+def test_loader_refuses_malformed_descriptors(golden):
+    z, pins = golden
+    p = pack_of(z, pins, "sip_normal_16x4096")
+    with pytest.raises(ValueError, match="invalid radix block offsets"):
+        _create(dict(p, rx_offsets=p["rx_offsets"][:-1]))
+    off = p["rx_offsets"].copy()
+    off[1] = 1
+    with pytest.raises(ValueError, match="fewer than the 352 its literal plane"):
+        _create(dict(p, rx_offsets=off))
+    with pytest.raises(ValueError, match="invalid radix palette entries"):
+        _create(dict(p, rx_palette=np.zeros_like(p["rx_palette"])))
+    with pytest.raises(ValueError, match="invalid radix block size"):
+        _create(dict(p, block_size=1000))
+    with pytest.raises(ValueError, match="2..8 widths"):
+        _create(dict(p, widths=[3, 7]))
+
+
+def test_long_block_is_refused(golden):
+    z, pins = golden
+    p = pack_of(z, pins, "sip_normal_16x4096")
+    off = p["rx_offsets"].astype(np.int64)
+    data = np.insert(p["rx_data"], int(off[1]), np.zeros(400, np.uint32))
+    off[1:] += 400
+    with pytest.raises(ValueError, match="more than the 608 any block"):
+        _create(dict(p, rx_offsets=off.astype(np.uint32), rx_data=data))
+
+
+def test_codec_validate_tensor_messages(golden):
+    z, pins = golden
+    p = dict(pack_pack := pack_of(z, pins, "gulp_normal_16x4096"), format_version=1)
+    codec.validate_tensor("a", p)
+    with pytest.raises(ValueError, match=r"pack tensor a \(radix\): block_size"):
+        codec.validate_tensor("a", dict(p, block_size=32))
+    with pytest.raises(ValueError, match="at most four"):
+        codec.validate_tensor("a", dict(p, widths=[2, 2, 2, 2, 8]))
+    with pytest.raises(ValueError, match="1..4 bits"):
+        codec.validate_tensor("a", dict(p, widths=[5, 8]))
+    with pytest.raises(ValueError, match="profile"):
+        codec.validate_tensor("a", dict(p, profile="nope"))
+    with pytest.raises(ValueError, match="invalid radix palette entries"):
+        codec.validate_tensor("a", dict(p, rx_palette=np.zeros_like(pack_pack["rx_palette"])))
+    with pytest.raises(ValueError, match="codec"):
+        codec.validate_tensor("a", dict(p, codec="fp8"))
+
+
+def test_pack_dir_round_trip(tmp_path, golden):
+    z, pins = golden
+    tensors = {}
+    for name in ("sip_normal_16x4096", "gulp_tail_16x4096"):
+        p = pack_of(z, pins, name)
+        tensors[name] = {**p, "bpw": float(p["bpw"])}
+    tensors["raw"] = codec.raw_dict(np.zeros((4, 8), np.uint16))
+    codec.save_pack_dir(str(tmp_path / "pk"), tensors, {"hfRepo": "x/y"})
+    got = dict(codec.iter_pack_dir(str(tmp_path / "pk")))
+    assert set(got) == set(tensors)
+    for name in ("sip_normal_16x4096", "gulp_tail_16x4096"):
+        for k in ("rx_palette", "rx_offsets", "rx_data"):
+            assert np.array_equal(got[name][k], tensors[name][k])
+    assert np.array_equal(got["raw"]["raw_bits"], tensors["raw"]["raw_bits"])
+
+
+def test_pack_dir_refuses_other_versions_and_escaping_files(tmp_path, golden):
+    import json
+
+    z, pins = golden
+    d = tmp_path / "pk"
+    codec.save_pack_dir(str(d), {"a": pack_of(z, pins, "sip_normal_16x4096")}, {})
+    meta = json.loads((d / "meta.json").read_text())
+    (d / "meta.json").write_text(json.dumps(dict(meta, formatVersion=2)))
+    with pytest.raises(ValueError, match="pack format 2"):
+        list(codec.iter_pack_dir(str(d)))
+    (d / "meta.json").write_text(json.dumps(dict(meta, tensors={"a": "../x.npz"})))
+    with pytest.raises(ValueError, match="bare basename"):
+        list(codec.iter_pack_dir(str(d)))
+
+
+def test_schedule_shape_classes_and_overrides():
+    assert radix_schedule.shape_class(151936, 4096) == "head"
+    assert radix_schedule.shape_class(1024, 4096) == "narrow"
+    assert radix_schedule.shape_class(4096, 12288) == "long"
+    assert radix_schedule.shape_class(12288, 4096) == "wide"
+    assert radix_schedule.shape_class(4096, 4096) == "square"
+    assert radix_schedule.family((3, 8)) == "sip" and radix_schedule.family((2, 2, 4, 8)) == "scheduled"
+    L = radix_schedule.select(4096, 4096, 1024, (3, 8))
+    assert L.box_class == "b200" and L.kernel == "sip-mma-sm100a" and L.source == "table"
+    assert radix_schedule.select(4096, 4100, 1024, (3, 8)).kernel == "generic-sm100a"
+    assert radix_schedule.select(4096, 4096, 1024, (2, 2, 4, 8)).kernel == "generic-sm100a"
+    e = radix_schedule.select(4096, 4096, 1024, (3, 8), override="tiles=row,warps=4")
+    assert e.gemv_tiles == 0 and e.gemv_warps == 4 and e.source == "env"
+    assert radix_schedule.select(1, 1, override="spike").gemv_warps == 2
+    with pytest.raises(ValueError):
+        radix_schedule.select(1, 1, override="warps=3")
+    with pytest.raises(ValueError):
+        radix_schedule.select(1, 1, override="bogus=1")
+    per = radix_schedule.select(1024, 4096, override='{"narrow": {"gemv_warps": 2}}')
+    assert per.gemv_warps == 2
+
+
+def test_registry_rows():
+    assert registry.supported("radix", 0, registry.GEMV, registry.CUDA_SM100)
+    assert registry.supported("radix", 0, registry.MC, registry.CUDA_SM100)
+    assert not registry.supported("radix", 0, registry.GEMV, registry.CPU)
+    assert not registry.supported("fp8", 0, registry.GEMV, registry.CUDA_SM100)
+    assert registry.kernel_of("cpu") == registry.CPU
+    assert "unknown combination" in registry.unsupported_note("fp8", 0, registry.GEMV, registry.CUDA_SM100)
+
+
+def test_routing_thresholds(monkeypatch):
+    from drinkme_b200 import swap
+
+    class Fake(swap.CompressedLinear):
+        pass
+
+    m = Fake({"R": 8, "C": 8, "codec": "radix"}, None)
+    swap._DENSE_MIN = None
+    monkeypatch.delenv("DRINKME_PREFILL_DENSE_MIN", raising=False)
+    assert m._route_rows(1) == "gemv"
+    assert [m._route_rows(k) for k in range(2, 9)] == ["mc"] * 7
+    assert m._route_rows(9) == "dense"
+    swap._DENSE_MIN = None
+    monkeypatch.setenv("DRINKME_PREFILL_DENSE_MIN", "0")
+    assert m._route_rows(9) == "loop" and m._route_rows(5) == "mc"
+    swap._DENSE_MIN = None
+    monkeypatch.setenv("DRINKME_PREFILL_DENSE_MIN", "4")
+    assert m._route_rows(4) == "dense" and m._route_rows(3) == "mc"
+    swap._DENSE_MIN = None
+
+
+def test_cpu_inputs_are_refused_not_served():
+    import torch
+
+    from drinkme_b200 import swap
+
+    m = swap.CompressedLinear({"R": 8, "C": 8, "codec": "radix"}, None)
+    with pytest.raises(ValueError, match="CUDA"):
+        m(torch.zeros(1, 8))
+    with pytest.raises(ValueError, match="CUDA"):
+        swap.to_device_radix({"R": 1}, "cpu")
