@@ -105,7 +105,7 @@ extern "C" int dm_tensor_create(const uint8_t *palette, size_t npalette, const u
     if (t->L.fast_sip) {
         const int64_t workers = std::min<int64_t>((int64_t)t->sms * 8, t->L.units);
         t->S.max_workers = (int32_t)workers;
-        const size_t pbytes = (size_t)workers * 2 * 64 * sizeof(float);
+        const size_t pbytes = (size_t)workers * 2 * 128 * sizeof(float);
         const size_t cbytes = (size_t)t->L.tiles * sizeof(int);
         const size_t xbytes = (size_t)6 * (size_t)t->L.C * 2;
         if ((e = cudaMalloc(&t->S.partials, pbytes)) != cudaSuccess ||
@@ -144,7 +144,7 @@ extern "C" int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err,
     }
     t->resident_bytes = src->data_bytes + ubytes;
     if (src->L.fast_sip) {
-        const size_t pbytes = (size_t)t->S.max_workers * 2 * 64 * sizeof(float);
+        const size_t pbytes = (size_t)t->S.max_workers * 2 * 128 * sizeof(float);
         const size_t cbytes = (size_t)t->L.tiles * sizeof(int);
         const size_t xbytes = (size_t)6 * (size_t)t->L.C * 2;
         if ((e = cudaMalloc(&t->S.partials, pbytes)) != cudaSuccess ||

@@ -14,10 +14,13 @@ constexpr int kErrWaitFull = 1;    // a consumer gave up waiting for a staged un
 constexpr int kErrWaitEmpty = 2;   // the producer gave up waiting for a slot
 constexpr int kErrWaitDrain = 3;   // the producer gave up draining its copies at exit
 
-// Upper bound on polls of one mbarrier phase. A healthy wait is a few
-// microseconds; this is seconds, after which the kernel records an error and
-// returns instead of spinning forever.
-constexpr uint32_t kWaitPolls = 1u << 26;
+// Upper bound on polls of one mbarrier phase. Each poll suspends the warp in
+// hardware for up to kSuspendNs (it resumes as soon as the phase completes),
+// so a healthy wait costs one or two polls; 2^16 polls bound a wait at about
+// two seconds, after which the kernel records an error and returns instead of
+// waiting forever.
+constexpr uint32_t kWaitPolls = 1u << 16;
+constexpr uint32_t kSuspendNs = 32768;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -46,9 +49,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, "
+        "p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "n"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -56,10 +60,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Waits for the phase of `bar` with parity `parity` to complete; false
 // (after writing `code` to *err) when the bound runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
-    }
     if (err) atomicExch(err, code);
     return false;
 }

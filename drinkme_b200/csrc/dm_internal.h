@@ -10,11 +10,11 @@
 
 namespace dm {
 
-// Rows per unit: a unit is 8 consecutive rows x one block column, the work
-// item of the GEMV kernels and the granularity of the device layout. Eight
-// rows are the n = 8 side of one m16n8k16 MMA (the weights are its B
-// operand, the activations its A operand).
-constexpr int kUnitRows = 8;
+// Rows per unit: a unit is 16 consecutive rows x one block column, the work
+// item of the GEMV kernels and the granularity of the device layout. Sixteen
+// rows are the m = 16 side of one m16n8k16 MMA (the weights are its A
+// operand, the activations its n = 8 B operand).
+constexpr int kUnitRows = 16;
 // Bytes of a unit's header: per row slot {u16 off16, u16 nesc, u16 sched,
 // u16 words}.
 constexpr int kUnitHeader = kUnitRows * 8;
@@ -52,7 +52,7 @@ struct TensorLayout {
 };
 
 struct Scratch {
-    float *partials = nullptr;   // [max_workers][2][8 rows][8 virtual rows]
+    float *partials = nullptr;   // [max_workers][2][16 rows][8 virtual rows]
     int *counters = nullptr;     // [tiles] arrival counters, zero between calls
     uint16_t *xsplit = nullptr;  // [6][C] bf16 hi/mid/lo rows of an fp32 activation pair
     int *err = nullptr;          // device error word
@@ -97,6 +97,6 @@ int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t 
                             void *stream, std::string &msg);
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg);
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *consumers);
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spg, int *ng, int dir_cap);
 
 }  // namespace dm

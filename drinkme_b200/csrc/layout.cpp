@@ -4,15 +4,15 @@
 // What changes is only where the bytes sit on the device: the reference keeps
 // the payload verbatim plus a zero pad (swap.to_device_radix,
 // src/drinkme/codec/swap.py:80-161); this loader regroups the same block
-// words into UNITS of 8 rows x 1 block column, each unit contiguous and
+// words into UNITS of 16 rows x 1 block column, each unit contiguous and
 // 16-byte aligned so one bulk copy stages it into shared memory:
 //
-//   unit  = [8 x RowEntry header][row-block streams, each 16-byte aligned]
+//   unit  = [16 x RowEntry header][row-block streams, each 16-byte aligned]
 //           [sip fast path: per row, the escape index — the uint16 position
 //            of every tier-0 escape (code 7) in block order, 16-byte aligned]
 //           [sip fast path, ragged last tile only: one null block whose
 //            weights all decode to +0]
-//   units in tile-major order (tile = 8 rows; all block columns of a tile
+//   units in tile-major order (tile = 16 rows; all block columns of a tile
 //   before the next tile), then a zero tail pad as long as the widest block
 //   (radix.block_word_bounds(B)[1] words), so no reader leaves the buffer.
 #include <algorithm>

@@ -8,18 +8,20 @@
 // activation row's result independent of the others.
 //
 // Design (B200-first):
-//   * A CTA = 1 producer warp + NC consumer warps. Each consumer warp is a
-//     WORKER owning a contiguous range of units (8 rows x 1 block column,
-//     see layout.cpp); the units of all workers of the grid cover the tensor
-//     in tile-major order, split evenly (stream-K).
+//   * A CTA = 1 producer warp + up to 4 groups of 4 consumer warps. Each
+//     group is a WORKER owning a contiguous range of units (16 rows x 1 block
+//     column, see layout.cpp); the units of all workers of the grid cover the
+//     tensor in tile-major order, split evenly (stream-K). The 4 warps of a
+//     group share each staged unit, each decoding a quarter of its k range,
+//     so 16 warps per SM hide the latencies on a few staged units.
 //   * The producer stages each unit with ONE 1-D bulk copy (the TMA engine)
 //     plus one 2 KB bulk copy per activation row of the unit's block column,
-//     into a per-worker ring of shared-memory slots, completing an mbarrier.
+//     into a per-group ring of shared-memory slots, completing an mbarrier.
 //   * A consumer decodes its unit straight into MMA operands: the weights
-//     are the B operand (n = 8 output rows) of mma.m16n8k16 bf16 with fp32
-//     accumulate, the activations the A operand (rows 0..7 = up to 8
-//     activation rows, rows 8..15 zero). Lane (g, t) decodes row g of the
-//     unit at k = 64q + 16t + [0, 16) for q = 0..15.
+//     are the A operand (m = 16 output rows) of mma.m16n8k16 bf16 with fp32
+//     accumulate, the activations the B operand (n = 8 = up to 8 activation
+//     rows). Lane (g, t) decodes rows g and g + 8 of the unit at
+//     k = 64q + 16t + [0, 16); warp w of a group takes q in [4w, 4w + 4).
 //   * Decode is byte-parallel: the 3-bit tier-0 codes are spread into
 //     nibbles with three AND + IMAD steps (the IMADs run on the FMA pipe,
 //     idle otherwise), then one PRMT per 4 weights looks four exponents up
@@ -28,9 +30,10 @@
 //     entry makes a weight whose code is 7 decode to exactly +0.
 //   * Escaped weights (about 2% of a N(0, 0.02) tensor) are added back as
 //     fp32 corrections: the loader's escape index lists each block's escape
-//     positions; lane (g, t) handles every fourth escape of row g.
-//   * A worker accumulates a tile's units in registers (each unit's MMA chain
-//     starts from zero; unit sums are added in unit order). A tile covered
+//     positions; the group's lanes split each row's escapes between them.
+//   * A worker accumulates a tile's units in registers (each unit's MMA chains
+//     start from zero; unit sums are added in unit order; the group's four
+//     warp partials are summed in warp order at the tile's end). A tile covered
 //     by one worker is written directly; a tile split across workers goes
 //     through scratch: each contributor writes its partial, the last to
 //     arrive (an atomic counter that it resets) sums them in worker order and
@@ -61,10 +64,14 @@ struct SipArgs {
     float *partials;
     int *counters;
     int *err;
-    int32_t slot_bytes, x_off, spw, nc, workers;
+    int32_t slot_bytes, x_off, spg, ng, workers, dir_cap;
 };
 
-constexpr int kMaxConsumers = 8;
+// A WORKER is a group of kGroupWarps consumer warps sharing each staged unit:
+// warp w of the group decodes quads [4w, 4w + 4) (k in [256w, 256w + 256)) of
+// every row of the unit, and every 16th escape from w * 4 on.
+constexpr int kGroupWarps = 4;
+constexpr int kMaxGroups = 4;
 
 __device__ __forceinline__ int64_t range_start(int64_t w, int64_t U, int64_t W) { return (w * U) / W; }
 __device__ __forceinline__ int64_t worker_of(int64_t u, int64_t U, int64_t W) { return ((u + 1) * W + U - 1) / U - 1; }
@@ -93,14 +100,55 @@ __device__ __forceinline__ void decode4(uint32_t L, uint32_t S, uint32_t th0, ui
     p23 = __byte_perm(lo, hi, 0x7362);
 }
 
-__device__ void store_outputs(const SipArgs &a, int64_t tile, const float (*P)[kMaxVirtualRows]) {
+// One row's quad: 16 weights at k = 64q + 16t + [0, 16) -> four bf16-pair
+// registers per half (p01[j] = weights 4j, 4j+1; p23[j] = weights 4j+2, 4j+3).
+__device__ __forceinline__ void decode_quad(const uint8_t *lit, const uint32_t *tier0, int q, int t, uint32_t sh,
+                                            uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1, uint32_t p01[4],
+                                            uint32_t p23[4]) {
+    const uint4 L = *reinterpret_cast<const uint4 *>(lit + 64 * q + 16 * t);
+    const int wi = (192 * q + 48 * t) >> 5;
+    const uint32_t w0 = tier0[wi], w1 = tier0[wi + 1];
+    const uint32_t lo32 = __funnelshift_r(w0, w1, sh);
+    const uint32_t hi = w1 >> sh;
+    const uint32_t xa = spread_codes(lo32 & 0x00FFFFFFu);
+    const uint32_t xb = spread_codes(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
+    decode4(L.x, xa, th0, th1, tl0, tl1, p01[0], p23[0]);
+    decode4(L.y, xa >> 16, th0, th1, tl0, tl1, p01[1], p23[1]);
+    decode4(L.z, xb, th0, th1, tl0, tl1, p01[2], p23[2]);
+    decode4(L.w, xb >> 16, th0, th1, tl0, tl1, p01[3], p23[3]);
+}
+
+// One quad of both of this lane's rows (g and g + 8) into the MMA chain: the
+// weights are the A operand (16 rows x 16 k), the activations the B operand
+// (16 k x 8 activation rows; lanes g < Mv hold activation row g).
+__device__ __forceinline__ void quad(const uint8_t *lit0, const uint32_t *t00, const uint8_t *lit1,
+                                     const uint32_t *t01, const uint8_t *xg, int q, int t, uint32_t sh, bool has_x,
+                                     uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1, float &d0, float &d1,
+                                     float &d2, float &d3) {
+    uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
+    if (has_x) {
+        X0 = *reinterpret_cast<const uint4 *>(xg + 128 * q + 32 * t);
+        X1 = *reinterpret_cast<const uint4 *>(xg + 128 * q + 32 * t + 16);
+    }
+    uint32_t a01[4], a23[4], c01[4], c23[4];
+    decode_quad(lit0, t00, q, t, sh, th0, th1, tl0, tl1, a01, a23);
+    decode_quad(lit1, t01, q, t, sh, th0, th1, tl0, tl1, c01, c23);
+    mma_bf16_16816(d0, d1, d2, d3, a01[0], c01[0], a23[0], c23[0], X0.x, X0.y);
+    mma_bf16_16816(d0, d1, d2, d3, a01[1], c01[1], a23[1], c23[1], X0.z, X0.w);
+    mma_bf16_16816(d0, d1, d2, d3, a01[2], c01[2], a23[2], c23[2], X1.x, X1.y);
+    mma_bf16_16816(d0, d1, d2, d3, a01[3], c01[3], a23[3], c23[3], X1.z, X1.w);
+}
+
+// P: the tile's partial [16 rows][8 virtual rows]; outputs m < M_out combine
+// their nsplit virtual rows, add the bias in fp32 and round once.
+__device__ void store_outputs(const SipArgs &a, int64_t tile, const float *P) {
     const int lane = threadIdx.x & 31;
     for (int o = lane; o < kUnitRows * a.M_out; o += 32) {
         const int r = o % kUnitRows, m = o / kUnitRows;
         const int64_t row = tile * kUnitRows + r;
         if (row >= a.rows) continue;
-        float y = P[r][m * a.nsplit];
-        for (int s = 1; s < a.nsplit; ++s) y += P[r][m * a.nsplit + s];
+        float y = P[r * 8 + m * a.nsplit];
+        for (int s = 1; s < a.nsplit; ++s) y += P[r * 8 + m * a.nsplit + s];
         if (a.bias) y += bf16_bits_to_f32(a.bias[row]);
         if (a.out_f32)
             reinterpret_cast<float *>(a.out)[m * a.rows + row] = y;
@@ -109,66 +157,108 @@ __device__ void store_outputs(const SipArgs &a, int64_t tile, const float (*P)[k
     }
 }
 
-__global__ void __launch_bounds__(32 * (1 + kMaxConsumers), 1) sip_gemv_kernel(SipArgs a) {
+__device__ __forceinline__ void group_sync(int group) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(kGroupWarps * 32) : "memory");
+}
+
+// One row's escapes (this lane's share) added to its corrections.
+template <int MV>
+__device__ __forceinline__ void escapes(const uint8_t *lit, RowEntry e, const uint8_t *xs, int j0, float corr[MV]) {
+    const int ne = e.nesc;
+    if (ne <= j0) return;
+    const uint8_t *term = lit + 1408;
+    const uint16_t *idx = reinterpret_cast<const uint16_t *>(lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
+    for (int j = j0; j < ne; j += 4 * kGroupWarps) {
+        const uint32_t pos = idx[j];
+        const uint32_t ex = term[j];
+        const uint32_t lb = lit[pos];
+        const float wv = __uint_as_float(((lb & 0x80u) << 24) | (ex << 23) | ((lb & 0x7Fu) << 16));
+        const uint8_t *xp = xs + pos * 2;
+#pragma unroll
+        for (int v = 0; v < MV; ++v)
+            corr[v] = fmaf(bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(xp + v * kXRowStride)), wv, corr[v]);
+    }
+}
+
+template <int MV>
+__global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_gemv_kernel(SipArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nslots = a.nc * a.spw;
+    const int nslots = a.ng * a.spg;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nslots * a.slot_bytes);
     uint64_t *empty = full + nslots;
-    float *xch = reinterpret_cast<float *>(empty + nslots);  // [nc][8][8] exchange per consumer
+    float *gbuf = reinterpret_cast<float *>(empty + nslots);  // [ng][kGroupWarps][16][8] partials
+    uint32_t *dir = reinterpret_cast<uint32_t *>(gbuf + a.ng * kGroupWarps * 128);  // this CTA's unit starts
+    const int64_t U = a.units, W = a.workers, NB = a.NB;
+    const int64_t cta_u0 = range_start((int64_t)blockIdx.x * a.ng, U, W);
+    const int64_t cta_u1 = range_start((int64_t)(blockIdx.x + 1) * a.ng, U, W);
+    const bool dir_in_smem = (cta_u1 - cta_u0 + 1) <= a.dir_cap;
     if (threadIdx.x == 0) {
         for (int s = 0; s < nslots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], kGroupWarps);
         }
         mbar_fence_init();
     }
+    if (warp == 0 && dir_in_smem)
+        for (int64_t i = lane; i <= cta_u1 - cta_u0; i += 32) dir[i] = a.unit16[cta_u0 + i];
     __syncthreads();
-    const int64_t U = a.units, W = a.workers, NB = a.NB;
 
     if (warp == 0) {
         // ---------------------------------------------------- producer --
+        // per-group cursors kept in registers (no division in the loop):
+        // next unit, its end, its block column, the slot it goes to and the
+        // number of units staged so far
         if (lane == 0) {
+            int32_t nu[kMaxGroups], eu[kMaxGroups], bc[kMaxGroups], si[kMaxGroups], fills[kMaxGroups];
+#pragma unroll
+            for (int g = 0; g < kMaxGroups; ++g) {
+                const int64_t w = (int64_t)blockIdx.x * a.ng + g;
+                nu[g] = g < a.ng ? (int32_t)range_start(w, U, W) : 0;
+                eu[g] = g < a.ng ? (int32_t)range_start(w + 1, U, W) : 0;
+                bc[g] = (int32_t)(nu[g] % NB);
+                si[g] = 0;
+                fills[g] = 0;
+            }
             bool ok = true;
-            int64_t issued[kMaxConsumers];
-            for (int c = 0; c < a.nc; ++c) issued[c] = 0;
-            for (int64_t round = 0; ok; ++round) {
+            for (;;) {
                 bool any = false;
-                for (int c = 0; c < a.nc && ok; ++c) {
-                    const int64_t w = (int64_t)blockIdx.x * a.nc + c;
-                    const int64_t u0 = range_start(w, U, W), u1 = range_start(w + 1, U, W);
-                    if (u0 + round >= u1) continue;
+#pragma unroll
+                for (int g = 0; g < kMaxGroups; ++g) {
+                    if (!ok || nu[g] >= eu[g]) continue;
                     any = true;
-                    const int64_t u = u0 + round;
-                    const int slot = c * a.spw + (int)(round % a.spw);
-                    const int64_t use = round / a.spw;
+                    const int slot = g * a.spg + si[g];
+                    const int use = fills[g] / a.spg;
                     if (use > 0 && !mbar_wait(&empty[slot], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) {
                         ok = false;
-                        break;
+                        continue;
                     }
-                    const uint32_t q0 = a.unit16[u], q1 = a.unit16[u + 1];
+                    const int32_t u = nu[g];
+                    const uint32_t q0 = dir_in_smem ? dir[u - cta_u0] : a.unit16[u];
+                    const uint32_t q1 = dir_in_smem ? dir[u + 1 - cta_u0] : a.unit16[u + 1];
                     const uint32_t ubytes = (q1 - q0) * 16u;
                     uint8_t *dst = smem + (size_t)slot * a.slot_bytes;
                     mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
                     bulk_g2s(dst, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
-                    const int64_t b = u % NB;
+                    const uint16_t *xb = a.x + (size_t)bc[g] * 1024;
                     for (int v = 0; v < a.Mv; ++v)
-                        bulk_g2s(dst + a.x_off + v * kXRowStride, a.x + v * a.x_stride + b * 1024, 2048u,
-                                 &full[slot]);
-                    issued[c] = round + 1;
+                        bulk_g2s(dst + a.x_off + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
+                    nu[g] = u + 1;
+                    bc[g] = (bc[g] + 1 == NB) ? 0 : bc[g] + 1;
+                    si[g] = (si[g] + 1 == a.spg) ? 0 : si[g] + 1;
+                    fills[g] += 1;
                 }
-                if (!any) break;
+                if (!any || !ok) break;
             }
             // drain: every copy this producer issued lands before the CTA exits
-            for (int c = 0; c < a.nc; ++c) {
-                for (int k = 0; k < a.spw; ++k) {
-                    // the last round that used slot (c, k)
-                    int64_t last = -1;
-                    for (int64_t r = issued[c] - 1; r >= 0 && r >= issued[c] - a.spw; --r)
-                        if (r % a.spw == k) { last = r; break; }
+#pragma unroll
+            for (int g = 0; g < kMaxGroups; ++g) {
+                for (int k = 0; k < a.spg && g < a.ng; ++k) {
+                    int last = -1;
+                    for (int f = fills[g] - 1; f >= 0 && f >= fills[g] - a.spg; --f)
+                        if (f % a.spg == k) { last = f; break; }
                     if (last < 0) continue;
-                    const int slot = c * a.spw + k;
-                    mbar_wait(&full[slot], (uint32_t)((last / a.spw) & 1), a.err, kErrWaitDrain);
+                    mbar_wait(&full[g * a.spg + k], (uint32_t)((last / a.spg) & 1), a.err, kErrWaitDrain);
                 }
             }
         }
@@ -176,185 +266,177 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumers), 1) sip_gemv_kernel(S
     }
 
     // ------------------------------------------------------- consumers --
-    const int c = warp - 1;
-    const int64_t w = (int64_t)blockIdx.x * a.nc + c;
+    const int gi = (warp - 1) / kGroupWarps, wi = (warp - 1) % kGroupWarps;
+    const int64_t w = (int64_t)blockIdx.x * a.ng + gi;
     const int64_t u0 = range_start(w, U, W), u1 = range_start(w + 1, U, W);
     const int g = lane >> 2, t = lane & 3;
     const uint32_t th0 = a.th0, th1 = a.th1, tl0 = a.tl0, tl1 = a.tl1;
-    const int Mv = a.Mv;
-    float (*X)[kMaxVirtualRows] = reinterpret_cast<float (*)[kMaxVirtualRows]>(xch + c * 64);
+    float *Pw = gbuf + (gi * kGroupWarps + wi) * 128;  // this warp's [16 rows][8 virtual rows]
+    float *P0 = gbuf + (gi * kGroupWarps) * 128;       // the group's sum
 
-    float acc0 = 0.f, acc1 = 0.f;  // D[batch g][rows 2t, 2t+1], summed over the tile's units
-    float corr[kMaxVirtualRows];   // row g's escape corrections per virtual activation row
+    // D[rows g, g + 8][activation rows 2t, 2t + 1] over this warp's k range, the tile so far
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    float cg[MV], cg8[MV];  // rows g and g + 8: escape corrections (this lane's share)
 #pragma unroll
-    for (int v = 0; v < kMaxVirtualRows; ++v) corr[v] = 0.f;
+    for (int v = 0; v < MV; ++v) cg[v] = cg8[v] = 0.f;
     int64_t tile = u0 / NB;
-    const int64_t first_tile = u0 / NB, last_tile = (u1 - 1) / NB;
+    const int64_t first_tile = u0 / NB;
 
     auto flush = [&](int64_t tl) {
-        // corrections: sum over the row's four lanes, then hand each to the
-        // lane holding D[batch][row]
 #pragma unroll
-        for (int v = 0; v < kMaxVirtualRows; ++v) {
-            float s = corr[v];
+        for (int v = 0; v < MV; ++v) {
+            float s = cg[v], s8 = cg8[v];
             s += __shfl_xor_sync(0xffffffffu, s, 1);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
-            corr[v] = s;
+            s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+            s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+            cg[v] = s;
+            cg8[v] = s8;
         }
-        __syncwarp();
+        // this warp's partial: corrections by row, then the D owners add theirs
         if (t == 0) {
 #pragma unroll
-            for (int v = 0; v < kMaxVirtualRows; ++v) X[g][v] = corr[v];
+            for (int v = 0; v < kMaxVirtualRows; ++v) {
+                Pw[g * 8 + v] = v < MV ? cg[v] : 0.f;
+                Pw[(g + 8) * 8 + v] = v < MV ? cg8[v] : 0.f;
+            }
         }
         __syncwarp();
-        float y0 = 0.f, y1 = 0.f;
-        if (g < Mv) {
-            y0 = acc0 + X[2 * t][g];
-            y1 = acc1 + X[2 * t + 1][g];
-        }
+        Pw[g * 8 + 2 * t] += acc0;
+        Pw[g * 8 + 2 * t + 1] += acc1;
+        Pw[(g + 8) * 8 + 2 * t] += acc2;
+        Pw[(g + 8) * 8 + 2 * t + 1] += acc3;
         __syncwarp();
-        // the tile's partial P[row][virtual row]
+        group_sync(gi);
+        if (wi == 0) {
+            // the group's sum, warps in order
+            float s[4];
 #pragma unroll
-        for (int v = 0; v < kMaxVirtualRows; ++v) X[g][v] = 0.f;
-        __syncwarp();
-        if (g < Mv) {
-            X[2 * t][g] = y0;
-            X[2 * t + 1][g] = y1;
-        }
-        __syncwarp();
-        const bool whole = tl * NB >= u0 && (tl + 1) * NB <= u1;
-        if (whole) {
-            store_outputs(a, tl, X);
-        } else {
-            const int slot = (tl == first_tile) ? 0 : 1;
-            float *mine = a.partials + (w * 2 + slot) * 64;
-            mine[lane] = X[lane / 8][lane % 8];
-            mine[lane + 32] = X[4 + lane / 8][lane % 8];
-            __threadfence();
+            for (int i = 0; i < 4; ++i) {
+                s[i] = P0[lane + 32 * i];
+#pragma unroll
+                for (int k = 1; k < kGroupWarps; ++k) s[i] += P0[k * 128 + lane + 32 * i];
+            }
             __syncwarp();
-            int last = 0;
-            if (lane == 0) {
-                const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
-                const int n = (int)(wl - wf + 1);
-                const int old = atomicAdd(&a.counters[tl], 1);
-                last = (old == n - 1);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) P0[lane + 32 * i] = s[i];
+            __syncwarp();
+            const bool whole = tl * NB >= u0 && (tl + 1) * NB <= u1;
+            if (whole) {
+                store_outputs(a, tl, P0);
+            } else {
+                const int slot = (tl == first_tile) ? 0 : 1;
+                float *mine = a.partials + (w * 2 + slot) * 128;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) mine[lane + 32 * i] = s[i];
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
+                    const int n = (int)(wl - wf + 1);
+                    const int old = atomicAdd(&a.counters[tl], 1);
+                    last = (old == n - 1);
+                    if (last) {
+                        __threadfence();
+                        a.counters[tl] = 0;
+                    }
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
-                    a.counters[tl] = 0;
-                }
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence();
-                const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
-                float s0 = 0.f, s1 = 0.f;
-                for (int64_t j = wf; j <= wl; ++j) {
-                    const int64_t j0 = range_start(j, U, W);
-                    const int sj = (tl == j0 / NB) ? 0 : 1;
-                    const float *pp = a.partials + (j * 2 + sj) * 64;
-                    s0 += __ldcg(pp + lane);
-                    s1 += __ldcg(pp + lane + 32);
-                }
-                __syncwarp();
-                X[lane / 8][lane % 8] = s0;
-                X[4 + lane / 8][lane % 8] = s1;
-                __syncwarp();
-                store_outputs(a, tl, X);
-            }
-        }
-        __syncwarp();
-        acc0 = acc1 = 0.f;
+                    const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
+                    float r[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int64_t j = wf; j <= wl; ++j) {
+                        const int64_t j0 = range_start(j, U, W);
+                        const int sj = (tl == j0 / NB) ? 0 : 1;
+                        const float *pp = a.partials + (j * 2 + sj) * 128;
 #pragma unroll
-        for (int v = 0; v < kMaxVirtualRows; ++v) corr[v] = 0.f;
+                        for (int i = 0; i < 4; ++i) r[i] += __ldcg(pp + lane + 32 * i);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) P0[lane + 32 * i] = r[i];
+                    __syncwarp();
+                    store_outputs(a, tl, P0);
+                }
+            }
+            __syncwarp();
+        }
+        group_sync(gi);
+        acc0 = acc1 = acc2 = acc3 = 0.f;
+#pragma unroll
+        for (int v = 0; v < MV; ++v) cg[v] = cg8[v] = 0.f;
     };
 
     bool ok = true;
+    const uint32_t sh = (t & 1) ? 16u : 0u;
+    const bool has_x = g < MV;
+    int32_t bcol = (int32_t)(u0 % NB);  // block column of unit u
+    int sidx = 0;                       // slot of unit u within the group's ring
+    uint32_t par = 0;                   // parity of that slot's current fill
+    const int q0 = 4 * wi, j0 = 4 * wi + t;
     for (int64_t u = u0; u < u1; ++u) {
-        const int64_t k = u - u0;
-        const int slot = c * a.spw + (int)(k % a.spw);
-        if (!mbar_wait(&full[slot], (uint32_t)((k / a.spw) & 1), a.err, kErrWaitFull)) {
+        const int slot = gi * a.spg + sidx;
+        if (!mbar_wait(&full[slot], par, a.err, kErrWaitFull)) {
             ok = false;
             break;
         }
-        const int64_t ut = u / NB;
-        if (ut != tile) {
+        if (bcol == 0 && u != u0) {
             flush(tile);
-            tile = ut;
+            tile += 1;
         }
         const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
-        const RowEntry e = reinterpret_cast<const RowEntry *>(base)[g];
-        const uint8_t *lit = base + (size_t)e.off16 * 16;
-        const uint32_t *tier0 = reinterpret_cast<const uint32_t *>(lit + 1024);
+        const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
+        const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
+        const uint8_t *lit0 = base + (size_t)e0.off16 * 16;
+        const uint8_t *lit1 = base + (size_t)e1.off16 * 16;
+        const uint32_t *t00 = reinterpret_cast<const uint32_t *>(lit0 + 1024);
+        const uint32_t *t01 = reinterpret_cast<const uint32_t *>(lit1 + 1024);
         const uint8_t *xs = base + a.x_off;
         const uint8_t *xg = xs + g * kXRowStride;
-        const uint32_t sh = (t & 1) ? 16u : 0u;
         float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-#pragma unroll 2
-        for (int q = 0; q < 16; ++q) {
-            const uint4 L = *reinterpret_cast<const uint4 *>(lit + 64 * q + 16 * t);
-            const int wi = (192 * q + 48 * t) >> 5;
-            const uint32_t w0 = tier0[wi], w1 = tier0[wi + 1];
-            const uint32_t lo32 = __funnelshift_r(w0, w1, sh);
-            const uint32_t hi = w1 >> sh;
-            const uint32_t xa = spread_codes(lo32 & 0x00FFFFFFu);
-            const uint32_t xb = spread_codes(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
-            uint32_t b0[4], b1[4];
-            decode4(L.x, xa, th0, th1, tl0, tl1, b0[0], b1[0]);
-            decode4(L.y, xa >> 16, th0, th1, tl0, tl1, b0[1], b1[1]);
-            decode4(L.z, xb, th0, th1, tl0, tl1, b0[2], b1[2]);
-            decode4(L.w, xb >> 16, th0, th1, tl0, tl1, b0[3], b1[3]);
-            uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-            if (g < Mv) {
-                X0 = *reinterpret_cast<const uint4 *>(xg + 128 * q + 32 * t);
-                X1 = *reinterpret_cast<const uint4 *>(xg + 128 * q + 32 * t + 16);
-            }
-            mma_bf16_16816(d0, d1, d2, d3, X0.x, 0u, X0.y, 0u, b0[0], b1[0]);
-            mma_bf16_16816(d0, d1, d2, d3, X0.z, 0u, X0.w, 0u, b0[1], b1[1]);
-            mma_bf16_16816(d0, d1, d2, d3, X1.x, 0u, X1.y, 0u, b0[2], b1[2]);
-            mma_bf16_16816(d0, d1, d2, d3, X1.z, 0u, X1.w, 0u, b0[3], b1[3]);
-        }
-        // escapes of row g: every fourth one, from lane t
-        const int ne = e.nesc;
-        if (ne) {
-            const uint8_t *term = lit + 1408;
-            const uint16_t *idx = reinterpret_cast<const uint16_t *>(lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
-            for (int j = t; j < ne; j += 4) {
-                const uint32_t pos = idx[j];
-                const uint32_t ex = term[j];
-                const uint32_t lb = lit[pos];
-                const float wv = __uint_as_float(((lb & 0x80u) << 24) | (ex << 23) | ((lb & 0x7Fu) << 16));
-#pragma unroll
-                for (int v = 0; v < kMaxVirtualRows; ++v) {
-                    if (v < Mv) {
-                        const uint32_t xb16 = *reinterpret_cast<const uint16_t *>(xs + v * kXRowStride + pos * 2);
-                        corr[v] = fmaf(bf16_bits_to_f32(xb16), wv, corr[v]);
-                    }
-                }
-            }
-        }
+        float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
+        quad(lit0, t00, lit1, t01, xg, q0 + 0, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+        quad(lit0, t00, lit1, t01, xg, q0 + 1, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+        quad(lit0, t00, lit1, t01, xg, q0 + 2, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+        quad(lit0, t00, lit1, t01, xg, q0 + 3, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+        // escapes of rows g and g + 8: the group's warps take every 16th one, lane t every 4th of those
+        escapes<MV>(lit0, e0, xs, j0, cg);
+        escapes<MV>(lit1, e1, xs, j0, cg8);
         acc0 += d0;
+        acc0 += f0;
         acc1 += d1;
+        acc1 += f1;
+        acc2 += d2;
+        acc2 += f2;
+        acc3 += d3;
+        acc3 += f3;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        bcol = (bcol + 1 == NB) ? 0 : bcol + 1;
+        if (++sidx == a.spg) {
+            sidx = 0;
+            par ^= 1u;
+        }
     }
     if (ok && u1 > u0) flush(tile);
-    (void)last_tile;
 }
 
-// Shared-memory plan for a launch: slot size, slots per consumer, consumers.
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spw, int *nc) {
+// Shared-memory plan for a launch: slot size, slots per group, groups.
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spg, int *ng, int dir_cap) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
     const int sb = unit + Mv * kXRowStride;
     const int budget = 227 * 1024;
-    for (int c = kMaxConsumers; c >= 1; c /= 2) {
-        for (int s = 3; s >= 2; --s) {
-            int need = c * s * (sb + 16) + c * 64 * 4 + 128;
-            if (need <= budget) {
-                *slot_bytes = sb;
-                *spw = s;
-                *nc = c;
-                return need;
-            }
+    const int fixed = kMaxGroups * kGroupWarps * 128 * 4 + (dir_cap + 1) * 4 + 256;
+    const int plans[][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 3}, {2, 2}, {1, 3}, {1, 2}};
+    for (const auto &pl : plans) {
+        int need = pl[0] * pl[1] * (sb + 16) + fixed;
+        if (need <= budget) {
+            *slot_bytes = sb;
+            *ng = pl[0];
+            *spg = pl[1];
+            return need;
         }
     }
     return -1;
@@ -362,31 +444,37 @@ int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spw, int 
 
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                     const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg) {
-    int slot_bytes = 0, spw = 0, nc = 0;
-    int smem = sip_shared_bytes(t, Mv, &slot_bytes, &spw, &nc);
+    const dm::TensorLayout &L = t->L;
+    int slot_bytes = 0, spg = 0, ng = 0;
+    // one CTA per SM; each worker (a group of warps) owns at least one unit
+    const int64_t grid0 = std::min<int64_t>(t->sms, L.units);
+    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid0 - 1) / grid0 + 2);
+    int smem = sip_shared_bytes(t, Mv, &slot_bytes, &spg, &ng, dir_cap);
     if (smem < 0) {
         msg = "sip kernel: a unit does not fit in shared memory";
         return DM_EINVAL;
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(sip_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    using Kern = void (*)(SipArgs);
+    static const Kern kernels[kMaxVirtualRows] = {sip_gemv_kernel<1>, sip_gemv_kernel<2>, sip_gemv_kernel<3>,
+                                                  sip_gemv_kernel<4>, sip_gemv_kernel<5>, sip_gemv_kernel<6>,
+                                                  sip_gemv_kernel<7>, sip_gemv_kernel<8>};
+    static bool attr_set[kMaxVirtualRows] = {false};
+    if (Mv < 1 || Mv > kMaxVirtualRows) {
+        msg = "sip kernel: 1..8 virtual activation rows";
+        return DM_EINVAL;
+    }
+    const Kern kern = kernels[Mv - 1];
+    if (!attr_set[Mv - 1]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
-        attr_set = true;
+        attr_set[Mv - 1] = true;
     }
-    const dm::TensorLayout &L = t->L;
-    // one CTA per SM; every worker (consumer warp) owns at least one unit
-    int64_t grid, workers;
-    if (L.units >= (int64_t)t->sms * nc) {
-        grid = t->sms;
-    } else {
-        grid = std::min<int64_t>(t->sms, L.units);
-        nc = (int)std::max<int64_t>(1, std::min<int64_t>(nc, L.units / grid));
-    }
-    workers = grid * nc;
+    int64_t grid = grid0;
+    if (L.units < (int64_t)t->sms * ng) ng = (int)std::max<int64_t>(1, std::min<int64_t>(ng, L.units / grid));
+    const int64_t workers = grid * ng;
     if (workers > t->S.max_workers) {
         msg = "sip kernel: scratch sized for fewer workers";
         return DM_EINVAL;
@@ -421,10 +509,11 @@ int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, in
     a.err = t->S.err;
     a.slot_bytes = slot_bytes;
     a.x_off = (t->L.max_unit_bytes + 127) & ~127;
-    a.spw = spw;
-    a.nc = nc;
+    a.spg = spg;
+    a.ng = ng;
     a.workers = (int32_t)workers;
-    sip_gemv_kernel<<<(unsigned)grid, 32 * (1 + nc), smem, (cudaStream_t)stream>>>(a);
+    a.dir_cap = dir_cap;
+    kern<<<(unsigned)grid, 32 * (1 + ng * kGroupWarps), smem, (cudaStream_t)stream>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
