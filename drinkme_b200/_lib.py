@@ -15,7 +15,8 @@ DM_OK, DM_EINVAL, DM_ECUDA, DM_EDEVICE, DM_ENOMEM = 0, 1, 2, 3, 4
 DM_BF16, DM_F32 = 0, 1
 DM_MC_MAX = 8
 
-EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv", "dm_decode",
+EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
+           "dm_gemv_noalloc", "dm_decode",
            "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check")
 
 
@@ -53,6 +54,7 @@ def lib():
         L.dm_tensor_destroy.argtypes = [p]
         L.dm_tensor_get_info.argtypes = [p, ct.POINTER(TensorInfo)]
         L.dm_gemv.argtypes = [p, p, i32, i64, p, p, i32, p, cp, sz]
+        L.dm_gemv_noalloc.argtypes = [p, p, i32, i64, p, p, i32, p, cp, sz]
         L.dm_decode.argtypes = [p, p, p, cp, sz]
         L.dm_prepare_schedule.argtypes = [p, sz, p, i64, p, i32, i32, i64, p, p, cp, sz]
         L.dm_gemv_raw.argtypes = [p, i64, i64, p, i32, i64, p, p, i32, p, cp, sz]

@@ -522,4 +522,88 @@ int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, in
     return DM_OK;
 }
 
+// The same launch with caller-supplied scratch (partials for `max_workers`
+// workers, per-tile counters that are zero on entry, the error word): the
+// variant behind dm_gemv_noalloc, whose scratch is a static device array.
+int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
+                         const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
+                         int64_t max_workers, void *stream, std::string &msg) {
+    const dm::TensorLayout &L = t->L;
+    int slot_bytes = 0, spg = 0, ng = 0;
+    const int64_t grid0 = std::min<int64_t>(t->sms, L.units);
+    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid0 - 1) / grid0 + 2);
+    int smem = sip_shared_bytes(t, Mv, &slot_bytes, &spg, &ng, dir_cap);
+    if (smem < 0) {
+        msg = "sip kernel: a unit does not fit in shared memory";
+        return DM_EINVAL;
+    }
+    using Kern = void (*)(SipArgs);
+    static const Kern kernels[kMaxVirtualRows] = {sip_gemv_kernel<1>, sip_gemv_kernel<2>, sip_gemv_kernel<3>,
+                                                  sip_gemv_kernel<4>, sip_gemv_kernel<5>, sip_gemv_kernel<6>,
+                                                  sip_gemv_kernel<7>, sip_gemv_kernel<8>};
+    static bool attr_set[kMaxVirtualRows] = {false};
+    if (Mv < 1 || Mv > kMaxVirtualRows) {
+        msg = "sip kernel: 1..8 virtual activation rows";
+        return DM_EINVAL;
+    }
+    const Kern kern = kernels[Mv - 1];
+    if (!attr_set[Mv - 1]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) {
+            msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+            return DM_ECUDA;
+        }
+        attr_set[Mv - 1] = true;
+    }
+    const int64_t grid = grid0;
+    if (L.units < (int64_t)t->sms * ng) ng = (int)std::max<int64_t>(1, std::min<int64_t>(ng, L.units / grid));
+    const int64_t workers = grid * ng;
+    if (workers > max_workers) {
+        msg = "sip kernel: " + std::to_string(workers) + " stream-K workers exceed the scratch's " +
+              std::to_string(max_workers);
+        return DM_EINVAL;
+    }
+    SipArgs a{};
+    a.data = t->d_data;
+    a.unit16 = t->d_unit16;
+    a.units = L.units;
+    a.rows = L.rows;
+    a.NB = L.NB;
+    uint8_t th[8], tl[8];
+    for (int c = 0; c < 7; ++c) {
+        th[c] = (uint8_t)(L.palette[c] >> 1);
+        tl[c] = (uint8_t)((L.palette[c] & 1u) << 7);
+    }
+    th[7] = 0x80;
+    tl[7] = 0x7F;
+    a.th0 = th[0] | (th[1] << 8) | (th[2] << 16) | ((uint32_t)th[3] << 24);
+    a.th1 = th[4] | (th[5] << 8) | (th[6] << 16) | ((uint32_t)th[7] << 24);
+    a.tl0 = tl[0] | (tl[1] << 8) | (tl[2] << 16) | ((uint32_t)tl[3] << 24);
+    a.tl1 = tl[4] | (tl[5] << 8) | (tl[6] << 16) | ((uint32_t)tl[7] << 24);
+    a.x = xv;
+    a.x_stride = x_stride;
+    a.Mv = Mv;
+    a.nsplit = nsplit;
+    a.M_out = M_out;
+    a.bias = bias;
+    a.out = out;
+    a.out_f32 = out_f32;
+    a.partials = partials;
+    a.counters = counters;
+    a.err = err;
+    a.slot_bytes = slot_bytes;
+    a.x_off = (t->L.max_unit_bytes + 127) & ~127;
+    a.spg = spg;
+    a.ng = ng;
+    a.workers = (int32_t)workers;
+    a.dir_cap = dir_cap;
+    kern<<<(unsigned)grid, 32 * (1 + ng * kGroupWarps), smem, (cudaStream_t)stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
+        return DM_ECUDA;
+    }
+    return DM_OK;
+}
+
 }  // namespace dm

@@ -97,6 +97,23 @@ int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info);
 int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
             int32_t out_dtype, void *stream, char *err, size_t err_len);
 
+/* dm_gemv for callers that cannot allocate device memory at call time — a
+ * serving engine that has given all free HBM to its own pool before decoding
+ * starts, or a decode loop that must not call cudaMalloc (which can
+ * synchronise the device). No counterpart in the reference. Same arguments,
+ * results and errors as dm_gemv (bitwise the same outputs); the only
+ * difference is where the kernel's scratch lives: one static array in the
+ * library's device memory (about 1.45 MiB, held on every GPU that loads the
+ * library until exit) instead of the tensor's own buffers. This call makes no
+ * cudaMalloc, cudaFree or other allocating call. Limits of that array
+ * (DM_EINVAL beyond them): tensors or row shards of at most 262,144 rows,
+ * fp32 activations of at most 32,768 columns. The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress): make it before
+ * capturing a CUDA graph on that device. Every call shares the array, so calls
+ * that overlap on the GPU (on any tensor, any stream) race. */
+int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
+                    int32_t out_dtype, void *stream, char *err, size_t err_len);
+
 /* The shard's decoded bf16 bit patterns, uint16 [rows, C] — replaces
  * radix_ops.decode_bits (src/drinkme/codec/radix_ops.py:418-427). */
 int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *err, size_t err_len);
