@@ -76,6 +76,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// CTAs (on SMs this grid leaves free) before this grid ends ...
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// ... and wait until the grid this one depends on has completed and its
+// writes are visible (returns at once when there is none).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <int LUT>
 __device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;

@@ -193,6 +193,7 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
     const int64_t cta_u0 = range_start((int64_t)blockIdx.x * a.ng, U, W);
     const int64_t cta_u1 = range_start((int64_t)(blockIdx.x + 1) * a.ng, U, W);
     const bool dir_in_smem = (cta_u1 - cta_u0 + 1) <= a.dir_cap;
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < nslots; ++s) {
             mbar_init(&full[s], 1);
@@ -221,6 +222,36 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
                 fills[g] = 0;
             }
             bool ok = true;
+            // the weights of every group's first spg units do not depend on
+            // the kernel before this one: stage them before waiting for it,
+            // then add their activation rows once it has completed
+#pragma unroll
+            for (int g = 0; g < kMaxGroups; ++g) {
+                for (int k = 0; k < a.spg && nu[g] + k < eu[g]; ++k) {
+                    const int32_t u = nu[g] + k;
+                    const int slot = g * a.spg + k;
+                    const uint32_t q0 = dir_in_smem ? dir[u - cta_u0] : a.unit16[u];
+                    const uint32_t q1 = dir_in_smem ? dir[u + 1 - cta_u0] : a.unit16[u + 1];
+                    const uint32_t ubytes = (q1 - q0) * 16u;
+                    mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
+                    bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
+                }
+            }
+            pdl_wait();
+#pragma unroll
+            for (int g = 0; g < kMaxGroups; ++g) {
+                for (int k = 0; k < a.spg && nu[g] < eu[g]; ++k) {
+                    const int slot = g * a.spg + k;
+                    const uint16_t *xb = a.x + (size_t)bc[g] * 1024;
+                    uint8_t *dst = smem + (size_t)slot * a.slot_bytes;
+                    for (int v = 0; v < a.Mv; ++v)
+                        bulk_g2s(dst + a.x_off + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
+                    nu[g] += 1;
+                    bc[g] = (bc[g] + 1 == NB) ? 0 : bc[g] + 1;
+                    si[g] = (si[g] + 1 == a.spg) ? 0 : si[g] + 1;
+                    fills[g] += 1;
+                }
+            }
             for (;;) {
                 bool any = false;
 #pragma unroll
@@ -513,8 +544,17 @@ int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, in
     a.ng = ng;
     a.workers = (int32_t)workers;
     a.dir_cap = dir_cap;
-    kern<<<(unsigned)grid, 32 * (1 + ng * kGroupWarps), smem, (cudaStream_t)stream>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(32 * (1 + ng * kGroupWarps));
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {
         msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
         return DM_ECUDA;
@@ -597,8 +637,17 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.ng = ng;
     a.workers = (int32_t)workers;
     a.dir_cap = dir_cap;
-    kern<<<(unsigned)grid, 32 * (1 + ng * kGroupWarps), smem, (cudaStream_t)stream>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(32 * (1 + ng * kGroupWarps));
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {
         msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
         return DM_ECUDA;

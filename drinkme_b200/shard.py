@@ -19,9 +19,9 @@ import torch
 from . import radix_ops, swap
 
 
-def row_range(R: int, rank: int, world: int, align: int = 8) -> tuple[int, int]:
+def row_range(R: int, rank: int, world: int, align: int = 16) -> tuple[int, int]:
     """Rank `rank`'s rows of R split over `world` ranks: equal shards of
-    ceil(R / world) rows rounded up to `align` (whole 8-row units), the last
+    ceil(R / world) rows rounded up to `align` (whole 16-row units), the last
     shard taking what is left (possibly nothing)."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"row_range: rank {rank} outside a world of {world}")
@@ -32,7 +32,7 @@ def row_range(R: int, rank: int, world: int, align: int = 8) -> tuple[int, int]:
     return r0, r1
 
 
-def shard_rows_padded(R: int, world: int, align: int = 8) -> int:
+def shard_rows_padded(R: int, world: int, align: int = 16) -> int:
     """The rows every rank's gather slot holds (the largest shard)."""
     return row_range(R, 0, world, align)[1]
 
