@@ -49,6 +49,17 @@ WORKLOADS = {
 # which input each linear reads: the hidden state (the step's H2D input) or
 # the attention / MLP intermediate (a resident synthetic activation)
 HIDDEN_INPUT = {"q", "k", "v", "gate", "up"}
+# linears that read the same activations run as ONE fused launch (one
+# dm_tensor_create_multi handle each): q|k|v and gate|up
+GROUPS = (("qkv", ("q", "k", "v")), ("o", ("o",)), ("gate_up", ("gate", "up")), ("down", ("down",)))
+
+
+def groups_of(wl, fuse=True):
+    """[(group name, [(linear, R, C), ...])] in step order."""
+    lin = {n: (n, R, C) for n, R, C in WORKLOADS[wl]["linears"]}
+    if not fuse:
+        return [(n, [lin[n]]) for n, _, _ in WORKLOADS[wl]["linears"]]
+    return [(g, [lin[n] for n in names]) for g, names in GROUPS]
 
 
 def parse():
@@ -58,6 +69,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="qwen3-32b")
+    ap.add_argument("--no-fuse", action="store_true", help="one launch per linear instead of q|k|v and gate|up")
     ap.add_argument("--variants", type=int, default=2,
                     help="distinct random tensors per shape; every layer still gets its own HBM copy")
     ap.add_argument("--no-secondary", action="store_true", help="skip the qwen3-8b chain beside the headline")
@@ -137,35 +149,42 @@ def make_bits(R, C, seed, device):
     return w.view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def build_stack(wl, rank, world, device, variants, log):
-    """Per layer and linear: this rank's row shard of a packed sip tensor, each
-    in its own HBM (variants distinct random tensors per shape, cloned per
-    layer). Returns (layers[[runtime]], pack stats)."""
+def build_stack(wl, rank, world, device, variants, log, fuse=True):
+    """Per layer and launch group: this rank's row shard of every linear of
+    the group (a fused handle for q|k|v and gate|up), each layer in its own
+    HBM (variants distinct random tensors per shape, cloned per layer).
+    Returns (layers[[runtime]], pack stats)."""
     from drinkme_b200 import codec, shard, swap
 
     spec = WORKLOADS[wl]
-    base = {}
+    groups = groups_of(wl, fuse)
     stats = {}
+    base = {}
     t0 = time.time()
-    for j, (name, R, C) in enumerate(spec["linears"]):
-        for v in range(variants):
-            key = (R, C, v)
-            if key in base:
-                continue
+    for v in range(variants):
+        packs = {}
+        for j, (name, R, C) in enumerate(spec["linears"]):
             bits = make_bits(R, C, seed=1000 * v + 17 * j + R + C, device=device)
             p = codec.pack_array_radix(bits, "sip")
             assert p is not None
-            r0, r1 = shard.row_range(R, rank, world)
-            rt = swap.to_device_radix(p, device, r0, r1) if r1 > r0 else None
-            base[key] = rt
-            stats[key] = {"bpw": p["bpw"], "words": int(p["rx_data"].size)}
-            del bits, p
-    log(f"packed {len(base)} distinct tensors in {time.time() - t0:.1f}s")
+            packs[name] = p
+            stats[(name, v)] = {"bpw": p["bpw"], "words": int(p["rx_data"].size)}
+            del bits
+        for gname, parts in groups:
+            ranges = [shard.row_range(R, rank, world) for _, R, _ in parts]
+            if all(r1 <= r0 for r0, r1 in ranges):
+                base[(gname, v)] = None
+            elif len(parts) == 1:
+                base[(gname, v)] = swap.to_device_radix(packs[parts[0][0]], device, *ranges[0])
+            else:
+                base[(gname, v)] = swap.to_device_radix_fused([packs[n] for n, _, _ in parts], device, ranges)
+        del packs
+    log(f"packed {len(stats)} distinct tensors into {len(base)} launch groups in {time.time() - t0:.1f}s")
     layers = []
     for layer in range(spec["layers"]):
         row = []
-        for name, R, C in spec["linears"]:
-            rt = base[(R, C, layer % variants)]
+        for gname, _ in groups:
+            rt = base[(gname, layer % variants)]
             if rt is not None and layer >= variants:
                 rt = dict(rt, rx_handle=rt["rx_handle"].clone())
             row.append(rt)
@@ -177,14 +196,16 @@ def build_stack(wl, rank, world, device, variants, log):
 # ------------------------------------------------------------------- step --
 
 class Chain:
-    """One decode token's linear stack with static buffers, for graph capture."""
+    """One decode token's linear stack with static buffers, for graph capture:
+    per layer, one launch per group (q|k|v, o, gate|up, down when fused)."""
 
-    def __init__(self, wl, layers, rank, world, device, head_weight=None):
+    def __init__(self, wl, layers, rank, world, device, head_weight=None, fuse=True):
         import torch
 
         from drinkme_b200 import shard
 
         self.spec = WORKLOADS[wl]
+        self.groups = groups_of(wl, fuse)
         self.layers = layers
         self.world = world
         self.device = device
@@ -192,28 +213,29 @@ class Chain:
         g = torch.Generator(device=device).manual_seed(12345)
         self.x_hidden = torch.randn((1, hidden), generator=g, device=device).to(torch.bfloat16)
         self.x_other = {}
-        for name, R, C in self.spec["linears"]:
+        for _, parts in self.groups:
+            name, R, C = parts[0]
             if name not in HIDDEN_INPUT and C not in self.x_other:
                 self.x_other[C] = torch.randn((1, C), generator=g, device=device).to(torch.bfloat16)
-        self.outs = []
-        self.fulls = []
-        self.works = []
+        # per group: the gather slot of one rank (sum of the parts' largest shards)
+        self.slot = [sum(shard.shard_rows_padded(R, world) for _, R, _ in parts) for _, parts in self.groups]
+        self.outs, self.works = [], []
         for row in layers:
-            o, f, w = [], [], []
-            for (name, R, C), rt in zip(self.spec["linears"], row):
+            o, w = [], []
+            for gi, rt in enumerate(row):
                 rows = 0 if rt is None else rt["R"]
-                o.append(torch.empty((1, rows), dtype=torch.bfloat16, device=device))
-                per = shard.shard_rows_padded(R, world)
-                w.append(torch.empty((world, 1, per), dtype=torch.bfloat16, device=device) if world > 1 else None)
-                f.append(None)
+                o.append(torch.zeros((1, self.slot[gi] if world > 1 else rows), dtype=torch.bfloat16,
+                                     device=device))
+                w.append(torch.empty((world, 1, self.slot[gi]), dtype=torch.bfloat16, device=device)
+                         if world > 1 else None)
             self.outs.append(o)
             self.works.append(w)
-            self.fulls.append(f)
         self.head = head_weight
         self.head_out = None
         self.last = None
 
-    def inputs(self, name, C):
+    def inputs(self, gi):
+        name, _, C = self.groups[gi][1][0]
         return self.x_hidden if name in HIDDEN_INPUT else self.x_other[C]
 
     def launches_per_step(self):
@@ -221,17 +243,23 @@ class Chain:
         return n + (1 if self.head is not None else 0)
 
     def step(self):
+        """Every group's GEMV of every layer; with N ranks each output slice
+        is all-gathered (rank-major: the consumer of q|k|v or gate|up reads
+        rank k's rows of each part at a fixed offset of slot k)."""
         import torch
+        import torch.distributed as dist
 
-        from drinkme_b200 import radix_ops, shard
+        from drinkme_b200 import radix_ops
 
         for li, row in enumerate(self.layers):
-            for j, ((name, R, C), rt) in enumerate(zip(self.spec["linears"], row)):
-                out = self.outs[li][j]
+            for gi, rt in enumerate(row):
+                out = self.outs[li][gi]
                 if rt is not None:
-                    radix_ops.gemv_into(rt, self.inputs(name, C), None, out)
+                    radix_ops.gemv_into(rt, self.inputs(gi), None, out[:, :rt["R"]])
                 if self.world > 1:
-                    self.last = shard.gather_rows(out, R, self.world, work=self.works[li][j])
+                    work = self.works[li][gi]
+                    dist.all_gather_into_tensor(work.view(self.world, self.slot[gi]), out.view(-1))
+                    self.last = work
                 else:
                     self.last = out
         if self.head is not None:
@@ -309,15 +337,16 @@ def kernel_times(chain, device, reps=3):
     out = {}
     tot_bytes = tot_ms = 0.0
     launches = 0
-    for j, (name, R, C) in enumerate(chain.spec["linears"]):
+    for j, (name, parts) in enumerate(chain.groups):
         items = [(li, row[j]) for li, row in enumerate(chain.layers) if row[j] is not None]
         if not items:
             continue
-        x = chain.inputs(name, C)
+        R, C = sum(p[1] for p in parts), parts[0][2]
+        x = chain.inputs(j)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for li, rt in items:
-                radix_ops.gemv_into(rt, x, None, chain.outs[li][j])
+                radix_ops.gemv_into(rt, x, None, chain.outs[li][j][:, :rt["R"]])
         g.replay()
         torch.cuda.synchronize(device)
         a = torch.cuda.Event(enable_timing=True)
@@ -388,6 +417,7 @@ def cpu_reference_sample(wl, budget_s=20.0, layers_sample=1):
     from oracle import oracle
 
     spec = WORKLOADS[wl]
+    torch.set_num_threads(os.cpu_count() or 1)  # every host thread, also under torchrun
     kind = "reference" if oracle.reference_native() is not None else "port"
     ws, xs = [], {}
     cold = 0.0
@@ -432,7 +462,8 @@ def main():
         for wl in WORKLOADS.values():
             wl["layers"] = a.layers
     spec = WORKLOADS[a.workload]
-    base_config = {"workload": f"{a.workload} decode linear stack, batch 1, sip, row-sharded over {world} GPU(s)",
+    base_config = {"workload": f"{a.workload} decode linear stack, batch 1, sip, row-sharded over {world} GPU(s)"
+                               + ("" if a.no_fuse else "; q|k|v and gate|up fused launches"),
                    "model_shape": a.workload, "layers": spec["layers"], "global_batch": 1,
                    "parallelism": f"rows{world}", "l2": "inputs larger than L2 (stack >> 126 MB)"}
 
@@ -467,8 +498,9 @@ def main():
         if rank == 0:
             print(f"[bench] {msg}", file=sys.stderr, flush=True)
 
-    layers, stats = build_stack(a.workload, rank, world, device, a.variants, log)
-    chain = Chain(a.workload, layers, rank, world, device)
+    fuse = not a.no_fuse
+    layers, stats = build_stack(a.workload, rank, world, device, a.variants, log, fuse)
+    chain = Chain(a.workload, layers, rank, world, device, fuse=fuse)
     clocks = ClockSampler(local)
     clocks.start()
     ms, _ = time_graph(chain, a.steps, a.warmup, world, rank, device)
@@ -520,10 +552,10 @@ def main():
         if not a.no_secondary and a.workload != "qwen3-8b":
             del chain, layers
             torch.cuda.empty_cache()
-            l8, _ = build_stack("qwen3-8b", 0, 1, device, a.variants, log)
+            l8, _ = build_stack("qwen3-8b", 0, 1, device, a.variants, log, fuse)
             g = torch.Generator(device=device).manual_seed(3)
             head = (torch.randn(WORKLOADS["qwen3-8b"]["head"], generator=g, device=device) * 0.02).to(torch.bfloat16)
-            c8 = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head)
+            c8 = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head, fuse=fuse)
             ms8, _ = time_graph(c8, a.steps, a.warmup, 1, 0, device)
             pk8, b8, t8, _ = kernel_times(c8, device)
             result["qwen3_8b_chain"] = {"config": "BASELINE configs[1]: 36 layers + raw lm_head 151936x4096",

@@ -15,7 +15,7 @@ DM_OK, DM_EINVAL, DM_ECUDA, DM_EDEVICE, DM_ENOMEM = 0, 1, 2, 3, 4
 DM_BF16, DM_F32 = 0, 1
 DM_MC_MAX = 8
 
-EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
+EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
            "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check")
 
@@ -35,6 +35,14 @@ class TensorInfo(ct.Structure):
                 ("resident_bytes", ct.c_int64), ("fast_path", ct.c_int32), ("device", ct.c_int32)]
 
 
+class PackPart(ct.Structure):
+    """dm_pack_part: one pack (or row range of one) of a fused tensor."""
+    _fields_ = [("host_palette", ct.c_void_p), ("npalette", ct.c_size_t), ("host_offsets", ct.c_void_p),
+                ("noffsets", ct.c_size_t), ("host_data", ct.c_void_p), ("nwords", ct.c_size_t),
+                ("R", ct.c_int64), ("C", ct.c_int64), ("host_widths", ct.c_void_p), ("nwidths", ct.c_int32),
+                ("block_size", ct.c_int32), ("row_begin", ct.c_int64), ("row_end", ct.c_int64)]
+
+
 _LIB = None
 
 
@@ -50,6 +58,7 @@ def lib():
         cp = ct.c_char_p
         L.dm_version.argtypes = []
         L.dm_tensor_create.argtypes = [p, sz, p, sz, p, sz, i64, i64, p, i32, i32, i64, i64, i32, ct.POINTER(p), cp, sz]
+        L.dm_tensor_create_multi.argtypes = [ct.POINTER(PackPart), i32, i32, ct.POINTER(p), cp, sz]
         L.dm_tensor_clone.argtypes = [p, ct.POINTER(p), cp, sz]
         L.dm_tensor_destroy.argtypes = [p]
         L.dm_tensor_get_info.argtypes = [p, ct.POINTER(TensorInfo)]

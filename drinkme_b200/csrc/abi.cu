@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "dm_internal.h"
 
@@ -60,23 +61,16 @@ void free_tensor(dm_tensor *t) {
 
 extern "C" int dm_version(void) { return 100; }
 
-extern "C" int dm_tensor_create(const uint8_t *palette, size_t npalette, const uint32_t *offsets, size_t noffsets,
-                                const uint32_t *data, size_t nwords, int64_t R, int64_t C, const int32_t *widths,
-                                int32_t nwidths, int32_t block_size, int64_t row_begin, int64_t row_end,
-                                int32_t device, dm_tensor **out, char *err, size_t err_len) {
-    if (!out || !offsets || !data || !widths || (!palette && npalette))
-        return fail(err, err_len, DM_EINVAL, "dm_tensor_create: null pointer");
-    *out = nullptr;
+namespace {
+
+// Lays `parts` out, copies the layout to `device` and sizes the scratch.
+int create_from_parts(const dm::PackPart *parts, int nparts, int32_t device, dm_tensor **out, char *err,
+                      size_t err_len) {
     std::string msg;
-    if (nwidths < 2 || nwidths > 8)
-        return fail(err, err_len, DM_EINVAL, "radix needs 2..8 widths in 1..8, ending with the exponent width");
-    if (dm::validate_pack(palette, npalette, offsets, noffsets, nwords, R, C, widths, nwidths, block_size, msg))
-        return fail(err, err_len, DM_EINVAL, msg);
     dm_tensor *t = new dm_tensor();
     t->device = device;
     std::string bytes, unit16;
-    if (dm::build_layout(palette, npalette, offsets, data, nwords, R, C, widths, nwidths, block_size, row_begin,
-                         row_end, t->L, bytes, unit16, msg)) {
+    if (dm::build_layout(parts, nparts, t->L, bytes, unit16, msg)) {
         delete t;
         return fail(err, err_len, DM_EINVAL, msg);
     }
@@ -119,6 +113,51 @@ extern "C" int dm_tensor_create(const uint8_t *palette, size_t npalette, const u
     }
     *out = t;
     return DM_OK;
+}
+
+int check_part(const dm_pack_part &p, const char *who, char *err, size_t err_len) {
+    if (!p.host_offsets || !p.host_data || !p.host_widths || (!p.host_palette && p.npalette))
+        return fail(err, err_len, DM_EINVAL, std::string(who) + ": null pointer");
+    if (p.nwidths < 2 || p.nwidths > 8)
+        return fail(err, err_len, DM_EINVAL, "radix needs 2..8 widths in 1..8, ending with the exponent width");
+    std::string msg;
+    if (dm::validate_pack(p.host_palette, p.npalette, p.host_offsets, p.noffsets, p.nwords, p.R, p.C, p.host_widths,
+                          p.nwidths, p.block_size, msg))
+        return fail(err, err_len, DM_EINVAL, msg);
+    return DM_OK;
+}
+
+dm::PackPart to_part(const dm_pack_part &p) {
+    return dm::PackPart{p.host_palette, p.npalette, p.host_offsets, p.noffsets, p.host_data, p.nwords, p.R, p.C,
+                        p.host_widths, p.nwidths, p.block_size, p.row_begin, p.row_end};
+}
+
+}  // namespace
+
+extern "C" int dm_tensor_create(const uint8_t *palette, size_t npalette, const uint32_t *offsets, size_t noffsets,
+                                const uint32_t *data, size_t nwords, int64_t R, int64_t C, const int32_t *widths,
+                                int32_t nwidths, int32_t block_size, int64_t row_begin, int64_t row_end,
+                                int32_t device, dm_tensor **out, char *err, size_t err_len) {
+    if (!out) return fail(err, err_len, DM_EINVAL, "dm_tensor_create: null pointer");
+    *out = nullptr;
+    const dm_pack_part p{palette, npalette, offsets, noffsets, data, nwords, R, C, widths, nwidths, block_size,
+                         row_begin, row_end};
+    if (int rc = check_part(p, "dm_tensor_create", err, err_len)) return rc;
+    const dm::PackPart part = to_part(p);
+    return create_from_parts(&part, 1, device, out, err, err_len);
+}
+
+extern "C" int dm_tensor_create_multi(const dm_pack_part *parts, int32_t nparts, int32_t device, dm_tensor **out,
+                                      char *err, size_t err_len) {
+    if (!out || !parts) return fail(err, err_len, DM_EINVAL, "dm_tensor_create_multi: null pointer");
+    *out = nullptr;
+    if (nparts < 1 || nparts > 64) return fail(err, err_len, DM_EINVAL, "dm_tensor_create_multi: 1..64 parts");
+    std::vector<dm::PackPart> ps;
+    for (int i = 0; i < nparts; ++i) {
+        if (int rc = check_part(parts[i], "dm_tensor_create_multi", err, err_len)) return rc;
+        ps.push_back(to_part(parts[i]));
+    }
+    return create_from_parts(ps.data(), nparts, device, out, err, err_len);
 }
 
 extern "C" int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err, size_t err_len) {
@@ -215,6 +254,8 @@ extern "C" int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64
                                              stream, msg);
             }
         }
+    } else if (t->L.nparts > 1) {
+        return fail(err, err_len, DM_EINVAL, "dm_gemv: a fused tensor needs 16-byte aligned activations");
     } else {
         rc = dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);
     }
@@ -226,7 +267,7 @@ extern "C" int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *
     if (!t || !out) return fail(err, err_len, DM_EINVAL, "dm_decode: null pointer");
     DeviceGuard g(t->device);
     std::string msg;
-    int rc = dm::launch_decode_generic(t, out, stream, msg);
+    int rc = t->L.fast_sip ? dm::launch_decode_sip(t, out, stream, msg) : dm::launch_decode_generic(t, out, stream, msg);
     if (rc) dm::set_error(err, err_len, msg);
     return rc;
 }

@@ -16,8 +16,8 @@ namespace dm {
 // operand, the activations its n = 8 B operand).
 constexpr int kUnitRows = 16;
 // Bytes of a unit's header: per row slot {u16 off16, u16 nesc, u16 sched,
-// u16 words}.
-constexpr int kUnitHeader = kUnitRows * 8;
+// u16 words}, then the sip exponent tables of the unit's part (4 words).
+constexpr int kUnitHeader = kUnitRows * 8 + 16;
 // Activations staged per unit: one 1024-weight block column of every
 // virtual activation row, row stride 2048 + 16 bytes (an odd number of
 // 16-byte slots, so the 8-lane phases of the B-fragment loads do not
@@ -33,8 +33,23 @@ struct RowEntry {
 };
 static_assert(sizeof(RowEntry) == 8, "row entry is 8 bytes");
 
+// One pack (or row shard of a pack) of a tensor: host arrays and shape.
+struct PackPart {
+    const uint8_t *palette;
+    size_t npal;
+    const uint32_t *offsets;
+    size_t noff;
+    const uint32_t *data;
+    size_t nwords;
+    int64_t R, C;
+    const int32_t *widths;
+    int32_t nw, B;
+    int64_t row0, row1;
+};
+
 struct TensorLayout {
     int64_t R = 0, C = 0, row0 = 0, rows = 0;
+    int32_t nparts = 1;
     int32_t B = 0, nw = 0, widths[8] = {0};
     int32_t covered = 0;
     uint8_t palette[256] = {0};
@@ -79,10 +94,9 @@ void set_error(char *err, size_t len, const std::string &msg);
 // Host layout (layout.cpp)
 int validate_pack(const uint8_t *palette, size_t npal, const uint32_t *offsets, size_t noff, size_t nwords,
                   int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, std::string &msg);
-int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, const uint32_t *data,
-                 size_t nwords, int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B,
-                 int64_t row0, int64_t row1, TensorLayout &L, std::string &bytes, std::string &unit16,
+int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string &bytes, std::string &unit16,
                  std::string &msg);
+int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
 int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw);
 
 // Kernel launchers (kernels.cu)
@@ -97,7 +111,7 @@ int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t 
                             void *stream, std::string &msg);
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg);
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spg, int *ng, int dir_cap);
+int sip_shared_bytes(const dm_tensor *t, int Mv, int nl, int *slot_bytes, int *spg, int *ng, int dir_cap);
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg);

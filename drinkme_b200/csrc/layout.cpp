@@ -7,7 +7,8 @@
 // words into UNITS of 16 rows x 1 block column, each unit contiguous and
 // 16-byte aligned so one bulk copy stages it into shared memory:
 //
-//   unit  = [16 x RowEntry header][row-block streams, each 16-byte aligned]
+//   unit  = [16 x RowEntry header][sip exponent tables, 16 bytes]
+//           [row-block streams, each 16-byte aligned]
 //           [sip fast path: per row, the escape index — the uint16 position
 //            of every tier-0 escape (code 7) in block order, 16-byte aligned]
 //           [sip fast path, ragged last tile only: one null block whose
@@ -15,6 +16,10 @@
 //   units in tile-major order (tile = 16 rows; all block columns of a tile
 //   before the next tile), then a zero tail pad as long as the widest block
 //   (radix.block_word_bounds(B)[1] words), so no reader leaves the buffer.
+//
+// A FUSED tensor concatenates the rows of several packs sharing their
+// columns (q, k and v; gate and up): each part keeps its own palette, whose
+// tables ride in the header of every unit of its tiles.
 #include <algorithm>
 #include <atomic>
 #include <cstring>
@@ -162,26 +167,70 @@ static uint16_t block_schedule(const uint32_t *blk, int64_t avail, int64_t n, co
 
 static inline int64_t a16(int64_t bytes) { return (bytes + 15) & ~int64_t(15); }
 
-int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, const uint32_t *data,
-                 size_t nwords, int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, int64_t row0,
-                 int64_t row1, TensorLayout &L, std::string &bytes, std::string &unit16, std::string &msg) {
-    if (row0 < 0 || row1 > R || row1 <= row0) { msg = "invalid row range"; return 1; }
+// The sip exponent tables of a part (the kernels' PRMT lookups): high part
+// p >> 1 with 0x80 at the escape code 7, low part (p & 1) << 7 with 0x7F at
+// code 7, each eight bytes as two words.
+static void sip_tables(const uint8_t *palette, uint32_t tab[4]) {
+    uint8_t th[8], tl[8];
+    for (int c = 0; c < 7; ++c) {
+        th[c] = (uint8_t)(palette[c] >> 1);
+        tl[c] = (uint8_t)((palette[c] & 1u) << 7);
+    }
+    th[7] = 0x80;  // escape marker: zeroes the sign in the high byte
+    tl[7] = 0x7F;  // escape: zeroes the mantissa in the low byte
+    tab[0] = th[0] | (th[1] << 8) | (th[2] << 16) | ((uint32_t)th[3] << 24);
+    tab[1] = th[4] | (th[5] << 8) | (th[6] << 16) | ((uint32_t)th[7] << 24);
+    tab[2] = tl[0] | (tl[1] << 8) | (tl[2] << 16) | ((uint32_t)tl[3] << 24);
+    tab[3] = tl[4] | (tl[5] << 8) | (tl[6] << 16) | ((uint32_t)tl[7] << 24);
+}
+
+int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string &bytes, std::string &unit16,
+                 std::string &msg) {
+    if (nparts < 1) { msg = "no tensor parts"; return 1; }
+    const PackPart &P0 = parts[0];
+    const int64_t C = P0.C;
+    const int32_t B = P0.B, nw = P0.nw;
+    const int32_t *widths = P0.widths;
+    for (int p = 0; p < nparts; ++p) {
+        const PackPart &P = parts[p];
+        if (P.row0 < 0 || P.row1 > P.R || P.row1 <= P.row0) { msg = "invalid row range"; return 1; }
+        if (P.C != C || P.B != B || P.nw != nw || std::memcmp(P.widths, widths, sizeof(int32_t) * nw) != 0) {
+            msg = "fused tensor parts must share columns, block size and tier widths";
+            return 1;
+        }
+    }
     L = TensorLayout();
-    L.R = R; L.C = C; L.row0 = row0; L.rows = row1 - row0; L.B = B; L.nw = nw;
+    L.C = C; L.B = B; L.nw = nw; L.nparts = nparts;
     for (int i = 0; i < nw; ++i) L.widths[i] = widths[i];
-    L.covered = (int32_t)npal;
-    std::memcpy(L.palette, palette, npal);
+    L.covered = (int32_t)P0.npal;
+    std::memcpy(L.palette, P0.palette, P0.npal);
     L.NB = (C + B - 1) / B;
+    L.fast_sip = nw == 2 && widths[0] == 3 && B == 1024 && C % 1024 == 0;
+    std::vector<int64_t> rowoff(nparts + 1, 0);
+    for (int p = 0; p < nparts; ++p) {
+        const int64_t n = parts[p].row1 - parts[p].row0;
+        if (nparts > 1 && p + 1 < nparts && n % kUnitRows != 0) {
+            msg = "fused tensor parts other than the last need a multiple of 16 rows";
+            return 1;
+        }
+        rowoff[p + 1] = rowoff[p] + n;
+    }
+    if (nparts > 1 && !L.fast_sip) {
+        msg = "fused tensors are served by the sip kernel: every part sip, 1024-weight blocks, rows of whole blocks";
+        return 1;
+    }
+    L.R = nparts == 1 ? P0.R : rowoff[nparts];
+    L.row0 = nparts == 1 ? P0.row0 : 0;
+    L.rows = rowoff[nparts];
     L.tiles = (L.rows + kUnitRows - 1) / kUnitRows;
     L.units = L.tiles * L.NB;
-    L.fast_sip = nw == 2 && widths[0] == 3 && B == 1024 && C % 1024 == 0;
-    {  // padded palette words (radix_pack.py:333-350)
+    {  // padded palette words of the first part (radix_pack.py:333-350)
         int32_t wpos = 0, base = 0;
         std::vector<uint8_t> t;
         for (int i = 0; i < nw - 1; ++i) {
             int32_t n = (1 << widths[i]) - 1, padded = ((n + 3) / 4) * 4;
             L.tier_table[i] = wpos;
-            for (int k = 0; k < padded; ++k) t.push_back(k < n ? palette[base + k] : 0);
+            for (int k = 0; k < padded; ++k) t.push_back(k < n ? P0.palette[base + k] : 0);
             base += n;
             wpos += padded / 4;
         }
@@ -189,20 +238,42 @@ int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, c
         if (wpos > 24) { msg = "radix palette tables too large for the device kernels"; return 1; }
         std::memcpy(L.pal_words, t.data(), t.size());
     }
-    const int64_t NB = L.NB, rows = L.rows;
-    const int64_t first_blk = row0 * NB, nblk = rows * NB;
-    L.payload_words = (int64_t)offsets[first_blk + nblk] - (int64_t)offsets[first_blk];
-    L.read_bytes = L.payload_words * 4 + (nblk + 1) * 4 + (int64_t)L.npal_words * 4 + (nw > 2 ? nblk * 2 : 0);
+    const int64_t NB = L.NB, rows = L.rows, nblk = rows * NB;
+    // global row -> (part, source block row)
+    std::vector<int32_t> rpart(rows);
+    std::vector<int64_t> rsrc(rows);
+    for (int p = 0; p < nparts; ++p)
+        for (int64_t r = rowoff[p]; r < rowoff[p + 1]; ++r) {
+            rpart[r] = p;
+            rsrc[r] = parts[p].row0 + (r - rowoff[p]);
+        }
+    for (int p = 0; p < nparts; ++p) {
+        const PackPart &P = parts[p];
+        const int64_t pb0 = P.row0 * NB, pnb = (P.row1 - P.row0) * NB;
+        const int64_t words = (int64_t)P.offsets[pb0 + pnb] - (int64_t)P.offsets[pb0];
+        L.payload_words += words;
+        L.read_bytes += words * 4 + (pnb + 1) * 4 + (int64_t)L.npal_words * 4 + (nw > 2 ? pnb * 2 : 0);
+    }
+    std::vector<uint32_t> tabs((size_t)nparts * 4, 0);
+    if (L.fast_sip)
+        for (int p = 0; p < nparts; ++p) sip_tables(parts[p].palette, &tabs[(size_t)p * 4]);
+    auto block_of = [&](int64_t i, const PackPart *&P, int64_t &gb) {
+        const int64_t r = i / NB, b = i % NB;
+        P = &parts[rpart[r]];
+        gb = rsrc[r] * NB + b;
+    };
 
     // pass 1: per block, escapes (fast path) and the schedule
     std::vector<uint16_t> nesc(nblk, 0), sched(nblk, 0);
     const bool fast = L.fast_sip;
     parallel_for(nblk, [&](int64_t i) {
-        int64_t gb = first_blk + i;
-        const uint32_t *blk = data + offsets[gb];
-        int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+        const PackPart *P;
+        int64_t gb;
+        block_of(i, P, gb);
+        const uint32_t *blk = P->data + P->offsets[gb];
+        int64_t words = (int64_t)P->offsets[gb + 1] - (int64_t)P->offsets[gb];
         int64_t n = std::min<int64_t>(B, C - (i % NB) * B);
-        sched[i] = block_schedule(blk, (int64_t)nwords - (int64_t)offsets[gb], n, widths, nw);
+        sched[i] = block_schedule(blk, (int64_t)P->nwords - (int64_t)P->offsets[gb], n, widths, nw);
         if (fast) {
             int e = sip_escapes(blk + 256, nullptr);
             // a block short of its terminal stream (validate cannot see it)
@@ -220,8 +291,11 @@ int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, c
         for (int s = 0; s < kUnitRows; ++s) {
             int64_t r = tile * kUnitRows + s;
             if (r >= rows) { absent = true; continue; }
-            int64_t i = r * NB + b, gb = first_blk + i;
-            int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+            const int64_t i = r * NB + b;
+            const PackPart *P;
+            int64_t gb;
+            block_of(i, P, gb);
+            int64_t words = (int64_t)P->offsets[gb + 1] - (int64_t)P->offsets[gb];
             sz += a16(words * 4);
             if (fast) sz += a16((int64_t)nesc[i] * 2);
         }
@@ -243,22 +317,29 @@ int build_layout(const uint8_t *palette, size_t npal, const uint32_t *offsets, c
         int64_t tile = u / NB, b = u % NB;
         char *base = out + ustart[u];
         RowEntry *hdr = reinterpret_cast<RowEntry *>(base);
+        if (fast) {
+            const int p = rpart[std::min<int64_t>(tile * kUnitRows, rows - 1)];
+            std::memcpy(base + kUnitRows * sizeof(RowEntry), &tabs[(size_t)p * 4], 16);
+        }
         int64_t at = kUnitHeader;
         int64_t null_at = -1;
         for (int s = 0; s < kUnitRows; ++s) {
             int64_t r = tile * kUnitRows + s;
             if (r >= rows) continue;
-            int64_t i = r * NB + b, gb = first_blk + i;
-            int64_t words = (int64_t)offsets[gb + 1] - (int64_t)offsets[gb];
+            const int64_t i = r * NB + b;
+            const PackPart *P;
+            int64_t gb;
+            block_of(i, P, gb);
+            int64_t words = (int64_t)P->offsets[gb + 1] - (int64_t)P->offsets[gb];
             hdr[s].off16 = (uint16_t)(at / 16);
             hdr[s].words = (uint16_t)words;
             hdr[s].sched = sched[i];
             hdr[s].nesc = nesc[i];
-            std::memcpy(base + at, data + offsets[gb], (size_t)words * 4);
+            std::memcpy(base + at, P->data + P->offsets[gb], (size_t)words * 4);
             at += a16(words * 4);
             if (fast) {
                 std::vector<uint16_t> pos(1024);
-                int e = sip_escapes(data + offsets[gb] + 256, pos.data());
+                int e = sip_escapes(P->data + P->offsets[gb] + 256, pos.data());
                 int keep = std::min<int>(e, nesc[i]);
                 std::memcpy(base + at, pos.data(), (size_t)keep * 2);
                 at += a16((int64_t)nesc[i] * 2);

@@ -97,6 +97,8 @@ extern "C" int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtyp
     const uint16_t *b16 = reinterpret_cast<const uint16_t *>(bias);
     const int of32 = out_dtype == DM_F32;
     const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (t->L.nparts > 1 && !aligned)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_noalloc: a fused tensor needs 16-byte aligned activations");
     if (!t->L.fast_sip || !aligned) {
         // the general kernel keeps its sums in registers: no scratch to place
         int rc = dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);

@@ -54,8 +54,7 @@ struct SipArgs {
     const uint8_t *data;
     const uint32_t *unit16;
     int64_t units, rows, NB;
-    uint32_t th0, th1, tl0, tl1;  // exponent lookup tables (high / low part)
-    const uint16_t *x;            // virtual activation rows [Mv][x_stride] bf16
+    const uint16_t *x;  // virtual activation rows [Mv][x_stride] bf16
     int64_t x_stride;
     int32_t Mv, nsplit, M_out;
     const uint16_t *bias;
@@ -65,6 +64,7 @@ struct SipArgs {
     int *counters;
     int *err;
     int32_t slot_bytes, x_off, spg, ng, workers, dir_cap;
+    int32_t nl, lpg;  // logical workers per CTA; per group (nl / ng)
 };
 
 // A WORKER is a group of kGroupWarps consumer warps sharing each staged unit:
@@ -190,8 +190,8 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
     float *gbuf = reinterpret_cast<float *>(empty + nslots);  // [ng][kGroupWarps][16][8] partials
     uint32_t *dir = reinterpret_cast<uint32_t *>(gbuf + a.ng * kGroupWarps * 128);  // this CTA's unit starts
     const int64_t U = a.units, W = a.workers, NB = a.NB;
-    const int64_t cta_u0 = range_start((int64_t)blockIdx.x * a.ng, U, W);
-    const int64_t cta_u1 = range_start((int64_t)(blockIdx.x + 1) * a.ng, U, W);
+    const int64_t cta_u0 = range_start((int64_t)blockIdx.x * a.nl, U, W);
+    const int64_t cta_u1 = range_start((int64_t)(blockIdx.x + 1) * a.nl, U, W);
     const bool dir_in_smem = (cta_u1 - cta_u0 + 1) <= a.dir_cap;
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
@@ -214,9 +214,9 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
             int32_t nu[kMaxGroups], eu[kMaxGroups], bc[kMaxGroups], si[kMaxGroups], fills[kMaxGroups];
 #pragma unroll
             for (int g = 0; g < kMaxGroups; ++g) {
-                const int64_t w = (int64_t)blockIdx.x * a.ng + g;
+                const int64_t w = (int64_t)blockIdx.x * a.nl + (int64_t)g * a.lpg;
                 nu[g] = g < a.ng ? (int32_t)range_start(w, U, W) : 0;
-                eu[g] = g < a.ng ? (int32_t)range_start(w + 1, U, W) : 0;
+                eu[g] = g < a.ng ? (int32_t)range_start(w + a.lpg, U, W) : 0;
                 bc[g] = (int32_t)(nu[g] % NB);
                 si[g] = 0;
                 fills[g] = 0;
@@ -298,10 +298,11 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
 
     // ------------------------------------------------------- consumers --
     const int gi = (warp - 1) / kGroupWarps, wi = (warp - 1) % kGroupWarps;
-    const int64_t w = (int64_t)blockIdx.x * a.ng + gi;
-    const int64_t u0 = range_start(w, U, W), u1 = range_start(w + 1, U, W);
+    // the group's units: its lpg logical workers' ranges, consecutive
+    int64_t w = (int64_t)blockIdx.x * a.nl + (int64_t)gi * a.lpg;
+    const int64_t gu0 = range_start(w, U, W), gu1 = range_start(w + a.lpg, U, W);
+    int64_t u0 = gu0, u1 = range_start(w + 1, U, W);  // the current logical worker's range
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t th0 = a.th0, th1 = a.th1, tl0 = a.tl0, tl1 = a.tl1;
     float *Pw = gbuf + (gi * kGroupWarps + wi) * 128;  // this warp's [16 rows][8 virtual rows]
     float *P0 = gbuf + (gi * kGroupWarps) * 128;       // the group's sum
 
@@ -311,8 +312,9 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
 #pragma unroll
     for (int v = 0; v < MV; ++v) cg[v] = cg8[v] = 0.f;
     int64_t tile = u0 / NB;
-    const int64_t first_tile = u0 / NB;
 
+    // tile tl of logical worker w (units [u0, u1)): the group's sums, then
+    // the tile's output, or this worker's partial of a tile it shares
     auto flush = [&](int64_t tl) {
 #pragma unroll
         for (int v = 0; v < MV; ++v) {
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
             if (whole) {
                 store_outputs(a, tl, P0);
             } else {
-                const int slot = (tl == first_tile) ? 0 : 1;
+                const int slot = (tl == u0 / NB) ? 0 : 1;
                 float *mine = a.partials + (w * 2 + slot) * 128;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) mine[lane + 32 * i] = s[i];
@@ -407,17 +409,27 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
     int sidx = 0;                       // slot of unit u within the group's ring
     uint32_t par = 0;                   // parity of that slot's current fill
     const int q0 = 4 * wi, j0 = 4 * wi + t;
-    for (int64_t u = u0; u < u1; ++u) {
+    for (int64_t u = gu0; u < gu1; ++u) {
         const int slot = gi * a.spg + sidx;
         if (!mbar_wait(&full[slot], par, a.err, kErrWaitFull)) {
             ok = false;
             break;
         }
-        if (bcol == 0 && u != u0) {
+        if (u == u1) {
+            // the next logical worker's range begins (never empty: W <= U)
+            flush(tile);
+            w += 1;
+            u0 = u1;
+            u1 = range_start(w + 1, U, W);
+            if (bcol == 0) tile += 1;
+        } else if (bcol == 0 && u != u0) {
             flush(tile);
             tile += 1;
         }
         const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
+        // the exponent tables of the unit's part (high part th0/th1, low tl0/tl1)
+        const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
+        const uint32_t th0 = tab.x, th1 = tab.y, tl0 = tab.z, tl1 = tab.w;
         const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
         const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
         const uint8_t *lit0 = base + (size_t)e0.off16 * 16;
@@ -451,17 +463,20 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
             par ^= 1u;
         }
     }
-    if (ok && u1 > u0) flush(tile);
+    if (ok && gu1 > gu0) flush(tile);
 }
 
-// Shared-memory plan for a launch: slot size, slots per group, groups.
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spg, int *ng, int dir_cap) {
+// Shared-memory plan for a launch: slot size, slots per group and groups,
+// the groups a divisor of the nl logical workers per CTA (so the work split,
+// and with it every sum's order, does not depend on Mv).
+int sip_shared_bytes(const dm_tensor *t, int Mv, int nl, int *slot_bytes, int *spg, int *ng, int dir_cap) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
     const int sb = unit + Mv * kXRowStride;
     const int budget = 227 * 1024;
     const int fixed = kMaxGroups * kGroupWarps * 128 * 4 + (dir_cap + 1) * 4 + 256;
-    const int plans[][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 3}, {2, 2}, {1, 3}, {1, 2}};
+    const int plans[][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 4}, {2, 3}, {2, 2}, {1, 4}, {1, 3}, {1, 2}};
     for (const auto &pl : plans) {
+        if (pl[0] > nl || nl % pl[0] != 0) continue;
         int need = pl[0] * pl[1] * (sb + 16) + fixed;
         if (need <= budget) {
             *slot_bytes = sb;
@@ -475,104 +490,24 @@ int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *spg, int 
 
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                     const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg) {
-    const dm::TensorLayout &L = t->L;
-    int slot_bytes = 0, spg = 0, ng = 0;
-    // one CTA per SM; each worker (a group of warps) owns at least one unit
-    const int64_t grid0 = std::min<int64_t>(t->sms, L.units);
-    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid0 - 1) / grid0 + 2);
-    int smem = sip_shared_bytes(t, Mv, &slot_bytes, &spg, &ng, dir_cap);
-    if (smem < 0) {
-        msg = "sip kernel: a unit does not fit in shared memory";
-        return DM_EINVAL;
-    }
-    using Kern = void (*)(SipArgs);
-    static const Kern kernels[kMaxVirtualRows] = {sip_gemv_kernel<1>, sip_gemv_kernel<2>, sip_gemv_kernel<3>,
-                                                  sip_gemv_kernel<4>, sip_gemv_kernel<5>, sip_gemv_kernel<6>,
-                                                  sip_gemv_kernel<7>, sip_gemv_kernel<8>};
-    static bool attr_set[kMaxVirtualRows] = {false};
-    if (Mv < 1 || Mv > kMaxVirtualRows) {
-        msg = "sip kernel: 1..8 virtual activation rows";
-        return DM_EINVAL;
-    }
-    const Kern kern = kernels[Mv - 1];
-    if (!attr_set[Mv - 1]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) {
-            msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-            return DM_ECUDA;
-        }
-        attr_set[Mv - 1] = true;
-    }
-    int64_t grid = grid0;
-    if (L.units < (int64_t)t->sms * ng) ng = (int)std::max<int64_t>(1, std::min<int64_t>(ng, L.units / grid));
-    const int64_t workers = grid * ng;
-    if (workers > t->S.max_workers) {
-        msg = "sip kernel: scratch sized for fewer workers";
-        return DM_EINVAL;
-    }
-    SipArgs a{};
-    a.data = t->d_data;
-    a.unit16 = t->d_unit16;
-    a.units = L.units;
-    a.rows = L.rows;
-    a.NB = L.NB;
-    uint8_t th[8], tl[8];
-    for (int c = 0; c < 7; ++c) {
-        th[c] = (uint8_t)(L.palette[c] >> 1);
-        tl[c] = (uint8_t)((L.palette[c] & 1u) << 7);
-    }
-    th[7] = 0x80;  // escape marker: zeroes the sign in the high byte
-    tl[7] = 0x7F;  // escape: zeroes the mantissa in the low byte
-    a.th0 = th[0] | (th[1] << 8) | (th[2] << 16) | ((uint32_t)th[3] << 24);
-    a.th1 = th[4] | (th[5] << 8) | (th[6] << 16) | ((uint32_t)th[7] << 24);
-    a.tl0 = tl[0] | (tl[1] << 8) | (tl[2] << 16) | ((uint32_t)tl[3] << 24);
-    a.tl1 = tl[4] | (tl[5] << 8) | (tl[6] << 16) | ((uint32_t)tl[7] << 24);
-    a.x = xv;
-    a.x_stride = x_stride;
-    a.Mv = Mv;
-    a.nsplit = nsplit;
-    a.M_out = M_out;
-    a.bias = bias;
-    a.out = out;
-    a.out_f32 = out_f32;
-    a.partials = t->S.partials;
-    a.counters = t->S.counters;
-    a.err = t->S.err;
-    a.slot_bytes = slot_bytes;
-    a.x_off = (t->L.max_unit_bytes + 127) & ~127;
-    a.spg = spg;
-    a.ng = ng;
-    a.workers = (int32_t)workers;
-    a.dir_cap = dir_cap;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(32 * (1 + ng * kGroupWarps));
-    cfg.dynamicSmemBytes = (size_t)smem;
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
-    if (e != cudaSuccess) {
-        msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
-        return DM_ECUDA;
-    }
-    return DM_OK;
+    return launch_gemv_sip_with(t, xv, x_stride, Mv, nsplit, M_out, bias, out, out_f32, t->S.partials,
+                                t->S.counters, t->S.err, t->S.max_workers, stream, msg);
 }
 
-// The same launch with caller-supplied scratch (partials for `max_workers`
-// workers, per-tile counters that are zero on entry, the error word): the
-// variant behind dm_gemv_noalloc, whose scratch is a static device array.
+// The launch with caller-supplied scratch (partials for `max_workers`
+// workers, per-tile counters that are zero on entry, the error word):
+// dm_gemv passes the tensor's own, dm_gemv_noalloc a static device array.
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg) {
     const dm::TensorLayout &L = t->L;
     int slot_bytes = 0, spg = 0, ng = 0;
+    // one CTA per SM and nl logical workers per CTA, each owning at least one
+    // unit: the split depends on the tensor alone
     const int64_t grid0 = std::min<int64_t>(t->sms, L.units);
+    const int nl = (int)std::min<int64_t>(kMaxGroups, L.units / grid0);
     const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid0 - 1) / grid0 + 2);
-    int smem = sip_shared_bytes(t, Mv, &slot_bytes, &spg, &ng, dir_cap);
+    int smem = sip_shared_bytes(t, Mv, nl, &slot_bytes, &spg, &ng, dir_cap);
     if (smem < 0) {
         msg = "sip kernel: a unit does not fit in shared memory";
         return DM_EINVAL;
@@ -596,8 +531,7 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         attr_set[Mv - 1] = true;
     }
     const int64_t grid = grid0;
-    if (L.units < (int64_t)t->sms * ng) ng = (int)std::max<int64_t>(1, std::min<int64_t>(ng, L.units / grid));
-    const int64_t workers = grid * ng;
+    const int64_t workers = grid * nl;
     if (workers > max_workers) {
         msg = "sip kernel: " + std::to_string(workers) + " stream-K workers exceed the scratch's " +
               std::to_string(max_workers);
@@ -609,17 +543,6 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.units = L.units;
     a.rows = L.rows;
     a.NB = L.NB;
-    uint8_t th[8], tl[8];
-    for (int c = 0; c < 7; ++c) {
-        th[c] = (uint8_t)(L.palette[c] >> 1);
-        tl[c] = (uint8_t)((L.palette[c] & 1u) << 7);
-    }
-    th[7] = 0x80;
-    tl[7] = 0x7F;
-    a.th0 = th[0] | (th[1] << 8) | (th[2] << 16) | ((uint32_t)th[3] << 24);
-    a.th1 = th[4] | (th[5] << 8) | (th[6] << 16) | ((uint32_t)th[7] << 24);
-    a.tl0 = tl[0] | (tl[1] << 8) | (tl[2] << 16) | ((uint32_t)tl[3] << 24);
-    a.tl1 = tl[4] | (tl[5] << 8) | (tl[6] << 16) | ((uint32_t)tl[7] << 24);
     a.x = xv;
     a.x_stride = x_stride;
     a.Mv = Mv;
@@ -637,6 +560,8 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.ng = ng;
     a.workers = (int32_t)workers;
     a.dir_cap = dir_cap;
+    a.nl = nl;
+    a.lpg = nl / ng;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(32 * (1 + ng * kGroupWarps));
@@ -650,6 +575,87 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {
         msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
+        return DM_ECUDA;
+    }
+    return DM_OK;
+}
+
+// ---------------------------------------------------------------- decode --
+// Dense decode of a sip tensor into bf16 bits [rows][C]: one CTA per unit
+// (16 rows x one 1024-weight block column), 256 threads. Thread (row s,
+// chunk c) decodes weights [64c, 64c + 64) of row s: 64 literal bytes and 64
+// tier-0 codes (six whole words) through the same PRMT tables as the GEMV,
+// into shared memory; the escapes then take their terminal exponents; the
+// tile leaves in 16-byte stores. An escape without a terminal byte inside
+// its block (a malformed block the loader clipped) stays +0, as in the GEMV.
+__global__ void __launch_bounds__(256) sip_decode_kernel(const uint8_t *__restrict__ data,
+                                                          const uint32_t *__restrict__ unit16, int64_t NB,
+                                                          int64_t rows, int64_t C, uint16_t *__restrict__ out) {
+    __shared__ __align__(16) uint16_t tileb[kUnitRows][1024 + 8];
+    const int64_t u = blockIdx.x;
+    const int64_t tile = u / NB, bcol = u % NB;
+    const uint8_t *base = data + (size_t)unit16[u] * 16;
+    const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
+    const int s = threadIdx.x >> 4, c = threadIdx.x & 15;
+    const RowEntry e = reinterpret_cast<const RowEntry *>(base)[s];
+    const uint8_t *lit = base + (size_t)e.off16 * 16;
+    const uint32_t *t0 = reinterpret_cast<const uint32_t *>(lit + 1024) + 6 * c;
+    uint32_t w[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) w[k] = t0[k];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 16 weights: 48 code bits from bit 48q
+        const uint4 Lq = *reinterpret_cast<const uint4 *>(lit + 64 * c + 16 * q);
+        const int b0 = 48 * q;
+        const uint32_t lo32 = __funnelshift_r(w[b0 >> 5], w[(b0 >> 5) + 1], b0 & 31);
+        const uint32_t hi = w[(b0 >> 5) + 1] >> (b0 & 31);
+        const uint32_t xa = spread_codes(lo32 & 0x00FFFFFFu);
+        const uint32_t xb = spread_codes(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
+        uint32_t p[8];
+        decode4(Lq.x, xa, tab.x, tab.y, tab.z, tab.w, p[0], p[1]);
+        decode4(Lq.y, xa >> 16, tab.x, tab.y, tab.z, tab.w, p[2], p[3]);
+        decode4(Lq.z, xb, tab.x, tab.y, tab.z, tab.w, p[4], p[5]);
+        decode4(Lq.w, xb >> 16, tab.x, tab.y, tab.z, tab.w, p[6], p[7]);
+        uint4 *dst = reinterpret_cast<uint4 *>(&tileb[s][64 * c + 16 * q]);
+        dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+        dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+    }
+    __syncthreads();
+    {  // escapes of row s: chunk c takes every 16th
+        const uint8_t *term = lit + 1408;
+        const uint16_t *idx = reinterpret_cast<const uint16_t *>(lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
+        for (int j = c; j < (int)e.nesc; j += 16) {
+            const uint32_t pos = idx[j] & 1023u;
+            const uint32_t lb = lit[pos];
+            tileb[s][pos] = (uint16_t)(((lb & 0x80u) << 8) | ((uint32_t)term[j] << 7) | (lb & 0x7Fu));
+        }
+    }
+    __syncthreads();
+    const int64_t c0 = bcol * 1024;
+    for (int i = threadIdx.x; i < kUnitRows * 128; i += 256) {
+        const int r = i >> 7, k = (i & 127) * 8;
+        const int64_t row = tile * kUnitRows + r;
+        if (row >= rows) continue;
+        *reinterpret_cast<uint4 *>(out + row * C + c0 + k) = *reinterpret_cast<const uint4 *>(&tileb[r][k]);
+    }
+}
+
+int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg) {
+    const TensorLayout &L = t->L;
+    if (!L.fast_sip) {
+        msg = "sip decode: not a sip tensor";
+        return DM_EINVAL;
+    }
+    if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) {
+        msg = "dm_decode: output of a sip tensor must be 16-byte aligned";
+        return DM_EINVAL;
+    }
+    if (L.units == 0) return DM_OK;
+    sip_decode_kernel<<<(unsigned)L.units, 256, 0, (cudaStream_t)stream>>>(t->d_data, t->d_unit16, L.NB, L.rows, L.C,
+                                                                          out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        msg = std::string("sip_decode_kernel: ") + cudaGetErrorString(e);
         return DM_ECUDA;
     }
     return DM_OK;

@@ -85,6 +85,41 @@ def to_device_radix(pack: dict, device="cuda", row_begin: int = 0, row_end: int 
     }
 
 
+def to_device_radix_fused(packs, device="cuda", ranges=None) -> dict:
+    """Several sip radix tensors reading the same activations (q, k, v;
+    gate, up) -> ONE runtime dict whose GEMV computes their outputs side by
+    side, [M, sum of rows] (dm_tensor_create_multi). `ranges` optionally
+    gives each pack's (row_begin, row_end) — a rank's row shard of each.
+    The dict serves every radix_ops GEMV arm; `split_fused` cuts an output
+    into the parts' views. No reference counterpart: the reference runs one
+    RadixCompressedLinear per projection (swap.py:395-456)."""
+    dev = _cuda_device(device)
+    packs = list(packs)
+    if not packs:
+        raise ValueError("to_device_radix_fused: no tensors")
+    ranges = [(int(a), int(pk["R"]) if b is None else int(b))
+              for pk, (a, b) in zip(packs, ranges or [(0, None)] * len(packs))]
+    h = RadixTensor.fused(packs, dev, ranges)
+    C = int(packs[0]["C"])
+    B = int(packs[0]["block_size"])
+    widths = tuple(int(w) for w in packs[0]["widths"])
+    rows = int(h.info.rows)
+    return {
+        "rx_handle": h,
+        "rx_schedule": torch.empty(0, dtype=torch.uint16, device=dev),
+        "rx_launch": select_launch(rows, C, B, widths).as_dict(),
+        "NW": int(h.info.payload_words),
+        "R": rows, "C": C, "R_full": rows, "row_begin": 0, "widths": widths, "block_size": B,
+        "NBK": int(h.info.nblocks), "codec": "radix", "format_version": codec.FORMAT_VERSION, "layout": 0,
+        "fused_rows": tuple(b - a for a, b in ranges),
+    }
+
+
+def split_fused(runtime: dict, y: torch.Tensor):
+    """The parts' outputs of a fused GEMV result [M, sum of rows], as views."""
+    return torch.split(y, list(runtime["fused_rows"]), dim=-1)
+
+
 def resident_bytes(runtime: dict) -> int:
     """Device bytes a runtime dict holds (pack.resident_bytes, pack.py:1170)."""
     n = sum(v.numel() * v.element_size() for v in runtime.values() if torch.is_tensor(v))

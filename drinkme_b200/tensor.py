@@ -10,6 +10,32 @@ import torch
 from . import _lib
 
 
+def _cuda(device) -> torch.device:
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError(f"drinkme_b200 serves CUDA devices only, not {dev}")
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
+def _part(pack: dict, row_begin, row_end):
+    """A dm_pack_part over a pack's host arrays, and the arrays to keep alive
+    until the library has copied them."""
+    pal = np.ascontiguousarray(pack["rx_palette"], dtype=np.uint8)
+    off = np.ascontiguousarray(pack["rx_offsets"], dtype=np.uint32)
+    data = np.ascontiguousarray(pack["rx_data"], dtype=np.uint32)
+    if "NW" in pack:
+        data = data[: int(pack["NW"])]
+    widths = [int(w) for w in pack["widths"]]
+    R, C = int(pack["R"]), int(pack["C"])
+    w = (ct.c_int32 * len(widths))(*widths)
+    part = _lib.PackPart(pal.ctypes.data, pal.size, off.ctypes.data, off.size, data.ctypes.data, data.size, R, C,
+                         ct.cast(w, ct.c_void_p), len(widths), int(pack["block_size"]), int(row_begin or 0),
+                         R if row_end is None else int(row_end))
+    return part, (pal, off, data, w)
+
+
 class RadixTensor:
     """Rows [row_begin, row_end) of a pack-format-1 radix tensor laid out on a
     CUDA device for the sm_100a kernels. Validation runs in the library
@@ -17,40 +43,50 @@ class RadixTensor:
     ValueError and allocates nothing."""
 
     def __init__(self, pack: dict, device, row_begin: int = 0, row_end: int | None = None):
-        dev = torch.device(device)
-        if dev.type != "cuda":
-            raise ValueError(f"drinkme_b200 serves CUDA devices only, not {dev}")
-        if dev.index is None:
-            dev = torch.device("cuda", torch.cuda.current_device())
-        pal = np.ascontiguousarray(pack["rx_palette"], dtype=np.uint8)
-        off = np.ascontiguousarray(pack["rx_offsets"], dtype=np.uint32)
-        data = np.ascontiguousarray(pack["rx_data"], dtype=np.uint32)
-        if "NW" in pack:
-            data = data[: int(pack["NW"])]
-        widths = [int(w) for w in pack["widths"]]
-        R, C = int(pack["R"]), int(pack["C"])
-        row_end = R if row_end is None else int(row_end)
-        w = (ct.c_int32 * len(widths))(*widths)
+        dev = _cuda(device)
+        part, keep = _part(pack, row_begin, row_end)
         handle = ct.c_void_p()
-        _lib.call("dm_tensor_create", pal.ctypes.data_as(ct.c_void_p), pal.size, off.ctypes.data_as(ct.c_void_p),
-                  off.size, data.ctypes.data_as(ct.c_void_p), data.size, R, C, w, len(widths),
-                  int(pack["block_size"]), int(row_begin), row_end, int(dev.index), ct.byref(handle))
+        _lib.call("dm_tensor_create", part.host_palette, part.npalette, part.host_offsets, part.noffsets,
+                  part.host_data, part.nwords, part.R, part.C, part.host_widths, part.nwidths, part.block_size,
+                  part.row_begin, part.row_end, int(dev.index), ct.byref(handle))
+        del keep
+        self._init(handle, dev, np.ascontiguousarray(pack["rx_palette"], dtype=np.uint8).copy(),
+                   tuple(int(w) for w in pack["widths"]))
+
+    @classmethod
+    def fused(cls, packs, device, ranges=None) -> "RadixTensor":
+        """One handle over the rows of several packs sharing their columns
+        (dm_tensor_create_multi): a GEMV on it yields [y_0 | y_1 | ...].
+        `ranges` optionally gives each part's (row_begin, row_end)."""
+        dev = _cuda(device)
+        ranges = ranges or [(0, None)] * len(packs)
+        if len(ranges) != len(packs):
+            raise ValueError("RadixTensor.fused: one row range per pack")
+        parts = (_lib.PackPart * len(packs))()
+        keep = []
+        for i, (pk, (r0, r1)) in enumerate(zip(packs, ranges)):
+            parts[i], k = _part(pk, r0, r1)
+            keep.append(k)
+        handle = ct.c_void_p()
+        _lib.call("dm_tensor_create_multi", parts, len(packs), int(dev.index), ct.byref(handle))
+        del keep
+        t = cls.__new__(cls)
+        t._init(handle, dev, np.ascontiguousarray(packs[0]["rx_palette"], dtype=np.uint8).copy(),
+                tuple(int(w) for w in packs[0]["widths"]))
+        return t
+
+    def _init(self, handle, dev, palette, widths) -> None:
         self.ptr = handle
         self.torch_device = dev
         self.info = _lib.TensorInfo()
         _lib.lib().dm_tensor_get_info(self.ptr, ct.byref(self.info))
-        self.palette = pal.copy()
-        self.widths = tuple(widths)
+        self.palette = palette
+        self.widths = widths
 
     @classmethod
     def _wrap(cls, handle: ct.c_void_p, like: "RadixTensor") -> "RadixTensor":
         t = cls.__new__(cls)
-        t.ptr = handle
-        t.torch_device = like.torch_device
-        t.info = _lib.TensorInfo()
-        _lib.lib().dm_tensor_get_info(t.ptr, ct.byref(t.info))
-        t.palette = like.palette
-        t.widths = like.widths
+        t._init(handle, like.torch_device, like.palette, like.widths)
         return t
 
     def clone(self) -> "RadixTensor":

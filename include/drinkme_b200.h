@@ -76,6 +76,35 @@ int dm_tensor_create(const uint8_t *host_palette, size_t npalette, const uint32_
                      const int32_t *host_widths, int32_t nwidths, int32_t block_size, int64_t row_begin,
                      int64_t row_end, int32_t device, dm_tensor **out, char *err, size_t err_len);
 
+/* One pack-format-1 tensor (or row range of one) for dm_tensor_create_multi:
+ * the arguments of dm_tensor_create, gathered. */
+typedef struct dm_pack_part {
+    const uint8_t *host_palette;
+    size_t npalette;
+    const uint32_t *host_offsets;
+    size_t noffsets;
+    const uint32_t *host_data;
+    size_t nwords;
+    int64_t R, C;
+    const int32_t *host_widths;
+    int32_t nwidths, block_size;
+    int64_t row_begin, row_end;
+} dm_pack_part;
+
+/* A FUSED tensor: the rows of `nparts` packs that read the same activations
+ * (q, k and v; gate and up) stacked in order into one handle, so one GEMV
+ * launch computes [y_0 | y_1 | ...] = x @ [W_0; W_1; ...]^T. Each part is
+ * validated as dm_tensor_create validates it and keeps its own palette
+ * (its exponent tables ride in the unit headers). Every part must be sip
+ * (widths 3, 8) with 1024-weight blocks, all share C (a multiple of 1024),
+ * and every part but the last must contribute a multiple of 16 rows
+ * (DM_EINVAL otherwise). The handle's R and rows are the total rows; its
+ * read_bytes the parts' sum. No reference counterpart: the reference runs
+ * one RadixCompressedLinear per projection (src/drinkme/codec/swap.py:
+ * 395-456); the fused handle serves the same arithmetic in one launch. */
+int dm_tensor_create_multi(const dm_pack_part *parts, int32_t nparts, int32_t device, dm_tensor **out, char *err,
+                           size_t err_len);
+
 int dm_tensor_destroy(dm_tensor *t);
 
 /* A second handle holding a device-side copy of `src` (same device, its own
@@ -93,7 +122,8 @@ int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info);
  * (DM_EINVAL outside, the ValueError of radix_ops.py:384-385), bias is a
  * bf16 [rows] vector or NULL, out is [M, rows] row-major in `out_dtype`.
  * Column m of an M-row call is bitwise the M=1 call on row m. Uses the
- * tensor's own scratch: calls on one tensor must not overlap on the GPU. */
+ * tensor's own scratch: calls on one tensor must not overlap on the GPU.
+ * A fused tensor (dm_tensor_create_multi) needs 16-byte aligned x. */
 int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
             int32_t out_dtype, void *stream, char *err, size_t err_len);
 
@@ -115,7 +145,8 @@ int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t 
                     int32_t out_dtype, void *stream, char *err, size_t err_len);
 
 /* The shard's decoded bf16 bit patterns, uint16 [rows, C] — replaces
- * radix_ops.decode_bits (src/drinkme/codec/radix_ops.py:418-427). */
+ * radix_ops.decode_bits (src/drinkme/codec/radix_ops.py:418-427). For a
+ * sip tensor (fast_path) `out` must be 16-byte aligned. */
 int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *err, size_t err_len);
 
 /* The gulp schedule over the ORIGINAL pack layout on the device: one

@@ -147,6 +147,26 @@ def test_mc_rows_bitwise_the_m1_call_and_within_bound(golden, runtimes):
         assert np.abs(y8 - ref).max() / max(np.abs(ref).max(), 1e-30) <= 1e-3, name
 
 
+@pytest.mark.parametrize("R,C", [(4096, 5120), (1024, 5120), (3000, 2048)])
+def test_mc_rows_bitwise_the_m1_call_on_tensors_spanning_every_sm(R, C):
+    """Tensors with units enough for several stream-K workers per SM: the
+    work split must not change with M (nor with fp32 activations, whose
+    split rows triple the staged activations)."""
+    g = torch.Generator().manual_seed(R + C)
+    W = (torch.randn(R, C, generator=g) * 0.02).to(torch.bfloat16)
+    rt = swap.to_device_radix(codec.pack_weight_radix(W, "sip"), DEV)
+    x = torch.randn(8, C, generator=g)
+    for dt in (torch.bfloat16, torch.float32):
+        xd = x.to(dt).to(DEV)
+        ones = [radix_ops.gemv(rt, xd[j]) for j in range(8)]
+        for M in (2, 3, 5, 8):
+            ym = radix_ops.gemv_mc(rt, xd[:M])
+            for j in range(M):
+                assert torch.equal(ym[j], ones[j]), (dt, M, j)
+    assert torch.equal(radix_ops.gemv_mc(rt, x[:4].to(torch.bfloat16).to(DEV)),
+                       radix_ops.gemv_mc(rt, x[:4].to(torch.bfloat16).float().to(DEV)))
+
+
 def test_bf16_x_equals_its_fp32_widening(golden, runtimes):
     z, pins = golden
     for name, rt in runtimes.items():

@@ -58,6 +58,32 @@ def test_loader_refuses_malformed_descriptors(golden):
         _create(dict(p, widths=[3, 7]))
 
 
+def test_fused_loader_refuses_parts_it_cannot_serve(golden):
+    """dm_tensor_create_multi validates every part and the fusion rules on the
+    host, before touching a device."""
+    import torch
+
+    from drinkme_b200.tensor import RadixTensor
+
+    z, pins = golden
+    p = pack_of(z, pins, "sip_normal_16x4096")
+    g = torch.Generator().manual_seed(0)
+    narrow = codec.pack_weight_radix((torch.randn(16, 2048, generator=g) * 0.02).to(torch.bfloat16), "sip")
+    gulp = codec.pack_weight_radix((torch.randn(16, 4096, generator=g) * 0.02).to(torch.bfloat16), "gulp")
+    with pytest.raises(ValueError, match="invalid radix palette entries"):
+        RadixTensor.fused([p, dict(p, rx_palette=np.zeros_like(p["rx_palette"]))], "cuda:0")
+    with pytest.raises(ValueError, match="multiple of 16 rows"):
+        RadixTensor.fused([p, p], "cuda:0", [(0, 13), (0, 16)])
+    with pytest.raises(ValueError, match="share columns, block size and tier widths"):
+        RadixTensor.fused([p, narrow], "cuda:0")
+    with pytest.raises(ValueError, match="share columns, block size and tier widths"):
+        RadixTensor.fused([p, gulp], "cuda:0")
+    with pytest.raises(ValueError, match="served by the sip kernel"):
+        RadixTensor.fused([gulp, gulp], "cuda:0")
+    with pytest.raises(ValueError, match="one row range per pack"):
+        RadixTensor.fused([p, p], "cuda:0", [(0, 16)])
+
+
 def test_long_block_is_refused(golden):
     z, pins = golden
     p = pack_of(z, pins, "sip_normal_16x4096")
