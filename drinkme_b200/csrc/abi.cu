@@ -97,7 +97,7 @@ int create_from_parts(const dm::PackPart *parts, int nparts, int32_t device, dm_
         return cuda_fail(err, err_len, e, "cudaMalloc(error word)");
     }
     if (t->L.fast_sip) {
-        const int64_t workers = std::min<int64_t>((int64_t)t->sms * 8, t->L.units);
+        const int64_t workers = std::min<int64_t>((int64_t)t->sms, t->L.units);  // one per CTA
         t->S.max_workers = (int32_t)workers;
         const size_t pbytes = (size_t)workers * 2 * 128 * sizeof(float);
         const size_t cbytes = (size_t)t->L.tiles * sizeof(int);

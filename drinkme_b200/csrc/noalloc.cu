@@ -28,7 +28,7 @@
 namespace {
 
 // The limits of the static scratch (about 1.45 MiB per GPU):
-constexpr int64_t kNoAllocMaxWorkers = 1024;  // stream-K workers of one launch (148 SMs x 4 groups = 592)
+constexpr int64_t kNoAllocMaxWorkers = 1024;  // stream-K workers (CTAs) of one launch: 148 on a B200
 constexpr int64_t kNoAllocMaxTiles = 16384;   // 16-row tiles: tensors (or row shards) of up to 262,144 rows
 constexpr int64_t kNoAllocMaxCols = 32768;    // columns of an fp32 activation row (its bf16 split)
 

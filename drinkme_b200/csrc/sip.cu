@@ -8,15 +8,17 @@
 // activation row's result independent of the others.
 //
 // Design (B200-first):
-//   * A CTA = 1 producer warp + up to 4 groups of 4 consumer warps. Each
-//     group is a WORKER owning a contiguous range of units (16 rows x 1 block
-//     column, see layout.cpp); the units of all workers of the grid cover the
-//     tensor in tile-major order, split evenly (stream-K). The 4 warps of a
-//     group share each staged unit, each decoding a quarter of its k range,
-//     so 16 warps per SM hide the latencies on a few staged units.
+//   * A CTA = 1 producer warp, 4 groups of 4 consumer warps and 1 epilogue
+//     warp, one CTA per SM. The CTA is a stream-K WORKER: the units (16 rows x
+//     1 block column, see layout.cpp) of the tensor in tile-major order are
+//     split evenly over the CTAs. Consecutive CTAs therefore share at most one
+//     tile at each boundary; the CTA processes those (at most two) PARTIAL
+//     tiles first and its whole tiles after them.
 //   * The producer stages each unit with ONE 1-D bulk copy (the TMA engine)
 //     plus one 2 KB bulk copy per activation row of the unit's block column,
-//     into a per-group ring of shared-memory slots, completing an mbarrier.
+//     into a ring of shared-memory slots, completing an mbarrier. Unit i of
+//     the CTA's sequence goes to group i mod 4; the 4 warps of the group
+//     share it, each decoding a quarter of its k range.
 //   * A consumer decodes its unit straight into MMA operands: the weights
 //     are the A operand (m = 16 output rows) of mma.m16n8k16 bf16 with fp32
 //     accumulate, the activations the B operand (n = 8 = up to 8 activation
@@ -31,15 +33,19 @@
 //   * Escaped weights (about 2% of a N(0, 0.02) tensor) are added back as
 //     fp32 corrections: the loader's escape index lists each block's escape
 //     positions; the group's lanes split each row's escapes between them.
-//   * A worker accumulates a tile's units in registers (each unit's MMA chains
-//     start from zero; unit sums are added in unit order; the group's four
-//     warp partials are summed in warp order at the tile's end). A tile covered
-//     by one worker is written directly; a tile split across workers goes
-//     through scratch: each contributor writes its partial, the last to
-//     arrive (an atomic counter that it resets) sums them in worker order and
-//     writes the output. Every sum has a fixed order, so results are
-//     deterministic and activation row m of an M-row call is bitwise the M=1
-//     call on row m.
+//   * A group accumulates its units of a tile in registers (each unit's MMA
+//     chains start from zero; unit sums added in unit order), sums its four
+//     warps in warp order at the tile's end and deposits the result in a
+//     small ring of tile slots; a group with no unit in a tile deposits
+//     zeros. The EPILOGUE warp sums a tile's four group deposits in group
+//     order and writes a whole tile's outputs; a partial tile's sum goes
+//     through scratch instead: each CTA writes its sum, the last to arrive (an
+//     atomic counter that it resets) adds them in CTA order and writes the
+//     outputs. As the partial tiles come first, those round trips overlap
+//     the CTA's remaining units, and the consumers never wait on them.
+//   * Every sum has a fixed order that depends on the tensor alone (not on
+//     M nor the number of staging slots), so results are deterministic and
+//     activation row m of an M-row call is bitwise the M=1 call on row m.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -60,18 +66,21 @@ struct SipArgs {
     const uint16_t *bias;
     void *out;
     int32_t out_f32;
-    float *partials;
-    int *counters;
+    float *partials;  // [grid][2][128]: a CTA's sums of its first / last tile
+    int *counters;    // [tiles], zero between launches
     int *err;
-    int32_t slot_bytes, x_off, spg, ng, workers, dir_cap;
-    int32_t nl, lpg;  // logical workers per CTA; per group (nl / ng)
+    int32_t slot_bytes, x_off, nslots, dir_cap;
 };
 
-// A WORKER is a group of kGroupWarps consumer warps sharing each staged unit:
-// warp w of the group decodes quads [4w, 4w + 4) (k in [256w, 256w + 256)) of
-// every row of the unit, and every 16th escape from w * 4 on.
+// A GROUP of kGroupWarps consumer warps shares each staged unit: warp w of
+// the group decodes quads [4w, 4w + 4) (k in [256w, 256w + 256)) of every
+// row of the unit, and every 16th escape from w * 4 on. The CTA has kGroups
+// groups (always: the sums' order must not depend on the launch).
 constexpr int kGroupWarps = 4;
-constexpr int kMaxGroups = 4;
+constexpr int kGroups = 4;
+constexpr int kTileRing = 4;  // tile slots between the groups and the epilogue warp
+constexpr int kSipThreads = 32 * (2 + kGroups * kGroupWarps);
+constexpr int kMaxSlots = 12;  // staging slots of the unit ring
 
 __device__ __forceinline__ int64_t range_start(int64_t w, int64_t U, int64_t W) { return (w * U) / W; }
 __device__ __forceinline__ int64_t worker_of(int64_t u, int64_t U, int64_t W) { return ((u + 1) * W + U - 1) / U - 1; }
@@ -139,22 +148,21 @@ __device__ __forceinline__ void quad(const uint8_t *lit0, const uint32_t *t00, c
     mma_bf16_16816(d0, d1, d2, d3, a01[3], c01[3], a23[3], c23[3], X1.z, X1.w);
 }
 
-// P: the tile's partial [16 rows][8 virtual rows]; outputs m < M_out combine
-// their nsplit virtual rows, add the bias in fp32 and round once.
-__device__ void store_outputs(const SipArgs &a, int64_t tile, const float *P) {
-    const int lane = threadIdx.x & 31;
-    for (int o = lane; o < kUnitRows * a.M_out; o += 32) {
-        const int r = o % kUnitRows, m = o / kUnitRows;
-        const int64_t row = tile * kUnitRows + r;
-        if (row >= a.rows) continue;
-        float y = P[r * 8 + m * a.nsplit];
-        for (int s = 1; s < a.nsplit; ++s) y += P[r * 8 + m * a.nsplit + s];
-        if (a.bias) y += bf16_bits_to_f32(a.bias[row]);
-        if (a.out_f32)
-            reinterpret_cast<float *>(a.out)[m * a.rows + row] = y;
-        else
-            reinterpret_cast<uint16_t *>(a.out)[m * a.rows + row] = f32_to_bf16_bits(y);
-    }
+// Output o = (row r, activation row m) of tile `tile` from the tile's sums
+// S[v][16] (virtual row v = m * nsplit + s): the nsplit virtual rows added in
+// order, the bias in fp32, one rounding.
+template <typename Sum>
+__device__ __forceinline__ void store_output(const SipArgs &a, int64_t tile, int o, Sum S) {
+    const int r = o & 15, m = o >> 4;
+    const int64_t row = tile * kUnitRows + r;
+    if (row >= a.rows) return;
+    float y = S(m * a.nsplit * 16 + r);
+    for (int s = 1; s < a.nsplit; ++s) y += S((m * a.nsplit + s) * 16 + r);
+    if (a.bias) y += bf16_bits_to_f32(a.bias[row]);
+    if (a.out_f32)
+        reinterpret_cast<float *>(a.out)[m * a.rows + row] = y;
+    else
+        reinterpret_cast<uint16_t *>(a.out)[m * a.rows + row] = f32_to_bf16_bits(y);
 }
 
 __device__ __forceinline__ void group_sync(int group) {
@@ -180,117 +188,188 @@ __device__ __forceinline__ void escapes(const uint8_t *lit, RowEntry e, const ui
     }
 }
 
+// The CTA's unit sequence: its first tile's units when that tile is partial
+// (segment A), its last tile's when partial (B), then its whole tiles (C).
+// Position p of the sequence -> unit and tile sequence number.
+struct Seq {
+    int64_t a0, b0, c0;     // first unit of A, B, C
+    int32_t nA, nAB, n;     // |A|, |A| + |B|, |A| + |B| + |C|
+    int32_t tsB, tsC;       // sequence numbers of B's tile and C's first tile
+    int32_t ntiles;
+    int64_t tA, tB, tC;     // tile ids of A, B and C's first tile
+    __device__ void init(int64_t cu0, int64_t cu1, int64_t NB) {
+        const int64_t f = cu0 / NB, l = (cu1 - 1) / NB;
+        const bool pa = cu0 > f * NB || cu1 < (f + 1) * NB;
+        const bool pb = l != f && cu1 < (l + 1) * NB;
+        const int64_t a1 = pa ? std::min(cu1, (f + 1) * NB) : cu0;
+        a0 = cu0;
+        b0 = pb ? l * NB : cu1;
+        c0 = a1;
+        const int64_t c1 = pb ? l * NB : cu1;
+        nA = (int32_t)(a1 - cu0);
+        nAB = nA + (int32_t)(pb ? cu1 - l * NB : 0);
+        n = (int32_t)(cu1 - cu0);
+        tsB = nA > 0 ? 1 : 0;
+        tsC = tsB + (nAB > nA ? 1 : 0);
+        ntiles = tsC + (int32_t)((c1 - c0) / NB);
+        tA = f;
+        tB = l;
+        tC = c0 / NB;
+    }
+    __device__ __forceinline__ int64_t tile_of(int32_t ts) const {
+        return ts < tsB ? tA : (ts < tsC ? tB : tC + (ts - tsC));
+    }
+};
+
 template <int MV>
-__global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_gemv_kernel(SipArgs a) {
+__global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int kP = 16 * MV;  // floats of one tile partial [MV][16]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nslots = a.ng * a.spg;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)nslots * a.slot_bytes);
-    uint64_t *empty = full + nslots;
-    float *gbuf = reinterpret_cast<float *>(empty + nslots);  // [ng][kGroupWarps][16][8] partials
-    uint32_t *dir = reinterpret_cast<uint32_t *>(gbuf + a.ng * kGroupWarps * 128);  // this CTA's unit starts
-    const int64_t U = a.units, W = a.workers, NB = a.NB;
-    const int64_t cta_u0 = range_start((int64_t)blockIdx.x * a.nl, U, W);
-    const int64_t cta_u1 = range_start((int64_t)(blockIdx.x + 1) * a.nl, U, W);
-    const bool dir_in_smem = (cta_u1 - cta_u0 + 1) <= a.dir_cap;
+    const int S = a.nslots;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * a.slot_bytes);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;          // [kTileRing]: 16 warp deposits
+    uint64_t *tempty = tfull + kTileRing;  // [kTileRing]: the epilogue warp's release
+    float *pwb = reinterpret_cast<float *>(tempty + kTileRing);  // [kGroups][2][kGroupWarps][kP]
+    float *tslot = pwb + kGroups * 2 * kGroupWarps * kP;          // [kTileRing][kGroups][kP]
+    float *ebuf = tslot + kTileRing * kGroups * kP;               // [kP] the epilogue's tile sum
+    uint32_t *dir = reinterpret_cast<uint32_t *>(ebuf + kP);     // this CTA's unit starts
+    const int64_t U = a.units, W = gridDim.x, NB = a.NB;
+    const int64_t cu0 = range_start(blockIdx.x, U, W), cu1 = range_start(blockIdx.x + 1, U, W);
+    const bool dir_in_smem = (cu1 - cu0 + 1) <= a.dir_cap;
+    Seq q;
+    q.init(cu0, cu1, NB);
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
-        for (int s = 0; s < nslots; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kGroupWarps);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kGroupWarps);
+        }
+        for (int i = 0; i < kTileRing; ++i) {
+            mbar_init(&tfull[i], kGroups * kGroupWarps);
+            mbar_init(&tempty[i], 1);
         }
         mbar_fence_init();
     }
     if (warp == 0 && dir_in_smem)
-        for (int64_t i = lane; i <= cta_u1 - cta_u0; i += 32) dir[i] = a.unit16[cta_u0 + i];
+        for (int64_t i = lane; i <= cu1 - cu0; i += 32) dir[i] = a.unit16[cu0 + i];
     __syncthreads();
+    // position p -> unit
+    auto unit_at = [&](int32_t p) -> int64_t {
+        return p < q.nA ? q.a0 + p : (p < q.nAB ? q.b0 + (p - q.nA) : q.c0 + (p - q.nAB));
+    };
 
     if (warp == 0) {
         // ---------------------------------------------------- producer --
-        // per-group cursors kept in registers (no division in the loop):
-        // next unit, its end, its block column, the slot it goes to and the
-        // number of units staged so far
         if (lane == 0) {
-            int32_t nu[kMaxGroups], eu[kMaxGroups], bc[kMaxGroups], si[kMaxGroups], fills[kMaxGroups];
-#pragma unroll
-            for (int g = 0; g < kMaxGroups; ++g) {
-                const int64_t w = (int64_t)blockIdx.x * a.nl + (int64_t)g * a.lpg;
-                nu[g] = g < a.ng ? (int32_t)range_start(w, U, W) : 0;
-                eu[g] = g < a.ng ? (int32_t)range_start(w + a.lpg, U, W) : 0;
-                bc[g] = (int32_t)(nu[g] % NB);
-                si[g] = 0;
-                fills[g] = 0;
-            }
-            bool ok = true;
-            // the weights of every group's first spg units do not depend on
-            // the kernel before this one: stage them before waiting for it,
-            // then add their activation rows once it has completed
-#pragma unroll
-            for (int g = 0; g < kMaxGroups; ++g) {
-                for (int k = 0; k < a.spg && nu[g] + k < eu[g]; ++k) {
-                    const int32_t u = nu[g] + k;
-                    const int slot = g * a.spg + k;
-                    const uint32_t q0 = dir_in_smem ? dir[u - cta_u0] : a.unit16[u];
-                    const uint32_t q1 = dir_in_smem ? dir[u + 1 - cta_u0] : a.unit16[u + 1];
-                    const uint32_t ubytes = (q1 - q0) * 16u;
-                    mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
-                    bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
-                }
-            }
+            auto stage_w = [&](int32_t p, int slot) {
+                const int64_t u = unit_at(p);
+                const uint32_t q0 = dir_in_smem ? dir[u - cu0] : a.unit16[u];
+                const uint32_t q1 = dir_in_smem ? dir[u + 1 - cu0] : a.unit16[u + 1];
+                const uint32_t ubytes = (q1 - q0) * 16u;
+                mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
+                bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
+            };
+            auto stage_x = [&](int32_t p, int slot) {
+                const int64_t u = unit_at(p);
+                const uint16_t *xb = a.x + (size_t)(u % NB) * 1024;
+                uint8_t *dst = smem + (size_t)slot * a.slot_bytes + a.x_off;
+                for (int v = 0; v < a.Mv; ++v) bulk_g2s(dst + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
+            };
+            // the first S units' weights do not depend on the kernel before
+            // this one: stage them, wait for it, then add their activations
+            const int32_t first = std::min<int32_t>(S, q.n);
+            for (int32_t p = 0; p < first; ++p) stage_w(p, p);
             pdl_wait();
-#pragma unroll
-            for (int g = 0; g < kMaxGroups; ++g) {
-                for (int k = 0; k < a.spg && nu[g] < eu[g]; ++k) {
-                    const int slot = g * a.spg + k;
-                    const uint16_t *xb = a.x + (size_t)bc[g] * 1024;
-                    uint8_t *dst = smem + (size_t)slot * a.slot_bytes;
-                    for (int v = 0; v < a.Mv; ++v)
-                        bulk_g2s(dst + a.x_off + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
-                    nu[g] += 1;
-                    bc[g] = (bc[g] + 1 == NB) ? 0 : bc[g] + 1;
-                    si[g] = (si[g] + 1 == a.spg) ? 0 : si[g] + 1;
-                    fills[g] += 1;
+            for (int32_t p = 0; p < first; ++p) stage_x(p, p);
+            int slot = 0;
+            uint32_t epar = 0;  // parity of the empty phase to wait for
+            bool ok = true;
+            for (int32_t p = first; p < q.n && ok; ++p) {
+                if (!mbar_wait(&empty[slot], epar, a.err, kErrWaitEmpty)) ok = false;
+                if (ok) {
+                    stage_w(p, slot);
+                    stage_x(p, slot);
                 }
-            }
-            for (;;) {
-                bool any = false;
-#pragma unroll
-                for (int g = 0; g < kMaxGroups; ++g) {
-                    if (!ok || nu[g] >= eu[g]) continue;
-                    any = true;
-                    const int slot = g * a.spg + si[g];
-                    const int use = fills[g] / a.spg;
-                    if (use > 0 && !mbar_wait(&empty[slot], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) {
-                        ok = false;
-                        continue;
-                    }
-                    const int32_t u = nu[g];
-                    const uint32_t q0 = dir_in_smem ? dir[u - cta_u0] : a.unit16[u];
-                    const uint32_t q1 = dir_in_smem ? dir[u + 1 - cta_u0] : a.unit16[u + 1];
-                    const uint32_t ubytes = (q1 - q0) * 16u;
-                    uint8_t *dst = smem + (size_t)slot * a.slot_bytes;
-                    mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
-                    bulk_g2s(dst, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
-                    const uint16_t *xb = a.x + (size_t)bc[g] * 1024;
-                    for (int v = 0; v < a.Mv; ++v)
-                        bulk_g2s(dst + a.x_off + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
-                    nu[g] = u + 1;
-                    bc[g] = (bc[g] + 1 == NB) ? 0 : bc[g] + 1;
-                    si[g] = (si[g] + 1 == a.spg) ? 0 : si[g] + 1;
-                    fills[g] += 1;
+                if (++slot == S) {
+                    slot = 0;
+                    epar ^= 1u;
                 }
-                if (!any || !ok) break;
             }
             // drain: every copy this producer issued lands before the CTA exits
+            for (int32_t p = std::max<int32_t>(0, q.n - S); p < q.n && ok; ++p)
+                mbar_wait(&full[p % S], (uint32_t)((p / S) & 1), a.err, kErrWaitDrain);
+        }
+        return;
+    }
+
+    if (warp == 1 + kGroups * kGroupWarps) {
+        // ---------------------------------------------------- epilogue --
+        bool ok = true;
+        for (int32_t ts = 0; ts < q.ntiles; ++ts) {
+            const int ring = ts % kTileRing;
+            if (ok && !mbar_wait(&tfull[ring], (uint32_t)((ts / kTileRing) & 1), a.err, kErrWaitFull)) ok = false;
+            float T[(kP + 31) / 32];
 #pragma unroll
-            for (int g = 0; g < kMaxGroups; ++g) {
-                for (int k = 0; k < a.spg && g < a.ng; ++k) {
-                    int last = -1;
-                    for (int f = fills[g] - 1; f >= 0 && f >= fills[g] - a.spg; --f)
-                        if (f % a.spg == k) { last = f; break; }
-                    if (last < 0) continue;
-                    mbar_wait(&full[g * a.spg + k], (uint32_t)((last / a.spg) & 1), a.err, kErrWaitDrain);
+            for (int i = 0; i < (kP + 31) / 32; ++i) {
+                const int e = lane + 32 * i;
+                float v = 0.f;
+                if (e < kP) {
+                    const float *sl = tslot + ring * kGroups * kP + e;
+                    v = sl[0];
+#pragma unroll
+                    for (int gg = 1; gg < kGroups; ++gg) v += sl[gg * kP];
                 }
+                T[i] = v;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ring]);
+            const int64_t tl = q.tile_of(ts);
+            bool store = ts >= q.tsC;
+            if (!store) {
+                // a tile shared with other CTAs: this CTA's sum to scratch,
+                // the last of them to arrive adds all in CTA order
+                const int cs = (tl == cu0 / NB) ? 0 : 1;
+                float *mine = a.partials + ((int64_t)blockIdx.x * 2 + cs) * 128;
+#pragma unroll
+                for (int i = 0; i < (kP + 31) / 32; ++i)
+                    if (lane + 32 * i < kP) mine[lane + 32 * i] = T[i];
+                __threadfence();
+                __syncwarp();
+                const int64_t cf = worker_of(tl * NB, U, W), cl = worker_of((tl + 1) * NB - 1, U, W);
+                int last = 0;
+                if (lane == 0) {
+                    const int old = atomicAdd(&a.counters[tl], 1);
+                    last = (old == (int)(cl - cf));
+                    if (last) {
+                        __threadfence();
+                        a.counters[tl] = 0;
+                    }
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    for (int64_t c = cf; c <= cl; ++c) {
+                        const int sc = (tl == range_start(c, U, W) / NB) ? 0 : 1;
+                        const float *pp = a.partials + (c * 2 + sc) * 128;
+#pragma unroll
+                        for (int i = 0; i < (kP + 31) / 32; ++i)
+                            if (lane + 32 * i < kP) {
+                                const float x = __ldcg(pp + lane + 32 * i);
+                                T[i] = (c == cf) ? x : T[i] + x;
+                            }
+                    }
+                    store = true;
+                }
+            }
+            if (store) {
+#pragma unroll
+                for (int i = 0; i < (kP + 31) / 32; ++i)
+                    if (lane + 32 * i < kP) ebuf[lane + 32 * i] = T[i];
+                __syncwarp();
+                for (int o = lane; o < 16 * a.M_out; o += 32) store_output(a, tl, o, [&](int e) { return ebuf[e]; });
+                __syncwarp();
             }
         }
         return;
@@ -298,24 +377,26 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
 
     // ------------------------------------------------------- consumers --
     const int gi = (warp - 1) / kGroupWarps, wi = (warp - 1) % kGroupWarps;
-    // the group's units: its lpg logical workers' ranges, consecutive
-    int64_t w = (int64_t)blockIdx.x * a.nl + (int64_t)gi * a.lpg;
-    const int64_t gu0 = range_start(w, U, W), gu1 = range_start(w + a.lpg, U, W);
-    int64_t u0 = gu0, u1 = range_start(w + 1, U, W);  // the current logical worker's range
     const int g = lane >> 2, t = lane & 3;
-    float *Pw = gbuf + (gi * kGroupWarps + wi) * 128;  // this warp's [16 rows][8 virtual rows]
-    float *P0 = gbuf + (gi * kGroupWarps) * 128;       // the group's sum
 
     // D[rows g, g + 8][activation rows 2t, 2t + 1] over this warp's k range, the tile so far
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     float cg[MV], cg8[MV];  // rows g and g + 8: escape corrections (this lane's share)
 #pragma unroll
     for (int v = 0; v < MV; ++v) cg[v] = cg8[v] = 0.f;
-    int64_t tile = u0 / NB;
+    int buf = 0;
+    bool ok = true;
 
-    // tile tl of logical worker w (units [u0, u1)): the group's sums, then
-    // the tile's output, or this worker's partial of a tile it shares
-    auto flush = [&](int64_t tl) {
+    // the tile ring slot of tile sequence number ts, once the epilogue warp
+    // has released its previous use
+    auto tile_slot = [&](int32_t ts) -> float * {
+        const int ring = ts % kTileRing, use = ts / kTileRing;
+        if (use > 0 && ok && !mbar_wait(&tempty[ring], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
+        return tslot + (ring * kGroups + gi) * kP;
+    };
+    // this group's sum of tile ts (its warps' partials in warp order) into
+    // the tile ring; the two partial buffers alternate, so one barrier will do
+    auto flush = [&](int32_t ts) {
 #pragma unroll
         for (int v = 0; v < MV; ++v) {
             float s = cg[v], s8 = cg8[v];
@@ -326,166 +407,138 @@ __global__ void __launch_bounds__(32 * (1 + kMaxGroups * kGroupWarps), 1) sip_ge
             cg[v] = s;
             cg8[v] = s8;
         }
-        // this warp's partial: corrections by row, then the D owners add theirs
+        float *grp = pwb + (gi * 2 + buf) * kGroupWarps * kP;
+        float *pw = grp + wi * kP;
         if (t == 0) {
 #pragma unroll
-            for (int v = 0; v < kMaxVirtualRows; ++v) {
-                Pw[g * 8 + v] = v < MV ? cg[v] : 0.f;
-                Pw[(g + 8) * 8 + v] = v < MV ? cg8[v] : 0.f;
+            for (int v = 0; v < MV; ++v) {
+                pw[v * 16 + g] = cg[v];
+                pw[v * 16 + g + 8] = cg8[v];
             }
         }
         __syncwarp();
-        Pw[g * 8 + 2 * t] += acc0;
-        Pw[g * 8 + 2 * t + 1] += acc1;
-        Pw[(g + 8) * 8 + 2 * t] += acc2;
-        Pw[(g + 8) * 8 + 2 * t + 1] += acc3;
-        __syncwarp();
-        group_sync(gi);
-        if (wi == 0) {
-            // the group's sum, warps in order
-            float s[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s[i] = P0[lane + 32 * i];
-#pragma unroll
-                for (int k = 1; k < kGroupWarps; ++k) s[i] += P0[k * 128 + lane + 32 * i];
-            }
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 4; ++i) P0[lane + 32 * i] = s[i];
-            __syncwarp();
-            const bool whole = tl * NB >= u0 && (tl + 1) * NB <= u1;
-            if (whole) {
-                store_outputs(a, tl, P0);
-            } else {
-                const int slot = (tl == u0 / NB) ? 0 : 1;
-                float *mine = a.partials + (w * 2 + slot) * 128;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) mine[lane + 32 * i] = s[i];
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
-                    const int n = (int)(wl - wf + 1);
-                    const int old = atomicAdd(&a.counters[tl], 1);
-                    last = (old == n - 1);
-                    if (last) {
-                        __threadfence();
-                        a.counters[tl] = 0;
-                    }
-                }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    const int64_t wf = worker_of(tl * NB, U, W), wl = worker_of((tl + 1) * NB - 1, U, W);
-                    float r[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int64_t j = wf; j <= wl; ++j) {
-                        const int64_t j0 = range_start(j, U, W);
-                        const int sj = (tl == j0 / NB) ? 0 : 1;
-                        const float *pp = a.partials + (j * 2 + sj) * 128;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) r[i] += __ldcg(pp + lane + 32 * i);
-                    }
-                    __syncwarp();
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) P0[lane + 32 * i] = r[i];
-                    __syncwarp();
-                    store_outputs(a, tl, P0);
-                }
-            }
-            __syncwarp();
+        if (2 * t < MV) {
+            pw[2 * t * 16 + g] += acc0;
+            pw[2 * t * 16 + g + 8] += acc2;
+        }
+        if (2 * t + 1 < MV) {
+            pw[(2 * t + 1) * 16 + g] += acc1;
+            pw[(2 * t + 1) * 16 + g + 8] += acc3;
         }
         group_sync(gi);
+        float *dst = tile_slot(ts);
+        for (int e = wi * 32 + lane; e < kP; e += kGroupWarps * 32) {
+            float v = grp[e];
+#pragma unroll
+            for (int k = 1; k < kGroupWarps; ++k) v += grp[k * kP + e];
+            dst[e] = v;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tfull[ts % kTileRing]);
+        buf ^= 1;
         acc0 = acc1 = acc2 = acc3 = 0.f;
 #pragma unroll
         for (int v = 0; v < MV; ++v) cg[v] = cg8[v] = 0.f;
     };
+    // a tile without units of this group: zeros
+    auto deposit_zero = [&](int32_t ts) {
+        float *dst = tile_slot(ts);
+        for (int e = wi * 32 + lane; e < kP; e += kGroupWarps * 32) dst[e] = 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tfull[ts % kTileRing]);
+    };
 
-    bool ok = true;
     const uint32_t sh = (t & 1) ? 16u : 0u;
     const bool has_x = g < MV;
-    int32_t bcol = (int32_t)(u0 % NB);  // block column of unit u
-    int sidx = 0;                       // slot of unit u within the group's ring
-    uint32_t par = 0;                   // parity of that slot's current fill
     const int q0 = 4 * wi, j0 = 4 * wi + t;
-    for (int64_t u = gu0; u < gu1; ++u) {
-        const int slot = gi * a.spg + sidx;
-        if (!mbar_wait(&full[slot], par, a.err, kErrWaitFull)) {
-            ok = false;
-            break;
+    int32_t cur = -1;  // tile sequence number of the group's current tile
+    int slot = gi % S;
+    uint32_t par = (uint32_t)((gi / S) & 1);
+    int32_t cq = -1, cts = 0;  // in segment C: the unit's offset in its tile, its tile's number
+    const int32_t nb = (int32_t)NB;
+    for (int32_t p = gi; p < q.n; p += kGroups) {
+        int32_t ts;
+        if (p < q.nA) {
+            ts = 0;
+        } else if (p < q.nAB) {
+            ts = q.tsB;
+        } else {
+            if (cq < 0) {
+                cq = (p - q.nAB) % nb;
+                cts = (p - q.nAB) / nb;
+            } else {
+                cq += kGroups;
+                while (cq >= nb) {
+                    cq -= nb;
+                    ++cts;
+                }
+            }
+            ts = q.tsC + cts;
         }
-        if (u == u1) {
-            // the next logical worker's range begins (never empty: W <= U)
-            flush(tile);
-            w += 1;
-            u0 = u1;
-            u1 = range_start(w + 1, U, W);
-            if (bcol == 0) tile += 1;
-        } else if (bcol == 0 && u != u0) {
-            flush(tile);
-            tile += 1;
+        if (ts != cur) {
+            if (cur >= 0) flush(cur);
+            for (int32_t z = cur + 1; z < ts; ++z) deposit_zero(z);
+            cur = ts;
         }
-        const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
-        // the exponent tables of the unit's part (high part th0/th1, low tl0/tl1)
-        const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
-        const uint32_t th0 = tab.x, th1 = tab.y, tl0 = tab.z, tl1 = tab.w;
-        const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
-        const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
-        const uint8_t *lit0 = base + (size_t)e0.off16 * 16;
-        const uint8_t *lit1 = base + (size_t)e1.off16 * 16;
-        const uint32_t *t00 = reinterpret_cast<const uint32_t *>(lit0 + 1024);
-        const uint32_t *t01 = reinterpret_cast<const uint32_t *>(lit1 + 1024);
-        const uint8_t *xs = base + a.x_off;
-        const uint8_t *xg = xs + g * kXRowStride;
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-        float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
-        quad(lit0, t00, lit1, t01, xg, q0 + 0, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
-        quad(lit0, t00, lit1, t01, xg, q0 + 1, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
-        quad(lit0, t00, lit1, t01, xg, q0 + 2, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
-        quad(lit0, t00, lit1, t01, xg, q0 + 3, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
-        // escapes of rows g and g + 8: the group's warps take every 16th one, lane t every 4th of those
-        escapes<MV>(lit0, e0, xs, j0, cg);
-        escapes<MV>(lit1, e1, xs, j0, cg8);
-        acc0 += d0;
-        acc0 += f0;
-        acc1 += d1;
-        acc1 += f1;
-        acc2 += d2;
-        acc2 += f2;
-        acc3 += d3;
-        acc3 += f3;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        bcol = (bcol + 1 == NB) ? 0 : bcol + 1;
-        if (++sidx == a.spg) {
-            sidx = 0;
+        if (ok && !mbar_wait(&full[slot], par, a.err, kErrWaitFull)) ok = false;
+        if (ok) {
+            const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
+            // the exponent tables of the unit's part (high part th0/th1, low tl0/tl1)
+            const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
+            const uint32_t th0 = tab.x, th1 = tab.y, tl0 = tab.z, tl1 = tab.w;
+            const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
+            const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
+            const uint8_t *lit0 = base + (size_t)e0.off16 * 16;
+            const uint8_t *lit1 = base + (size_t)e1.off16 * 16;
+            const uint32_t *t00 = reinterpret_cast<const uint32_t *>(lit0 + 1024);
+            const uint32_t *t01 = reinterpret_cast<const uint32_t *>(lit1 + 1024);
+            const uint8_t *xs = base + a.x_off;
+            const uint8_t *xg = xs + g * kXRowStride;
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+            float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
+            quad(lit0, t00, lit1, t01, xg, q0 + 0, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 1, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 2, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 3, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+            // escapes of rows g and g + 8: the group's warps take every 16th one, lane t every 4th of those
+            escapes<MV>(lit0, e0, xs, j0, cg);
+            escapes<MV>(lit1, e1, xs, j0, cg8);
+            acc0 += d0;
+            acc0 += f0;
+            acc1 += d1;
+            acc1 += f1;
+            acc2 += d2;
+            acc2 += f2;
+            acc3 += d3;
+            acc3 += f3;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        slot += kGroups;
+        while (slot >= S) {
+            slot -= S;
             par ^= 1u;
         }
     }
-    if (ok && gu1 > gu0) flush(tile);
+    if (cur >= 0) flush(cur);
+    for (int32_t z = cur + 1; z < q.ntiles; ++z) deposit_zero(z);
 }
 
-// Shared-memory plan for a launch: slot size, slots per group and groups,
-// the groups a divisor of the nl logical workers per CTA (so the work split,
-// and with it every sum's order, does not depend on Mv).
-int sip_shared_bytes(const dm_tensor *t, int Mv, int nl, int *slot_bytes, int *spg, int *ng, int dir_cap) {
+// Shared-memory plan for a launch: the slot size and the number of slots.
+// Fixed part: the barriers, the groups' partial buffers, the tile ring, the
+// epilogue's sum and the directory.
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int dir_cap) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
     const int sb = unit + Mv * kXRowStride;
     const int budget = 227 * 1024;
-    const int fixed = kMaxGroups * kGroupWarps * 128 * 4 + (dir_cap + 1) * 4 + 256;
-    const int plans[][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 4}, {2, 3}, {2, 2}, {1, 4}, {1, 3}, {1, 2}};
-    for (const auto &pl : plans) {
-        if (pl[0] > nl || nl % pl[0] != 0) continue;
-        int need = pl[0] * pl[1] * (sb + 16) + fixed;
-        if (need <= budget) {
-            *slot_bytes = sb;
-            *ng = pl[0];
-            *spg = pl[1];
-            return need;
-        }
-    }
-    return -1;
+    const int kP = 16 * Mv;
+    const int fixed = (2 * kMaxSlots + 2 * kTileRing) * 8 +
+                      (kGroups * 2 * kGroupWarps + kTileRing * kGroups + 1) * kP * 4 + (dir_cap + 1) * 4 + 128;
+    const int n = std::min(kMaxSlots, (budget - fixed) / sb);
+    if (n < 2) return -1;
+    *slot_bytes = sb;
+    *nslots = n;
+    return n * sb + fixed;
 }
 
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
@@ -495,19 +548,27 @@ int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, in
 }
 
 // The launch with caller-supplied scratch (partials for `max_workers`
-// workers, per-tile counters that are zero on entry, the error word):
+// CTAs, per-tile counters that are zero on entry, the error word):
 // dm_gemv passes the tensor's own, dm_gemv_noalloc a static device array.
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg) {
     const dm::TensorLayout &L = t->L;
-    int slot_bytes = 0, spg = 0, ng = 0;
-    // one CTA per SM and nl logical workers per CTA, each owning at least one
-    // unit: the split depends on the tensor alone
-    const int64_t grid0 = std::min<int64_t>(t->sms, L.units);
-    const int nl = (int)std::min<int64_t>(kMaxGroups, L.units / grid0);
-    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid0 - 1) / grid0 + 2);
-    int smem = sip_shared_bytes(t, Mv, nl, &slot_bytes, &spg, &ng, dir_cap);
+    if (Mv < 1 || Mv > kMaxVirtualRows) {
+        msg = "sip kernel: 1..8 virtual activation rows";
+        return DM_EINVAL;
+    }
+    // one CTA per SM, each a stream-K worker owning at least one unit: the
+    // split depends on the tensor alone
+    const int64_t grid = std::min<int64_t>(t->sms, L.units);
+    if (grid > max_workers) {
+        msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
+              std::to_string(max_workers);
+        return DM_EINVAL;
+    }
+    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid - 1) / grid + 2);
+    int slot_bytes = 0, nslots = 0;
+    const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, dir_cap);
     if (smem < 0) {
         msg = "sip kernel: a unit does not fit in shared memory";
         return DM_EINVAL;
@@ -517,10 +578,6 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
                                                   sip_gemv_kernel<4>, sip_gemv_kernel<5>, sip_gemv_kernel<6>,
                                                   sip_gemv_kernel<7>, sip_gemv_kernel<8>};
     static bool attr_set[kMaxVirtualRows] = {false};
-    if (Mv < 1 || Mv > kMaxVirtualRows) {
-        msg = "sip kernel: 1..8 virtual activation rows";
-        return DM_EINVAL;
-    }
     const Kern kern = kernels[Mv - 1];
     if (!attr_set[Mv - 1]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -529,13 +586,6 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
             return DM_ECUDA;
         }
         attr_set[Mv - 1] = true;
-    }
-    const int64_t grid = grid0;
-    const int64_t workers = grid * nl;
-    if (workers > max_workers) {
-        msg = "sip kernel: " + std::to_string(workers) + " stream-K workers exceed the scratch's " +
-              std::to_string(max_workers);
-        return DM_EINVAL;
     }
     SipArgs a{};
     a.data = t->d_data;
@@ -555,16 +605,12 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.counters = counters;
     a.err = err;
     a.slot_bytes = slot_bytes;
-    a.x_off = (t->L.max_unit_bytes + 127) & ~127;
-    a.spg = spg;
-    a.ng = ng;
-    a.workers = (int32_t)workers;
+    a.x_off = (L.max_unit_bytes + 127) & ~127;
+    a.nslots = nslots;
     a.dir_cap = dir_cap;
-    a.nl = nl;
-    a.lpg = nl / ng;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(32 * (1 + ng * kGroupWarps));
+    cfg.blockDim = dim3(kSipThreads);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
