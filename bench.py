@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="qwen3-32b")
     ap.add_argument("--no-fuse", action="store_true", help="one launch per linear instead of q|k|v and gate|up")
+    ap.add_argument("--gather", choices=("peer", "nccl"), default="peer",
+                    help="N > 1: the output gather fused into the GEMV over NVLink (peer), or NCCL all-gather")
     ap.add_argument("--variants", type=int, default=2,
                     help="distinct random tensors per shape; every layer still gets its own HBM copy")
     ap.add_argument("--no-secondary", action="store_true", help="skip the qwen3-8b chain beside the headline")
@@ -199,7 +201,7 @@ class Chain:
     """One decode token's linear stack with static buffers, for graph capture:
     per layer, one launch per group (q|k|v, o, gate|up, down when fused)."""
 
-    def __init__(self, wl, layers, rank, world, device, head_weight=None, fuse=True):
+    def __init__(self, wl, layers, rank, world, device, head_weight=None, fuse=True, gather="peer"):
         import torch
 
         from drinkme_b200 import shard
@@ -233,6 +235,21 @@ class Chain:
         self.head = head_weight
         self.head_out = None
         self.last = None
+        self.gather = gather if world > 1 else None
+        self.plan = None
+        if self.gather == "peer":
+            from drinkme_b200 import shard as _shard
+
+            if any(rt is None for row in layers for rt in row):
+                raise ValueError("the fused gather needs rows of every linear on every rank")
+            G = len(self.groups)
+            self.plan = _shard.PeerGather([self.slot[i % G] for i in range(len(layers) * G)], 1, torch.bfloat16,
+                                          rank, world, device)
+
+    def close(self):
+        if self.plan is not None:
+            self.plan.close()
+            self.plan = None
 
     def inputs(self, gi):
         name, _, C = self.groups[gi][1][0]
@@ -251,8 +268,17 @@ class Chain:
 
         from drinkme_b200 import radix_ops
 
+        G = len(self.groups)
+        n = len(self.layers) * G
         for li, row in enumerate(self.layers):
             for gi, rt in enumerate(row):
+                if self.plan is not None:
+                    # this rank's rows into every rank's gathered output; wait
+                    # for the previous linear's gather before reading x
+                    i = li * G + gi
+                    self.plan.gemv(rt, self.inputs(gi), i, wait=(i - 1) % n)
+                    self.last = self.plan.output(i)
+                    continue
                 out = self.outs[li][gi]
                 if rt is not None:
                     radix_ops.gemv_into(rt, self.inputs(gi), None, out[:, :rt["R"]])
@@ -463,7 +489,8 @@ def main():
             wl["layers"] = a.layers
     spec = WORKLOADS[a.workload]
     base_config = {"workload": f"{a.workload} decode linear stack, batch 1, sip, row-sharded over {world} GPU(s)"
-                               + ("" if a.no_fuse else "; q|k|v and gate|up fused launches"),
+                               + ("" if a.no_fuse else "; q|k|v and gate|up fused launches")
+                               + ("" if world == 1 else f"; output gather: {a.gather}"),
                    "model_shape": a.workload, "layers": spec["layers"], "global_batch": 1,
                    "parallelism": f"rows{world}", "l2": "inputs larger than L2 (stack >> 126 MB)"}
 
@@ -500,7 +527,7 @@ def main():
 
     fuse = not a.no_fuse
     layers, stats = build_stack(a.workload, rank, world, device, a.variants, log, fuse)
-    chain = Chain(a.workload, layers, rank, world, device, fuse=fuse)
+    chain = Chain(a.workload, layers, rank, world, device, fuse=fuse, gather=a.gather)
     clocks = ClockSampler(local)
     clocks.start()
     ms, _ = time_graph(chain, a.steps, a.warmup, world, rank, device)
@@ -572,6 +599,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        chain.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -14,10 +14,12 @@ LIB_PATH = os.path.join(HERE, "libdrinkme_b200.so")
 DM_OK, DM_EINVAL, DM_ECUDA, DM_EDEVICE, DM_ENOMEM = 0, 1, 2, 3, 4
 DM_BF16, DM_F32 = 0, 1
 DM_MC_MAX = 8
+DM_MAX_RANKS = 8
 
 EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
-           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check")
+           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check",
+           "dm_gemv_gather", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
 
 
 class DrinkmeError(RuntimeError):
@@ -41,6 +43,14 @@ class PackPart(ct.Structure):
                 ("noffsets", ct.c_size_t), ("host_data", ct.c_void_p), ("nwords", ct.c_size_t),
                 ("R", ct.c_int64), ("C", ct.c_int64), ("host_widths", ct.c_void_p), ("nwidths", ct.c_int32),
                 ("block_size", ct.c_int32), ("row_begin", ct.c_int64), ("row_end", ct.c_int64)]
+
+
+class Gather(ct.Structure):
+    """dm_gather: the fused NVLink output gather of one row-sharded linear."""
+    _fields_ = [("world", ct.c_int32), ("rank", ct.c_int32), ("slot", ct.c_int64),
+                ("peer_out", ct.c_void_p * DM_MAX_RANKS), ("peer_flags", ct.c_void_p * DM_MAX_RANKS),
+                ("gen", ct.c_void_p), ("done", ct.c_void_p), ("wait_flags", ct.c_void_p), ("wait_gen", ct.c_void_p),
+                ("abort", ct.c_void_p)]
 
 
 _LIB = None
@@ -70,6 +80,12 @@ def lib():
         L.dm_pack_plan.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, ct.POINTER(ct.c_uint64), cp, sz]
         L.dm_pack_encode.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, p, ct.c_uint64, cp, sz]
         L.dm_tensor_check.argtypes = [p, ct.POINTER(ct.c_int32), cp, sz]
+        L.dm_gemv_gather.argtypes = [p, p, i64, p, i32, ct.POINTER(Gather), p, cp, sz]
+        L.dm_ipc_handle.argtypes = [p, p, cp, sz]
+        L.dm_ipc_open.argtypes = [p, i32, ct.POINTER(p), cp, sz]
+        L.dm_ipc_close.argtypes = [p, cp, sz]
+        L.dm_device_alloc.argtypes = [i32, sz, ct.POINTER(p), cp, sz]
+        L.dm_device_free.argtypes = [p, cp, sz]
         for name in EXPORTS:
             getattr(L, name).restype = ct.c_int
         _LIB = L

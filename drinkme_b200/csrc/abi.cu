@@ -317,3 +317,77 @@ extern "C" int dm_tensor_check(const dm_tensor *t, int32_t *device_error, char *
     *device_error = v;
     return DM_OK;
 }
+
+extern "C" int dm_gemv_gather(const dm_tensor *t, const void *x, int64_t M, const void *bias, int32_t out_dtype,
+                              const dm_gather *g, void *stream, char *err, size_t err_len) {
+    if (!t || !x || !g) return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: null pointer");
+    if (M < 1 || M > DM_MC_MAX)
+        return fail(err, err_len, DM_EINVAL,
+                    "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
+    if (out_dtype != DM_BF16 && out_dtype != DM_F32)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: dtype must be DM_BF16 or DM_F32");
+    if (!t->L.fast_sip) return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: needs a sip tensor (the fast path)");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: activations must be 16-byte aligned");
+    if (g->world < 1 || g->world > DM_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: rank outside a world of 1.." + std::to_string(DM_MAX_RANKS));
+    if (g->slot < t->L.rows) return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: slot smaller than this rank's rows");
+    for (int r = 0; r < g->world; ++r)
+        if (!g->peer_out[r] || !g->peer_flags[r]) return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: null peer pointer");
+    if (!g->gen || !g->done || !g->abort || (!g->wait_flags) != (!g->wait_gen))
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_gather: counters / wait words incomplete");
+    DeviceGuard guard(t->device);
+    std::string msg;
+    int rc = dm::launch_gemv_sip_with(t, reinterpret_cast<const uint16_t *>(x), t->L.C, (int)M, 1, (int)M,
+                                      reinterpret_cast<const uint16_t *>(bias), nullptr, out_dtype == DM_F32,
+                                      t->S.partials, t->S.counters, t->S.err, t->S.max_workers, stream, msg, g);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_ipc_handle(const void *dptr, uint8_t *out64, char *err, size_t err_len) {
+    if (!dptr || !out64) return fail(err, err_len, DM_EINVAL, "dm_ipc_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(dptr));
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(out64, &h, 64);
+    return DM_OK;
+}
+
+extern "C" int dm_ipc_open(const uint8_t *handle64, int32_t device, void **dptr, char *err, size_t err_len) {
+    if (!handle64 || !dptr) return fail(err, err_len, DM_EINVAL, "dm_ipc_open: null pointer");
+    DeviceGuard g(device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle64, 64);
+    cudaError_t e = cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaIpcOpenMemHandle");
+    return DM_OK;
+}
+
+extern "C" int dm_ipc_close(void *dptr, char *err, size_t err_len) {
+    if (!dptr) return fail(err, err_len, DM_EINVAL, "dm_ipc_close: null pointer");
+    cudaError_t e = cudaIpcCloseMemHandle(dptr);
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaIpcCloseMemHandle");
+    return DM_OK;
+}
+
+extern "C" int dm_device_alloc(int32_t device, size_t bytes, void **dptr, char *err, size_t err_len) {
+    if (!dptr || bytes == 0) return fail(err, err_len, DM_EINVAL, "dm_device_alloc: null pointer or no bytes");
+    DeviceGuard g(device);
+    cudaError_t e = cudaMalloc(dptr, bytes);
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaMalloc");
+    if ((e = cudaMemset(*dptr, 0, bytes)) != cudaSuccess) {
+        cudaFree(*dptr);
+        *dptr = nullptr;
+        return cuda_fail(err, err_len, e, "cudaMemset");
+    }
+    return DM_OK;
+}
+
+extern "C" int dm_device_free(void *dptr, char *err, size_t err_len) {
+    if (!dptr) return fail(err, err_len, DM_EINVAL, "dm_device_free: null pointer");
+    cudaError_t e = cudaFree(dptr);
+    if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaFree");
+    return DM_OK;
+}

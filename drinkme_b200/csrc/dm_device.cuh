@@ -13,6 +13,7 @@ namespace dm {
 constexpr int kErrWaitFull = 1;    // a consumer gave up waiting for a staged unit
 constexpr int kErrWaitEmpty = 2;   // the producer gave up waiting for a slot
 constexpr int kErrWaitDrain = 3;   // the producer gave up draining its copies at exit
+constexpr int kErrWaitPeer = 4;    // a wait for another GPU's output flag gave up
 
 // Upper bound on polls of one mbarrier phase. Each poll suspends the warp in
 // hardware for up to kSuspendNs (it resumes as soon as the phase completes),
@@ -20,6 +21,9 @@ constexpr int kErrWaitDrain = 3;   // the producer gave up draining its copies a
 // two seconds, after which the kernel records an error and returns instead of
 // waiting forever.
 constexpr uint32_t kWaitPolls = 1u << 16;
+// A wait for another GPU's flag: 2^23 polls about 128 ns apart, about a
+// second, then error kErrWaitPeer.
+constexpr uint32_t kPeerPolls = 1u << 23;
 constexpr uint32_t kSuspendNs = 32768;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -75,6 +79,35 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+
+// Acquire / release accesses of flag words another GPU writes or reads.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders generic-proxy accesses of global memory (e.g. another GPU's stores
+// made visible by an acquire) before this thread's later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, a multiple
+// of 16 bytes; no data is returned, nothing completes on a barrier).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses of shared memory
+// before its later async-proxy ones (a bulk copy into a slot just read).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Programmatic dependent launch: let the next kernel in the stream start its
 // CTAs (on SMs this grid leaves free) before this grid ends ...

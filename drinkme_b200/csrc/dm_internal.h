@@ -114,6 +114,7 @@ int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f3
 int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int dir_cap);
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
-                         int64_t max_workers, void *stream, std::string &msg);
+                         int64_t max_workers, void *stream, std::string &msg,
+                         const dm_gather *gather = nullptr);
 
 }  // namespace dm

@@ -70,6 +70,18 @@ struct SipArgs {
     int *counters;    // [tiles], zero between launches
     int *err;
     int32_t slot_bytes, x_off, nslots, dir_cap;
+    // row-sharded outputs gathered over NVLink (world > 0): every output is
+    // also stored into each rank's gathered buffer [M][world * slot] at
+    // rank * slot + row; the last CTA then raises each rank's flag of this
+    // linear to the new launch count. Before staging activations, every CTA
+    // waits for the flags of the linear its input depends on.
+    int32_t world, rank;
+    int64_t gslot;
+    void *peer_out[DM_MAX_RANKS];
+    uint32_t *peer_flags[DM_MAX_RANKS];
+    uint32_t *gen, *done;
+    const uint32_t *wait_flags, *wait_gen;
+    uint32_t *abort;
 };
 
 // A GROUP of kGroupWarps consumer warps shares each staged unit: warp w of
@@ -159,10 +171,55 @@ __device__ __forceinline__ void store_output(const SipArgs &a, int64_t tile, int
     float y = S(m * a.nsplit * 16 + r);
     for (int s = 1; s < a.nsplit; ++s) y += S((m * a.nsplit + s) * 16 + r);
     if (a.bias) y += bf16_bits_to_f32(a.bias[row]);
+    if (a.world > 0) {
+        // into every rank's gathered output (this GPU's own included)
+        const int64_t at = (int64_t)m * a.world * a.gslot + (int64_t)a.rank * a.gslot + row;
+        if (a.out_f32) {
+            for (int r = 0; r < a.world; ++r) reinterpret_cast<float *>(a.peer_out[r])[at] = y;
+        } else {
+            const uint16_t b = f32_to_bf16_bits(y);
+            for (int r = 0; r < a.world; ++r) reinterpret_cast<uint16_t *>(a.peer_out[r])[at] = b;
+        }
+        return;
+    }
     if (a.out_f32)
         reinterpret_cast<float *>(a.out)[m * a.rows + row] = y;
     else
         reinterpret_cast<uint16_t *>(a.out)[m * a.rows + row] = f32_to_bf16_bits(y);
+}
+
+// The wait for the flags of the linear this launch's input depends on: each
+// rank's flag word reaches this rank's own launch count of that linear
+// (bounded; gives up with an error code).
+__device__ __forceinline__ void wait_inputs(const SipArgs &a) {
+    if (a.world <= 0 || a.wait_flags == nullptr) return;
+    const uint32_t want = ld_acquire_gpu(a.wait_gen);
+    for (int r = 0; r < a.world; ++r) {
+        uint32_t i = 0;
+        while ((int32_t)(ld_acquire_sys(a.wait_flags + r) - want) < 0) {
+            // a rank gave up before: do not wait again
+            if (++i > kPeerPolls || (i % 64 == 0 && ld_acquire_gpu(a.abort) != 0u)) {
+                atomicExch(a.err, kErrWaitPeer);
+                atomicExch(a.abort, 1u);
+                return;
+            }
+            __nanosleep(128);
+        }
+    }
+    fence_proxy_async_global();
+}
+
+// After this CTA's last output: the CTA count of the launch; the last CTA
+// raises every rank's flag of this linear to the new launch count.
+__device__ __forceinline__ void signal_outputs(const SipArgs &a) {
+    if (a.world <= 0) return;
+    __threadfence_system();  // this CTA's stores (local and peer) before its count
+    if (atomicAdd(a.done, 1u) + 1u != gridDim.x) return;
+    __threadfence_system();
+    *a.done = 0u;
+    const uint32_t g = *a.gen + 1u;
+    *a.gen = g;
+    for (int r = 0; r < a.world; ++r) st_release_sys(a.peer_flags[r] + a.rank, g);
 }
 
 __device__ __forceinline__ void group_sync(int group) {
@@ -282,6 +339,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
             const int32_t first = std::min<int32_t>(S, q.n);
             for (int32_t p = 0; p < first; ++p) stage_w(p, p);
             pdl_wait();
+            wait_inputs(a);
             for (int32_t p = 0; p < first; ++p) stage_x(p, p);
             int slot = 0;
             uint32_t epar = 0;  // parity of the empty phase to wait for
@@ -372,6 +430,8 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                 __syncwarp();
             }
         }
+        __syncwarp();
+        if (lane == 0) signal_outputs(a);
         return;
     }
 
@@ -544,7 +604,7 @@ int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, i
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                     const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg) {
     return launch_gemv_sip_with(t, xv, x_stride, Mv, nsplit, M_out, bias, out, out_f32, t->S.partials,
-                                t->S.counters, t->S.err, t->S.max_workers, stream, msg);
+                                t->S.counters, t->S.err, t->S.max_workers, stream, msg, nullptr);
 }
 
 // The launch with caller-supplied scratch (partials for `max_workers`
@@ -552,7 +612,7 @@ int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, in
 // dm_gemv passes the tensor's own, dm_gemv_noalloc a static device array.
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
-                         int64_t max_workers, void *stream, std::string &msg) {
+                         int64_t max_workers, void *stream, std::string &msg, const dm_gather *gather) {
     const dm::TensorLayout &L = t->L;
     if (Mv < 1 || Mv > kMaxVirtualRows) {
         msg = "sip kernel: 1..8 virtual activation rows";
@@ -608,6 +668,20 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.x_off = (L.max_unit_bytes + 127) & ~127;
     a.nslots = nslots;
     a.dir_cap = dir_cap;
+    if (gather) {
+        a.world = gather->world;
+        a.rank = gather->rank;
+        a.gslot = gather->slot;
+        for (int r = 0; r < gather->world; ++r) {
+            a.peer_out[r] = gather->peer_out[r];
+            a.peer_flags[r] = gather->peer_flags[r];
+        }
+        a.gen = gather->gen;
+        a.done = gather->done;
+        a.wait_flags = gather->wait_flags;
+        a.wait_gen = gather->wait_gen;
+        a.abort = gather->abort;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(kSipThreads);

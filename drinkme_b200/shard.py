@@ -97,3 +97,131 @@ class ShardedRadixLinear(torch.nn.Module):
 def local_gemv_into(rt: dict, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """This rank's slice of a sharded linear into a caller-owned buffer."""
     return radix_ops.gemv_into(rt, x, None, out)
+
+
+# ------------------------------------------------- fused NVLink gather --
+
+def _device_view(ptr: int, shape, dtype: torch.dtype) -> torch.Tensor:
+    """A torch tensor over device memory this package allocated (zero copy,
+    through the CUDA array interface; bf16 travels as int16)."""
+    code = {torch.bfloat16: "<i2", torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+
+    class _Raw:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": code, "data": (int(ptr), False),
+                                    "version": 3, "strides": None}
+
+    t = torch.as_tensor(_Raw(), device="cuda")
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+
+
+class PeerGather:
+    """The gathered outputs of a sequence of row-sharded linears on the GPUs
+    of one box: per linear a buffer [M][world * slot] on every rank, which
+    every rank's GEMV writes its rows into over NVLink (plain peer stores,
+    CUDA IPC mappings; no multicast), and per linear `world` flag words the
+    writers raise to their launch count. dm_gemv_gather fuses both into the
+    GEMV; linear i may wait for linear `wait` before reading its activations.
+
+    All ranks build it collectively (the IPC handles travel over `group`)
+    with the same `slots`; close() (collective) unmaps and frees it."""
+
+    def __init__(self, slots, M: int, out_dtype, rank: int, world: int, device, group=None):
+        import ctypes as ct
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if not 1 <= world <= _lib.DM_MAX_RANKS:
+            raise ValueError(f"PeerGather: world {world} outside 1..{_lib.DM_MAX_RANKS}")
+        self.slots = [int(s) for s in slots]
+        self.M, self.rank, self.world, self.group = int(M), int(rank), int(world), group
+        self.dtype = out_dtype
+        self.device = torch.device(device)
+        esz = 4 if out_dtype == torch.float32 else 2
+        off, at = [], 0
+        for s in self.slots:
+            off.append(at)
+            at += -(-self.M * self.world * s * esz // 256) * 256
+        self.flag_off = at  # per linear: world flag words, 64-byte aligned
+        at += len(self.slots) * 64 * (-(-self.world * 4 // 64))
+        self.cnt_off = at  # per linear: gen, done (this rank's own); then the abort word
+        at += len(self.slots) * 8 + 4
+        self.out_off, self.bytes = off, -(-at // 256) * 256
+        base = ct.c_void_p()
+        _lib.call("dm_device_alloc", self.device.index, self.bytes, ct.byref(base))
+        self.base = base.value
+        h = (ct.c_uint8 * 64)()
+        _lib.call("dm_ipc_handle", ct.c_void_p(self.base), h)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, bytes(h), group=group)
+        self.peer_base = []
+        for r in range(self.world):
+            if r == self.rank:
+                self.peer_base.append(self.base)
+                continue
+            hp = (ct.c_uint8 * 64).from_buffer_copy(handles[r])
+            p = ct.c_void_p()
+            _lib.call("dm_ipc_open", hp, self.device.index, ct.byref(p))
+            self.peer_base.append(p.value)
+
+    def _flags(self, base: int, i: int) -> int:
+        return base + self.flag_off + i * 64 * (-(-self.world * 4 // 64))
+
+    def desc(self, i: int, wait: int | None = None):
+        """The dm_gather of linear i (waiting for linear `wait` first)."""
+        from . import _lib
+
+        g = _lib.Gather()
+        g.world, g.rank, g.slot = self.world, self.rank, self.slots[i]
+        for r in range(self.world):
+            g.peer_out[r] = self.peer_base[r] + self.out_off[i]
+            g.peer_flags[r] = self._flags(self.peer_base[r], i)
+        g.gen = self.base + self.cnt_off + 8 * i
+        g.done = self.base + self.cnt_off + 8 * i + 4
+        g.abort = self.base + self.cnt_off + 8 * len(self.slots)
+        if wait is not None:
+            g.wait_flags = self._flags(self.base, wait)
+            g.wait_gen = self.base + self.cnt_off + 8 * wait
+        return g
+
+    def output(self, i: int) -> torch.Tensor:
+        """This rank's gathered output of linear i, [M, world * slot]
+        (rank k's rows at [k * slot, k * slot + rows_k))."""
+        return _device_view(self.base + self.out_off[i], (self.M, self.world * self.slots[i]), self.dtype)
+
+    def gemv(self, rt: dict, x: torch.Tensor, i: int, wait: int | None = None, bias=None) -> None:
+        """This rank's rows of linear i (runtime dict `rt`), gathered into every
+        rank's output(i) and published; the activations `x` [M, C] bf16."""
+        import ctypes as ct
+
+        from . import _lib
+
+        h = rt["rx_handle"]
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("PeerGather.gemv: activations must be contiguous bf16")
+        b = bias.to(device=x.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
+        _lib.call("dm_gemv_gather", h.ptr, ct.c_void_p(x.data_ptr()), x.shape[0],
+                  ct.c_void_p(b.data_ptr() if b is not None else 0), _lib.DM_F32 if self.dtype == torch.float32
+                  else _lib.DM_BF16, ct.byref(self.desc(i, wait)),
+                  ct.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
+
+    def close(self) -> None:
+        """Collective: every rank stops using the others' memory, then unmaps."""
+        import ctypes as ct
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for r, p in enumerate(self.peer_base):
+            if r != self.rank:
+                _lib.call("dm_ipc_close", ct.c_void_p(p))
+        _lib.call("dm_device_free", ct.c_void_p(self.base))
+        self.base = None

@@ -43,6 +43,9 @@ extern "C" {
  * multi-column kernel (radix_ops.py:379-398 refuses M outside 1..8). */
 #define DM_MC_MAX 8
 
+/* The most ranks (GPUs of one box) a row-sharded linear gathers over. */
+#define DM_MAX_RANKS 8
+
 typedef struct dm_tensor dm_tensor; /* opaque device-resident radix tensor */
 
 typedef struct dm_tensor_info {
@@ -143,6 +146,50 @@ int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const
  * that overlap on the GPU (on any tensor, any stream) race. */
 int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
                     int32_t out_dtype, void *stream, char *err, size_t err_len);
+
+/* The output gather of a row-sharded linear over NVLink, fused into its GEMV
+ * (the exchange the reference lacks: it has no multi-GPU code; this replaces
+ * an all-gather after each shard's dm_gemv). Rank `rank` of `world` holds
+ * rows [rank * slot, rank * slot + rows) of the linear (its dm_tensor, made
+ * with that row range or as a fused tensor of such ranges). Every rank owns a
+ * gathered output buffer [M][world * slot] and `world` flag words for this
+ * linear, and maps every other rank's (dm_ipc_open); the arrays below give
+ * them in this process's address space, index = rank. `gen` and `done` are
+ * this rank's own zero-initialised words for this linear. With `wait_flags`
+ * and `wait_gen` (this rank's flag words and launch count of the linear the
+ * activations depend on) the kernel first waits, bounded, until every rank
+ * has published that linear's output. */
+typedef struct dm_gather {
+    int32_t world, rank;
+    int64_t slot;
+    void *peer_out[DM_MAX_RANKS];
+    uint32_t *peer_flags[DM_MAX_RANKS];
+    uint32_t *gen, *done;
+    const uint32_t *wait_flags, *wait_gen;
+    uint32_t *abort; /* this rank's word, shared by all its linears: set when a wait gives up; later waits then return at once */
+} dm_gather;
+
+/* dm_gemv of this rank's rows, the outputs stored into every rank's
+ * gathered buffer at [m][rank * slot + row] (no local `out`), then every
+ * rank's flag word `rank` of this linear raised to the new launch count.
+ * bf16 activations (16-byte aligned), 1 <= M <= 8, a sip tensor; one kernel
+ * launch, no host synchronisation (CUDA-graph capturable). A wait that gave
+ * up is reported by dm_tensor_check. Kernels of different ranks wait on one
+ * another: run one rank per GPU. */
+int dm_gemv_gather(const dm_tensor *t, const void *x, int64_t M, const void *bias, int32_t out_dtype,
+                   const dm_gather *g, void *stream, char *err, size_t err_len);
+
+/* CUDA IPC of a device allocation (plain peer mappings; no multicast):
+ * the 64-byte handle of `dptr` (the start of a cudaMalloc block), and the
+ * mapping of a peer's handle on `device` (closed by dm_ipc_close). */
+int dm_ipc_handle(const void *dptr, uint8_t *out64, char *err, size_t err_len);
+int dm_ipc_open(const uint8_t *handle64, int32_t device, void **dptr, char *err, size_t err_len);
+int dm_ipc_close(void *dptr, char *err, size_t err_len);
+
+/* Device memory for gather buffers and flags: cudaMalloc'd and zeroed (the
+ * start of the block is what dm_ipc_handle exports). */
+int dm_device_alloc(int32_t device, size_t bytes, void **dptr, char *err, size_t err_len);
+int dm_device_free(void *dptr, char *err, size_t err_len);
 
 /* The shard's decoded bf16 bit patterns, uint16 [rows, C] — replaces
  * radix_ops.decode_bits (src/drinkme/codec/radix_ops.py:418-427). For a
