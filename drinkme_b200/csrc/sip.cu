@@ -70,6 +70,7 @@ struct SipArgs {
     int *counters;    // [tiles], zero between launches
     int *err;
     int32_t slot_bytes, x_off, nslots, dir_cap;
+    int32_t tile_split;  // 1: CTAs own whole tiles (no tile is shared), else units are split evenly
     // row-sharded outputs gathered over NVLink (world > 0): every output is
     // also stored into each rank's gathered buffer [M][world * slot] at
     // rank * slot + row; the last CTA then raises each rank's flag of this
@@ -209,13 +210,15 @@ __device__ __forceinline__ void wait_inputs(const SipArgs &a) {
     fence_proxy_async_global();
 }
 
-// After this CTA's last output: the CTA count of the launch; the last CTA
-// raises every rank's flag of this linear to the new launch count.
+// After this CTA's last output (called by one lane, after a __syncwarp of
+// the warp that stored them): the CTA count of the launch; the last CTA,
+// having acquired every count, raises every rank's flag of this linear to
+// the new launch count with a system-scope release.
 __device__ __forceinline__ void signal_outputs(const SipArgs &a) {
     if (a.world <= 0) return;
-    __threadfence_system();  // this CTA's stores (local and peer) before its count
-    if (atomicAdd(a.done, 1u) + 1u != gridDim.x) return;
-    __threadfence_system();
+    // the count needs GPU scope only: the last CTA's system-scope release
+    // below carries every CTA's stores (ordered before it here) to the peers
+    if (atom_add_acq_rel_gpu(a.done, 1u) + 1u != gridDim.x) return;
     *a.done = 0u;
     const uint32_t g = *a.gen + 1u;
     *a.gen = g;
@@ -293,7 +296,9 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     float *ebuf = tslot + kTileRing * kGroups * kP;               // [kP] the epilogue's tile sum
     uint32_t *dir = reinterpret_cast<uint32_t *>(ebuf + kP);     // this CTA's unit starts
     const int64_t U = a.units, W = gridDim.x, NB = a.NB;
-    const int64_t cu0 = range_start(blockIdx.x, U, W), cu1 = range_start(blockIdx.x + 1, U, W);
+    const int64_t T = (U + NB - 1) / NB;
+    const int64_t cu0 = a.tile_split ? range_start(blockIdx.x, T, W) * NB : range_start(blockIdx.x, U, W);
+    const int64_t cu1 = a.tile_split ? range_start(blockIdx.x + 1, T, W) * NB : range_start(blockIdx.x + 1, U, W);
     const bool dir_in_smem = (cu1 - cu0 + 1) <= a.dir_cap;
     Seq q;
     q.init(cu0, cu1, NB);
@@ -393,21 +398,18 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
 #pragma unroll
                 for (int i = 0; i < (kP + 31) / 32; ++i)
                     if (lane + 32 * i < kP) mine[lane + 32 * i] = T[i];
-                __threadfence();
+                // the warp's partial, released by lane 0's count; the last to
+                // count acquires every other CTA's partial with it
                 __syncwarp();
                 const int64_t cf = worker_of(tl * NB, U, W), cl = worker_of((tl + 1) * NB - 1, U, W);
                 int last = 0;
                 if (lane == 0) {
-                    const int old = atomicAdd(&a.counters[tl], 1);
-                    last = (old == (int)(cl - cf));
-                    if (last) {
-                        __threadfence();
-                        a.counters[tl] = 0;
-                    }
+                    const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + tl), 1u);
+                    last = (old == (uint32_t)(cl - cf));
+                    if (last) a.counters[tl] = 0;
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
-                    __threadfence();
                     for (int64_t c = cf; c <= cl; ++c) {
                         const int sc = (tl == range_start(c, U, W) / NB) ? 0 : 1;
                         const float *pp = a.partials + (c * 2 + sc) * 128;
@@ -618,15 +620,25 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         msg = "sip kernel: 1..8 virtual activation rows";
         return DM_EINVAL;
     }
-    // one CTA per SM, each a stream-K worker owning at least one unit: the
-    // split depends on the tensor alone
-    const int64_t grid = std::min<int64_t>(t->sms, L.units);
+    // One CTA per SM, each a stream-K worker owning at least one unit; or,
+    // when the units are too few for the CTAs to own whole tiles (every tile
+    // would be shared and every launch would end in the cross-CTA fixup),
+    // CTAs that own whole tiles whenever that costs no more decode rounds
+    // than the fixup. The split depends on the tensor alone.
+    const int64_t tiles = L.tiles;
+    const int64_t gridA = std::min<int64_t>(t->sms, L.units), gridB = std::min<int64_t>(t->sms, tiles);
+    const int64_t perA = (L.units + gridA - 1) / gridA;
+    const int64_t roundsA = (perA + kGroups - 1) / kGroups + (perA < 2 * L.NB ? 2 : 0);  // + the fixup at the end
+    const int64_t roundsB = (tiles + gridB - 1) / gridB * ((L.NB + kGroups - 1) / kGroups);
+    const int tile_split = roundsB <= roundsA ? 1 : 0;
+    const int64_t grid = tile_split ? gridB : gridA;
     if (grid > max_workers) {
         msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
               std::to_string(max_workers);
         return DM_EINVAL;
     }
-    const int dir_cap = (int)std::min<int64_t>(4096, (L.units + grid - 1) / grid + 2);
+    const int64_t per_cta = tile_split ? (tiles + grid - 1) / grid * L.NB : perA;
+    const int dir_cap = (int)std::min<int64_t>(4096, per_cta + 2);
     int slot_bytes = 0, nslots = 0;
     const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, dir_cap);
     if (smem < 0) {
@@ -668,6 +680,7 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.x_off = (L.max_unit_bytes + 127) & ~127;
     a.nslots = nslots;
     a.dir_cap = dir_cap;
+    a.tile_split = tile_split;
     if (gather) {
         a.world = gather->world;
         a.rank = gather->rank;
