@@ -34,7 +34,8 @@ class TensorInfo(ct.Structure):
     _fields_ = [("R", ct.c_int64), ("C", ct.c_int64), ("row_begin", ct.c_int64), ("rows", ct.c_int64),
                 ("block_size", ct.c_int32), ("nwidths", ct.c_int32), ("widths", ct.c_int32 * 8),
                 ("nblocks", ct.c_int64), ("payload_words", ct.c_int64), ("read_bytes", ct.c_int64),
-                ("resident_bytes", ct.c_int64), ("fast_path", ct.c_int32), ("device", ct.c_int32)]
+                ("resident_bytes", ct.c_int64), ("fast_path", ct.c_int32), ("device", ct.c_int32),
+                ("device_bytes_per_call", ct.c_int64)]
 
 
 class PackPart(ct.Structure):

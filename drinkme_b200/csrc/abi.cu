@@ -63,16 +63,82 @@ extern "C" int dm_version(void) { return 100; }
 
 namespace {
 
+// A pack of another radix profile (gulp, balanced, ...) with whole
+// 1024-weight blocks, re-encoded as sip: the loader decodes its rows to the
+// exact bf16 bits and this library's encoder (dm_pack_plan/encode) packs
+// them again with widths (3, 8), so the sip kernels serve it. The decoded
+// weights are the same bits; the device bytes differ from the source pack's
+// by a few percent. Returns false (serve the pack as given) when the profile
+// is already sip, the blocks do not fit the sip kernels, or sip would take
+// more than 5/4 of the source words.
+struct Transcoded {
+    std::vector<uint8_t> pal;
+    std::vector<uint32_t> off, data;
+    int32_t widths[2] = {3, 8};
+};
+
+bool transcode_to_sip(const dm::PackPart &P, Transcoded &o, dm::PackPart &out) {
+    if (P.nw == 2 && P.widths[0] == 3 && P.widths[1] == 8) return false;
+    if (P.B != 1024 || P.C % 1024 != 0) return false;
+    const int64_t rows = P.row1 - P.row0, NB = P.C / 1024;
+    std::vector<uint16_t> bits((size_t)(rows * P.C));
+    dm::decode_rows(P, bits.data());
+    o.pal.assign(7, 0);
+    o.off.assign((size_t)(rows * NB + 1), 0);
+    uint64_t nwords = 0;
+    char e[256];
+    if (dm_pack_plan(bits.data(), rows, P.C, o.widths, 2, 1024, 0, o.pal.data(), o.off.data(), &nwords, e,
+                     sizeof e) != DM_OK)
+        return false;
+    int64_t src_words = 0;
+    dm::pack_read_bytes(P, &src_words);
+    if ((int64_t)nwords * 4 > src_words * 5) return false;
+    o.data.assign((size_t)nwords, 0);
+    if (dm_pack_encode(bits.data(), rows, P.C, o.widths, 2, 1024, 0, o.pal.data(), o.off.data(), o.data.data(),
+                       nwords, e, sizeof e) != DM_OK)
+        return false;
+    out = dm::PackPart{o.pal.data(), o.pal.size(), o.off.data(), o.off.size(), o.data.data(), o.data.size(), rows,
+                       P.C, o.widths, 2, 1024, 0, rows};
+    return true;
+}
+
 // Lays `parts` out, copies the layout to `device` and sizes the scratch.
-int create_from_parts(const dm::PackPart *parts, int nparts, int32_t device, dm_tensor **out, char *err,
+int create_from_parts(const dm::PackPart *given, int nparts, int32_t device, dm_tensor **out, char *err,
                       size_t err_len) {
     std::string msg;
     dm_tensor *t = new dm_tensor();
     t->device = device;
     std::string bytes, unit16;
-    if (dm::build_layout(parts, nparts, t->L, bytes, unit16, msg)) {
+    // the source packs' own read bytes and payload words (the reference's count)
+    int64_t src_read = 0, src_words = 0;
+    for (int i = 0; i < nparts; ++i) {
+        int64_t w = 0;
+        src_read += dm::pack_read_bytes(given[i], &w);
+        src_words += w;
+    }
+    std::vector<Transcoded> owned((size_t)nparts);
+    std::vector<dm::PackPart> parts(given, given + nparts);
+    bool transcoded = false;
+    for (int i = 0; i < nparts; ++i) transcoded |= transcode_to_sip(given[i], owned[i], parts[i]);
+    if (transcoded)
+        for (int i = 0; i < nparts; ++i)
+            if (!(parts[i].nw == 2 && parts[i].widths[0] == 3)) {  // all parts sip, or none re-encoded
+                parts.assign(given, given + nparts);
+                transcoded = false;
+                break;
+            }
+    if (dm::build_layout(parts.data(), nparts, t->L, bytes, unit16, msg)) {
         delete t;
         return fail(err, err_len, DM_EINVAL, msg);
+    }
+    t->L.dev_read_bytes = t->L.read_bytes;
+    if (transcoded) {
+        t->L.src_nw = given[0].nw;
+        for (int i = 0; i < given[0].nw; ++i) t->L.src_widths[i] = given[0].widths[i];
+        t->L.read_bytes = src_read;
+        t->L.payload_words = src_words;
+        t->L.R = nparts == 1 ? given[0].R : t->L.R;
+        t->L.row0 = nparts == 1 ? given[0].row0 : 0;
     }
     DeviceGuard g(device);
     cudaError_t e;
@@ -212,8 +278,10 @@ extern "C" int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info) {
     info->row_begin = t->L.row0;
     info->rows = t->L.rows;
     info->block_size = t->L.B;
-    info->nwidths = t->L.nw;
-    for (int i = 0; i < 8; ++i) info->widths[i] = t->L.widths[i];
+    // the pack's own profile (a re-encoded pack reports the widths it came with)
+    info->nwidths = t->L.src_nw ? t->L.src_nw : t->L.nw;
+    for (int i = 0; i < 8; ++i) info->widths[i] = t->L.src_nw ? t->L.src_widths[i] : t->L.widths[i];
+    info->device_bytes_per_call = t->L.src_nw ? t->L.dev_read_bytes : t->L.read_bytes;
     info->nblocks = t->L.rows * t->L.NB;
     info->payload_words = t->L.payload_words;
     info->read_bytes = t->L.read_bytes;

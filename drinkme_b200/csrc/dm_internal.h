@@ -50,12 +50,15 @@ struct PackPart {
 struct TensorLayout {
     int64_t R = 0, C = 0, row0 = 0, rows = 0;
     int32_t nparts = 1;
+    // the packs' own profile when the loader re-encoded them as sip (0: as given)
+    int32_t src_nw = 0, src_widths[8] = {0};
     int32_t B = 0, nw = 0, widths[8] = {0};
     int32_t covered = 0;
     uint8_t palette[256] = {0};
     int64_t NB = 0, tiles = 0, units = 0;
     int64_t payload_words = 0;  // NW of this shard
-    int64_t read_bytes = 0;
+    int64_t read_bytes = 0;      // radix_ops.read_bytes of the source pack(s)
+    int64_t dev_read_bytes = 0;  // the same count over the layout the kernels stream
     bool fast_sip = false;
     int32_t max_unit_bytes = 0;
     // padded palette words (radix_pack.padded_palette_words): nonterminal tiers,
@@ -97,6 +100,8 @@ int validate_pack(const uint8_t *palette, size_t npal, const uint32_t *offsets, 
 int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string &bytes, std::string &unit16,
                  std::string &msg);
 int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
+void decode_rows(const PackPart &P, uint16_t *out);
+int64_t pack_read_bytes(const PackPart &P, int64_t *payload_words);
 int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw);
 
 // Kernel launchers (kernels.cu)

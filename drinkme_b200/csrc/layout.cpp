@@ -143,6 +143,65 @@ static int sip_escapes(const uint32_t *tier0, uint16_t *out) {
     return count;
 }
 
+// One block of any radix profile decoded to bf16 bit patterns (radix.py:
+// 241-278, the reference's CPU decode): the literal plane, then per
+// nonterminal tier the codes of the weights still active (an escape code
+// passes the weight on to the next tier), then the terminal exponents.
+// Words the block does not hold read as zero.
+static void decode_block(const uint32_t *blk, int64_t words, int64_t n, const uint8_t *palette,
+                         const int32_t *widths, int32_t nw, uint16_t *out) {
+    uint32_t lit[4096], expo[4096];
+    int32_t active[4096];
+    int64_t pos = 0;
+    for (int64_t i = 0; i < n; ++i) lit[i] = field_at(blk, words, i, 8);
+    pos += cw(n, 8);
+    int64_t count = n, base = 0;
+    for (int64_t i = 0; i < n; ++i) active[i] = (int32_t)i;
+    for (int t = 0; t < nw - 1; ++t) {
+        const int32_t w = widths[t];
+        const uint32_t esc = (1u << w) - 1;
+        int64_t kept = 0;
+        for (int64_t i = 0; i < count; ++i) {
+            const uint32_t code = field_at(blk + pos, words - pos, i, w);
+            if (code == esc) {
+                active[kept++] = active[i];
+            } else {
+                expo[active[i]] = palette[base + code];
+            }
+        }
+        pos += cw(count, w);
+        base += esc;
+        count = kept;
+    }
+    for (int64_t i = 0; i < count; ++i) expo[active[i]] = field_at(blk + pos, words - pos, i, 8);
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = (uint16_t)((lit[i] & 0x7Fu) | ((lit[i] >> 7) << 15) | (expo[i] << 7));
+}
+
+// Rows [P.row0, P.row1) of a validated pack as bf16 bit patterns.
+void decode_rows(const PackPart &P, uint16_t *out) {
+    const int64_t NB = (P.C + P.B - 1) / P.B, rows = P.row1 - P.row0;
+    parallel_for(rows * NB, [&](int64_t i) {
+        const int64_t r = P.row0 + i / NB, b = i % NB, gb = r * NB + b;
+        const int64_t n = std::min<int64_t>(P.B, P.C - b * P.B);
+        const int64_t start = P.offsets[gb], words = (int64_t)P.offsets[gb + 1] - start;
+        decode_block(P.data + start, words, n, P.palette, P.widths, P.nw, out + (i / NB) * P.C + b * P.B);
+    });
+}
+
+// radix_ops.read_bytes (radix_ops.py:435-441) of rows [row0, row1) of a
+// pack: its payload words, its slice of the directory, the padded palette
+// words (radix_pack.py:333-350) and, for more than one nonterminal tier,
+// the uint16 schedule.
+int64_t pack_read_bytes(const PackPart &P, int64_t *payload_words) {
+    const int64_t NB = (P.C + P.B - 1) / P.B, b0 = P.row0 * NB, nb = (P.row1 - P.row0) * NB;
+    const int64_t words = (int64_t)P.offsets[b0 + nb] - (int64_t)P.offsets[b0];
+    int64_t pal_words = 0;
+    for (int i = 0; i < P.nw - 1; ++i) pal_words += (((1 << P.widths[i]) - 1) + 3) / 4;
+    if (payload_words) *payload_words = words;
+    return words * 4 + (nb + 1) * 4 + pal_words * 4 + (P.nw > 2 ? nb * 2 : 0);
+}
+
 // radix_pack.py:376-411 (schedule_np) for one block: byte (k-1) = word
 // length of nonterminal tier k (k >= 1); reads past `avail` are zero.
 static uint16_t block_schedule(const uint32_t *blk, int64_t avail, int64_t n, const int32_t *widths, int32_t nw) {

@@ -368,78 +368,154 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     }
 
     if (warp == 1 + kGroups * kGroupWarps) {
-        // ---------------------------------------------------- epilogue --
-        bool ok = true;
-        for (int32_t ts = 0; ts < q.ntiles; ++ts) {
-            const int ring = ts % kTileRing;
-            if (ok && !mbar_wait(&tfull[ring], (uint32_t)((ts / kTileRing) & 1), a.err, kErrWaitFull)) ok = false;
-            float T[(kP + 31) / 32];
-#pragma unroll
-            for (int i = 0; i < (kP + 31) / 32; ++i) {
-                const int e = lane + 32 * i;
-                float v = 0.f;
-                if (e < kP) {
-                    const float *sl = tslot + ring * kGroups * kP + e;
-                    v = sl[0];
-#pragma unroll
-                    for (int gg = 1; gg < kGroups; ++gg) v += sl[gg * kP];
+        if constexpr (MV == 0) {
+            return;  // decode: nothing to sum
+        } else {
+            // ---------------------------------------------------- epilogue --
+            bool ok = true;
+            for (int32_t ts = 0; ts < q.ntiles; ++ts) {
+                const int ring = ts % kTileRing;
+                if (ok && !mbar_wait(&tfull[ring], (uint32_t)((ts / kTileRing) & 1), a.err, kErrWaitFull)) ok = false;
+                float T[(kP + 31) / 32];
+    #pragma unroll
+                for (int i = 0; i < (kP + 31) / 32; ++i) {
+                    const int e = lane + 32 * i;
+                    float v = 0.f;
+                    if (e < kP) {
+                        const float *sl = tslot + ring * kGroups * kP + e;
+                        v = sl[0];
+    #pragma unroll
+                        for (int gg = 1; gg < kGroups; ++gg) v += sl[gg * kP];
+                    }
+                    T[i] = v;
                 }
-                T[i] = v;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[ring]);
+                const int64_t tl = q.tile_of(ts);
+                bool store = ts >= q.tsC;
+                if (!store) {
+                    // a tile shared with other CTAs: this CTA's sum to scratch,
+                    // the last of them to arrive adds all in CTA order
+                    const int cs = (tl == cu0 / NB) ? 0 : 1;
+                    float *mine = a.partials + ((int64_t)blockIdx.x * 2 + cs) * 128;
+    #pragma unroll
+                    for (int i = 0; i < (kP + 31) / 32; ++i)
+                        if (lane + 32 * i < kP) mine[lane + 32 * i] = T[i];
+                    // the warp's partial, released by lane 0's count; the last to
+                    // count acquires every other CTA's partial with it
+                    __syncwarp();
+                    const int64_t cf = worker_of(tl * NB, U, W), cl = worker_of((tl + 1) * NB - 1, U, W);
+                    int last = 0;
+                    if (lane == 0) {
+                        const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + tl), 1u);
+                        last = (old == (uint32_t)(cl - cf));
+                        if (last) a.counters[tl] = 0;
+                    }
+                    last = __shfl_sync(0xffffffffu, last, 0);
+                    if (last) {
+                        for (int64_t c = cf; c <= cl; ++c) {
+                            const int sc = (tl == range_start(c, U, W) / NB) ? 0 : 1;
+                            const float *pp = a.partials + (c * 2 + sc) * 128;
+    #pragma unroll
+                            for (int i = 0; i < (kP + 31) / 32; ++i)
+                                if (lane + 32 * i < kP) {
+                                    const float x = __ldcg(pp + lane + 32 * i);
+                                    T[i] = (c == cf) ? x : T[i] + x;
+                                }
+                        }
+                        store = true;
+                    }
+                }
+                if (store) {
+    #pragma unroll
+                    for (int i = 0; i < (kP + 31) / 32; ++i)
+                        if (lane + 32 * i < kP) ebuf[lane + 32 * i] = T[i];
+                    __syncwarp();
+                    for (int o = lane; o < 16 * a.M_out; o += 32) store_output(a, tl, o, [&](int e) { return ebuf[e]; });
+                    __syncwarp();
+                }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[ring]);
-            const int64_t tl = q.tile_of(ts);
-            bool store = ts >= q.tsC;
-            if (!store) {
-                // a tile shared with other CTAs: this CTA's sum to scratch,
-                // the last of them to arrive adds all in CTA order
-                const int cs = (tl == cu0 / NB) ? 0 : 1;
-                float *mine = a.partials + ((int64_t)blockIdx.x * 2 + cs) * 128;
-#pragma unroll
-                for (int i = 0; i < (kP + 31) / 32; ++i)
-                    if (lane + 32 * i < kP) mine[lane + 32 * i] = T[i];
-                // the warp's partial, released by lane 0's count; the last to
-                // count acquires every other CTA's partial with it
-                __syncwarp();
-                const int64_t cf = worker_of(tl * NB, U, W), cl = worker_of((tl + 1) * NB - 1, U, W);
-                int last = 0;
-                if (lane == 0) {
-                    const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + tl), 1u);
-                    last = (old == (uint32_t)(cl - cf));
-                    if (last) a.counters[tl] = 0;
-                }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    for (int64_t c = cf; c <= cl; ++c) {
-                        const int sc = (tl == range_start(c, U, W) / NB) ? 0 : 1;
-                        const float *pp = a.partials + (c * 2 + sc) * 128;
-#pragma unroll
-                        for (int i = 0; i < (kP + 31) / 32; ++i)
-                            if (lane + 32 * i < kP) {
-                                const float x = __ldcg(pp + lane + 32 * i);
-                                T[i] = (c == cf) ? x : T[i] + x;
-                            }
-                    }
-                    store = true;
-                }
-            }
-            if (store) {
-#pragma unroll
-                for (int i = 0; i < (kP + 31) / 32; ++i)
-                    if (lane + 32 * i < kP) ebuf[lane + 32 * i] = T[i];
-                __syncwarp();
-                for (int o = lane; o < 16 * a.M_out; o += 32) store_output(a, tl, o, [&](int e) { return ebuf[e]; });
-                __syncwarp();
-            }
+            if (lane == 0) signal_outputs(a);
+            return;
         }
-        __syncwarp();
-        if (lane == 0) signal_outputs(a);
-        return;
     }
 
     // ------------------------------------------------------- consumers --
     const int gi = (warp - 1) / kGroupWarps, wi = (warp - 1) % kGroupWarps;
     const int g = lane >> 2, t = lane & 3;
+    if constexpr (MV == 0) {
+        // DECODE: each unit's weights straight to the bf16 output [rows][C]:
+        // the group's stores, one group barrier, then the escaped weights'
+        // true values over their +0 (every group barrier is kept even after a
+        // failed wait, so none is left short)
+        uint16_t *out = reinterpret_cast<uint16_t *>(a.out);
+        const int64_t C = NB * 1024;
+        const uint32_t sh = (t & 1) ? 16u : 0u;
+        const int q0 = 4 * wi, j0 = 4 * wi + t;
+        bool ok = true;
+        int slot = gi % S;
+        uint32_t par = (uint32_t)((gi / S) & 1);
+        for (int32_t p = gi; p < q.n; p += kGroups) {
+            const int64_t u = unit_at(p);
+            const int64_t tile = u / NB, bcol = u - tile * NB;
+            const int64_t r0 = tile * kUnitRows + g, r1 = r0 + 8;
+            if (ok && !mbar_wait(&full[slot], par, a.err, kErrWaitFull)) ok = false;
+            const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
+            const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
+            const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
+            const uint8_t *lit0 = base + (size_t)e0.off16 * 16;
+            const uint8_t *lit1 = base + (size_t)e1.off16 * 16;
+            if (ok) {
+                const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
+                const uint32_t *t00 = reinterpret_cast<const uint32_t *>(lit0 + 1024);
+                const uint32_t *t01 = reinterpret_cast<const uint32_t *>(lit1 + 1024);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t a01[4], a23[4], c01[4], c23[4];
+                    decode_quad(lit0, t00, q0 + k, t, sh, tab.x, tab.y, tab.z, tab.w, a01, a23);
+                    decode_quad(lit1, t01, q0 + k, t, sh, tab.x, tab.y, tab.z, tab.w, c01, c23);
+                    const int64_t col = bcol * 1024 + 64 * (q0 + k) + 16 * t;
+                    if (r0 < a.rows) {
+                        uint4 *d = reinterpret_cast<uint4 *>(out + r0 * C + col);
+                        d[0] = make_uint4(a01[0], a23[0], a01[1], a23[1]);
+                        d[1] = make_uint4(a01[2], a23[2], a01[3], a23[3]);
+                    }
+                    if (r1 < a.rows) {
+                        uint4 *d = reinterpret_cast<uint4 *>(out + r1 * C + col);
+                        d[0] = make_uint4(c01[0], c23[0], c01[1], c23[1]);
+                        d[1] = make_uint4(c01[2], c23[2], c01[3], c23[3]);
+                    }
+                }
+            }
+            group_sync(gi);
+            if (ok) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const RowEntry e = h ? e1 : e0;
+                    const uint8_t *lit = h ? lit1 : lit0;
+                    const int64_t row = h ? r1 : r0;
+                    const uint8_t *term = lit + 1408;
+                    const uint16_t *idx = reinterpret_cast<const uint16_t *>(lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
+                    if (row < a.rows)
+                        for (int j = j0; j < (int)e.nesc; j += 4 * kGroupWarps) {
+                            const uint32_t pos = idx[j] & 1023u;
+                            const uint32_t lb = lit[pos];
+                            out[row * C + bcol * 1024 + pos] =
+                                (uint16_t)(((lb & 0x80u) << 8) | ((uint32_t)term[j] << 7) | (lb & 0x7Fu));
+                        }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+            }
+            slot += kGroups;
+            while (slot >= S) {
+                slot -= S;
+                par ^= 1u;
+            }
+        }
+        return;
+    } else {
 
     // D[rows g, g + 8][activation rows 2t, 2t + 1] over this warp's k range, the tile so far
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
@@ -584,6 +660,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     }
     if (cur >= 0) flush(cur);
     for (int32_t z = cur + 1; z < q.ntiles; ++z) deposit_zero(z);
+    }
 }
 
 // Shared-memory plan for a launch: the slot size and the number of slots.
@@ -616,7 +693,7 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg, const dm_gather *gather) {
     const dm::TensorLayout &L = t->L;
-    if (Mv < 1 || Mv > kMaxVirtualRows) {
+    if (Mv < 0 || Mv > kMaxVirtualRows) {  // 0: decode to bf16
         msg = "sip kernel: 1..8 virtual activation rows";
         return DM_EINVAL;
     }
@@ -646,18 +723,18 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         return DM_EINVAL;
     }
     using Kern = void (*)(SipArgs);
-    static const Kern kernels[kMaxVirtualRows] = {sip_gemv_kernel<1>, sip_gemv_kernel<2>, sip_gemv_kernel<3>,
-                                                  sip_gemv_kernel<4>, sip_gemv_kernel<5>, sip_gemv_kernel<6>,
-                                                  sip_gemv_kernel<7>, sip_gemv_kernel<8>};
-    static bool attr_set[kMaxVirtualRows] = {false};
-    const Kern kern = kernels[Mv - 1];
-    if (!attr_set[Mv - 1]) {
+    static const Kern kernels[kMaxVirtualRows + 1] = {sip_gemv_kernel<0>, sip_gemv_kernel<1>, sip_gemv_kernel<2>,
+                                                      sip_gemv_kernel<3>, sip_gemv_kernel<4>, sip_gemv_kernel<5>,
+                                                      sip_gemv_kernel<6>, sip_gemv_kernel<7>, sip_gemv_kernel<8>};
+    static bool attr_set[kMaxVirtualRows + 1] = {false};
+    const Kern kern = kernels[Mv];
+    if (!attr_set[Mv]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
-        attr_set[Mv - 1] = true;
+        attr_set[Mv] = true;
     }
     SipArgs a{};
     a.data = t->d_data;
@@ -713,66 +790,6 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     return DM_OK;
 }
 
-// ---------------------------------------------------------------- decode --
-// Dense decode of a sip tensor into bf16 bits [rows][C]: one CTA per unit
-// (16 rows x one 1024-weight block column), 256 threads. Thread (row s,
-// chunk c) decodes weights [64c, 64c + 64) of row s: 64 literal bytes and 64
-// tier-0 codes (six whole words) through the same PRMT tables as the GEMV,
-// into shared memory; the escapes then take their terminal exponents; the
-// tile leaves in 16-byte stores. An escape without a terminal byte inside
-// its block (a malformed block the loader clipped) stays +0, as in the GEMV.
-__global__ void __launch_bounds__(256) sip_decode_kernel(const uint8_t *__restrict__ data,
-                                                          const uint32_t *__restrict__ unit16, int64_t NB,
-                                                          int64_t rows, int64_t C, uint16_t *__restrict__ out) {
-    __shared__ __align__(16) uint16_t tileb[kUnitRows][1024 + 8];
-    const int64_t u = blockIdx.x;
-    const int64_t tile = u / NB, bcol = u % NB;
-    const uint8_t *base = data + (size_t)unit16[u] * 16;
-    const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
-    const int s = threadIdx.x >> 4, c = threadIdx.x & 15;
-    const RowEntry e = reinterpret_cast<const RowEntry *>(base)[s];
-    const uint8_t *lit = base + (size_t)e.off16 * 16;
-    const uint32_t *t0 = reinterpret_cast<const uint32_t *>(lit + 1024) + 6 * c;
-    uint32_t w[6];
-#pragma unroll
-    for (int k = 0; k < 6; ++k) w[k] = t0[k];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {  // 16 weights: 48 code bits from bit 48q
-        const uint4 Lq = *reinterpret_cast<const uint4 *>(lit + 64 * c + 16 * q);
-        const int b0 = 48 * q;
-        const uint32_t lo32 = __funnelshift_r(w[b0 >> 5], w[(b0 >> 5) + 1], b0 & 31);
-        const uint32_t hi = w[(b0 >> 5) + 1] >> (b0 & 31);
-        const uint32_t xa = spread_codes(lo32 & 0x00FFFFFFu);
-        const uint32_t xb = spread_codes(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
-        uint32_t p[8];
-        decode4(Lq.x, xa, tab.x, tab.y, tab.z, tab.w, p[0], p[1]);
-        decode4(Lq.y, xa >> 16, tab.x, tab.y, tab.z, tab.w, p[2], p[3]);
-        decode4(Lq.z, xb, tab.x, tab.y, tab.z, tab.w, p[4], p[5]);
-        decode4(Lq.w, xb >> 16, tab.x, tab.y, tab.z, tab.w, p[6], p[7]);
-        uint4 *dst = reinterpret_cast<uint4 *>(&tileb[s][64 * c + 16 * q]);
-        dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-        dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
-    }
-    __syncthreads();
-    {  // escapes of row s: chunk c takes every 16th
-        const uint8_t *term = lit + 1408;
-        const uint16_t *idx = reinterpret_cast<const uint16_t *>(lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
-        for (int j = c; j < (int)e.nesc; j += 16) {
-            const uint32_t pos = idx[j] & 1023u;
-            const uint32_t lb = lit[pos];
-            tileb[s][pos] = (uint16_t)(((lb & 0x80u) << 8) | ((uint32_t)term[j] << 7) | (lb & 0x7Fu));
-        }
-    }
-    __syncthreads();
-    const int64_t c0 = bcol * 1024;
-    for (int i = threadIdx.x; i < kUnitRows * 128; i += 256) {
-        const int r = i >> 7, k = (i & 127) * 8;
-        const int64_t row = tile * kUnitRows + r;
-        if (row >= rows) continue;
-        *reinterpret_cast<uint4 *>(out + row * C + c0 + k) = *reinterpret_cast<const uint4 *>(&tileb[r][k]);
-    }
-}
-
 int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg) {
     const TensorLayout &L = t->L;
     if (!L.fast_sip) {
@@ -784,14 +801,9 @@ int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::stri
         return DM_EINVAL;
     }
     if (L.units == 0) return DM_OK;
-    sip_decode_kernel<<<(unsigned)L.units, 256, 0, (cudaStream_t)stream>>>(t->d_data, t->d_unit16, L.NB, L.rows, L.C,
-                                                                          out);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        msg = std::string("sip_decode_kernel: ") + cudaGetErrorString(e);
-        return DM_ECUDA;
-    }
-    return DM_OK;
+    // the GEMV kernel's pipeline in its decode mode (no activations)
+    return launch_gemv_sip_with(t, nullptr, 0, 0, 1, 1, nullptr, out, 0, t->S.partials, t->S.counters, t->S.err,
+                                t->S.max_workers, stream, msg);
 }
 
 }  // namespace dm

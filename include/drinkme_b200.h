@@ -59,6 +59,8 @@ typedef struct dm_tensor_info {
     int64_t resident_bytes;    /* device bytes the handle holds (layout + scratch) */
     int32_t fast_path;         /* 1 when the sm_100a sip kernel serves this tensor's GEMV */
     int32_t device;
+    int64_t device_bytes_per_call; /* read_bytes' count over what the kernels stream: differs when the
+                                      loader re-encoded a non-sip pack as sip (dm_tensor_create) */
 } dm_tensor_info;
 
 /* Library version (major * 10000 + minor * 100 + patch). */
@@ -73,7 +75,11 @@ int dm_version(void);
  * per-unit headers, the gulp schedule and, for the sip fast path, an
  * escape index) and copies it to the device. Host pointers: the pack's
  * rx_palette (unpadded, `npalette` entries), rx_offsets (R*NB+1 entries),
- * rx_data (`nwords`). Synchronous. */
+ * rx_data (`nwords`). Synchronous. A pack of another profile (gulp,
+ * balanced) with 1024-weight blocks and rows of whole blocks is decoded on
+ * the host and re-encoded as sip for the sip kernels (the same bits; the
+ * handle still reports the pack's own widths, payload words and read_bytes;
+ * device_bytes_per_call gives the re-encoded count). */
 int dm_tensor_create(const uint8_t *host_palette, size_t npalette, const uint32_t *host_offsets,
                      size_t noffsets, const uint32_t *host_data, size_t nwords, int64_t R, int64_t C,
                      const int32_t *host_widths, int32_t nwidths, int32_t block_size, int64_t row_begin,

@@ -96,3 +96,16 @@ def test_fused_tensor_refuses_misaligned_activations():
     buf = torch.zeros(1025, dtype=torch.bfloat16, device=DEV)
     with pytest.raises(ValueError, match="16-byte aligned"):
         radix_ops.gemv_mc(rt, buf[1:].reshape(1, 1024))
+
+
+def test_fused_sip_and_reencoded_gulp_parts():
+    """A gulp part with whole 1024-weight blocks is re-encoded as sip by the
+    loader and fuses with sip parts; every part's bits stay exact."""
+    Ws = _weights((128, 64), 4096, seed=17)
+    packs = [codec.pack_weight_radix(Ws[0], "sip"), codec.pack_weight_radix(Ws[1], "gulp")]
+    rt = swap.to_device_radix_fused(packs, DEV)
+    bits = np.concatenate([codec.bits_of(W) for W in Ws])
+    assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits)
+    x = torch.randn(4, 4096, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
+    ok, worst = _within_bound(radix_ops.gemv_mc(rt, x).cpu().numpy(), x, bits)
+    assert ok, worst

@@ -106,8 +106,43 @@ def test_fast_path_serves_the_sip_whole_block_tensors(runtimes):
     assert kinds["sip_normal_16x4096"] == radix_ops.DECODER_SIP_MMA
     assert kinds["sip_tail_16x4096"] == radix_ops.DECODER_SIP_MMA
     assert kinds["sip_normal_4x12288"] == radix_ops.DECODER_SIP_MMA
-    assert kinds["gulp_normal_16x4096"] == radix_ops.DECODER_GENERIC
+    # other profiles with whole 1024-weight blocks: re-encoded as sip by the loader
+    assert kinds["gulp_normal_16x4096"] == radix_ops.DECODER_SIP_MMA
+    assert kinds["balanced_normal_16x4096"] == radix_ops.DECODER_SIP_MMA
+    # ragged blocks: the general kernel
     assert kinds["sip_tail_3x1025"] == radix_ops.DECODER_GENERIC
+    assert kinds["gulp_tail_17x3079"] == radix_ops.DECODER_GENERIC
+    assert kinds["gulp_tail_b32_7x100"] == radix_ops.DECODER_GENERIC
+
+
+@pytest.mark.parametrize("profile", ["gulp", "balanced"])
+def test_other_profiles_reencoded_as_sip_keep_their_bits_and_counts(profile):
+    """A gulp / balanced pack served by the sip kernels: the loader decodes it
+    and re-encodes it as sip; the bits stay the source's, the handle reports
+    the pack's own widths, payload words and read_bytes, and the GEMV stays
+    within the float64 bound for M = 1..8."""
+    g = torch.Generator().manual_seed(21)
+    W = (torch.randn(512, 8192, generator=g) * 0.02).to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, profile)
+    rt = swap.to_device_radix(p, DEV)
+    info = rt["rx_handle"].info
+    assert radix_ops.decoder_of(rt) == radix_ops.DECODER_SIP_MMA
+    assert tuple(info.widths[:info.nwidths]) == tuple(p["widths"])
+    assert info.payload_words == p["rx_data"].size
+    nb = 512 * 8
+    pal_words = sum(((1 << w) - 1 + 3) // 4 for w in p["widths"][:-1])
+    assert radix_ops.read_bytes(rt) == p["rx_data"].size * 4 + (nb + 1) * 4 + pal_words * 4 + (
+        nb * 2 if len(p["widths"]) > 2 else 0)
+    assert info.device_bytes_per_call > 0
+    bits = codec.bits_of(W)
+    assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits)
+    x = torch.randn(8, 8192, generator=g).to(torch.bfloat16).to(DEV)
+    for M in (1, 2, 4, 8):
+        ok, worst = _within_bound(radix_ops.gemv_mc(rt, x[:M]).cpu().numpy(), x[:M], bits)
+        assert ok, (profile, M, worst)
+    # a row shard re-encodes only its rows
+    rs = swap.to_device_radix(p, DEV, 128, 320)
+    assert np.array_equal(radix_ops.decode_bits(rs).cpu().numpy().view(np.uint16), bits[128:320])
 
 
 def test_gemv_fp32_x_within_bound(golden, runtimes):

@@ -69,7 +69,8 @@ def test_fused_loader_refuses_parts_it_cannot_serve(golden):
     p = pack_of(z, pins, "sip_normal_16x4096")
     g = torch.Generator().manual_seed(0)
     narrow = codec.pack_weight_radix((torch.randn(16, 2048, generator=g) * 0.02).to(torch.bfloat16), "sip")
-    gulp = codec.pack_weight_radix((torch.randn(16, 4096, generator=g) * 0.02).to(torch.bfloat16), "gulp")
+    # ragged blocks: not re-encoded as sip, so never fusable
+    gulp = codec.pack_weight_radix((torch.randn(16, 3079, generator=g) * 0.02).to(torch.bfloat16), "gulp")
     with pytest.raises(ValueError, match="invalid radix palette entries"):
         RadixTensor.fused([p, dict(p, rx_palette=np.zeros_like(p["rx_palette"]))], "cuda:0")
     with pytest.raises(ValueError, match="multiple of 16 rows"):
