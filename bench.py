@@ -77,6 +77,7 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true", help="skip the qwen3-8b chain beside the headline")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLAS dense arm")
+    ap.add_argument("--no-configs", action="store_true", help="skip configs 3 (gulp, M = 2/4/8) and 5 (prefill)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small profiling cases only; the headline uses the model's)")
     return ap.parse_args()
@@ -397,6 +398,104 @@ def kernel_times(chain, device, reps=3):
     return out, tot_bytes, tot_ms, launches
 
 
+def _graph_us(fn, device, reps=10):
+    """Device µs of one replay of a CUDA graph of fn() (events on the replay
+    stream, after a warm replay)."""
+    import torch
+
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    g.replay()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        a.record(s)
+        for _ in range(reps):
+            g.replay()
+        b.record(s)
+    torch.cuda.synchronize(device)
+    us = a.elapsed_time(b) / reps * 1e3
+    del g
+    return us
+
+
+def config3_gulp_mc(device, peak):
+    """the Qwen3-8B linears packed gulp, through the
+    narrow linear (radix_ops.gemv_mc_fused) with M = 2, 4, 8 rows (and M = 1
+    beside them): µs per linear summed over one layer's seven linears, each
+    shape rotated over copies larger than 3x L2, and the GB/s on the gulp
+    read_bytes (the loader serves gulp through the sip kernels)."""
+    import numpy as np
+    import torch
+
+    from drinkme_b200 import codec, radix_ops, swap
+
+    res, total_bytes = {}, 0
+    rows = {M: 0.0 for M in (1, 2, 4, 8)}
+    for j, (name, R, C) in enumerate(WORKLOADS["qwen3-8b"]["linears"]):
+        bits = make_bits(R, C, seed=1000 + j, device=device)
+        p = codec.pack_array_radix(bits, "gulp")
+        rt0 = swap.to_device_radix(p, device)
+        n = max(3, int(3 * 126e6 // radix_ops.read_bytes(rt0)) + 1)
+        rts = [rt0] + [dict(rt0, rx_handle=rt0["rx_handle"].clone()) for _ in range(n - 1)]
+        total_bytes += radix_ops.read_bytes(rt0)
+        for M in rows:
+            g = torch.Generator(device=device)
+            x = torch.cat([torch.randn((1, C), generator=g.manual_seed(100 + m), device=device)
+                           for m in range(M)]).to(torch.bfloat16)
+            outs = [torch.empty((M, R), dtype=torch.bfloat16, device=device) for _ in rts]
+            us = _graph_us(lambda: [radix_ops.gemv_into(rt, x, None, o) for rt, o in zip(rts, outs)], device) / n
+            rows[M] += us
+            res.setdefault(name, {})[f"M{M}_us"] = round(us, 2)
+        res[name]["bpw"] = p["bpw"]
+        res[name]["device_bytes_per_call"] = int(rt0["rx_handle"].info.device_bytes_per_call)
+        del rts, outs, bits, p
+        torch.cuda.empty_cache()
+    summary = {f"M{M}": {"layer_us": round(us, 2), "gulp_gbs": round(total_bytes / us * 1e-3, 1),
+                         "frac_of_peak": round(total_bytes / us * 1e-3 / peak, 4),
+                         "us_per_row": round(us / M, 2)} for M, us in rows.items()}
+    return {"config": "BASELINE configs[2]: Qwen3-8B linears packed gulp, M = 2/4/8 activation rows",
+            "per_layer": summary, "per_linear": res,
+            "note": "gulp packs with whole 1024-weight blocks are re-encoded as sip by the loader (same bits)"}
+
+
+def config5_prefill(device):
+    """x [512, C] against sip gate/up 12288x4096 and down
+    4096x12288: the package's prefill route (CompressedLinear's dense arm: the
+    sip pipeline's decode mode to bf16, then cuBLAS) next to cuBLAS bf16 on
+    the uncompressed weights; TFLOP/s = 2 * 512 * R * C / time."""
+    import torch
+
+    from drinkme_b200 import codec, radix_ops, swap
+
+    out = {}
+    for name, R, C in (("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288)):
+        bits = make_bits(R, C, seed=7 + R + C, device=device)
+        p = codec.pack_array_radix(bits, "sip")
+        rt = swap.to_device_radix(p, device)
+        x = torch.randn((512, C), generator=torch.Generator(device=device).manual_seed(2),
+                        device=device).to(torch.bfloat16)
+        ws = [(torch.randn((R, C), device=device) * 0.02).to(torch.bfloat16) for _ in range(3)]
+        us_cublas = _graph_us(lambda: [torch.nn.functional.linear(x, w) for w in ws], device) / 3
+        us_decode = _graph_us(lambda: radix_ops.decode_weight(rt), device)
+        us_path = _graph_us(lambda: torch.nn.functional.linear(x, radix_ops.decode_weight(rt)), device)
+        fl = 2 * 512 * R * C
+        out[name] = {"path_us": round(us_path, 2), "path_tflops": round(fl / us_path * 1e-6, 1),
+                     "decode_us": round(us_decode, 2), "cublas_bf16_us": round(us_cublas, 2),
+                     "cublas_tflops": round(fl / us_cublas * 1e-6, 1)}
+        del ws, rt, p, bits
+        torch.cuda.empty_cache()
+    return {"config": "BASELINE configs[4]: prefill x [512, C], sip gate/up/down of Qwen3-8B",
+            "route": "decode to bf16 (sip pipeline, decode mode) then cuBLAS", "per_linear": out}
+
+
 def cublas_arm(shapes, device, reps=20):
     """cuBLAS dense bf16 (F.linear, M = 1) on uncompressed weights of the same
     shapes, rotating over copies larger than L2: µs per call and GB/s."""
@@ -590,6 +689,9 @@ def main():
                                         "fused_gemv_gbs": round(b8 / (t8 * 1e-3) / 1e9, 1),
                                         "frac_of_peak": round(b8 / (t8 * 1e-3) / 1e9 / peak, 4),
                                         "per_linear": pk8}
+        if not a.no_configs:
+            result["config3_gulp_mc"] = config3_gulp_mc(device, peak)
+            result["config5_prefill"] = config5_prefill(device)
         if not a.no_cpu:
             tok_s, kind, cores, sample, cold = cpu_reference_sample(a.workload)
             result["cpu_baseline"] = {"value": round(tok_s, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
