@@ -486,14 +486,17 @@ def config5_prefill(device):
         us_cublas = _graph_us(lambda: [torch.nn.functional.linear(x, w) for w in ws], device) / 3
         us_decode = _graph_us(lambda: radix_ops.decode_weight(rt), device)
         us_path = _graph_us(lambda: torch.nn.functional.linear(x, radix_ops.decode_weight(rt)), device)
+        us_tc = _graph_us(lambda: radix_ops.prefill(rt, x, None, torch.bfloat16), device)
         fl = 2 * 512 * R * C
         out[name] = {"path_us": round(us_path, 2), "path_tflops": round(fl / us_path * 1e-6, 1),
                      "decode_us": round(us_decode, 2), "cublas_bf16_us": round(us_cublas, 2),
-                     "cublas_tflops": round(fl / us_cublas * 1e-6, 1)}
+                     "cublas_tflops": round(fl / us_cublas * 1e-6, 1),
+                     "tcgen05_prefill_us": round(us_tc, 2), "tcgen05_prefill_tflops": round(fl / us_tc * 1e-6, 1)}
         del ws, rt, p, bits
         torch.cuda.empty_cache()
     return {"config": "BASELINE configs[4]: prefill x [512, C], sip gate/up/down of Qwen3-8B",
-            "route": "decode to bf16 (sip pipeline, decode mode) then cuBLAS", "per_linear": out}
+            "route": "decode to bf16 (sip pipeline, decode mode) then cuBLAS; tcgen05_* = the fused tensor-core "
+                     "prefill kernel (decoded tiles in shared memory, TMEM accumulators)", "per_linear": out}
 
 
 def cublas_arm(shapes, device, reps=20):

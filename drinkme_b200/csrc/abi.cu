@@ -459,3 +459,23 @@ extern "C" int dm_device_free(void *dptr, char *err, size_t err_len) {
     if (e != cudaSuccess) return cuda_fail(err, err_len, e, "cudaFree");
     return DM_OK;
 }
+
+extern "C" int64_t dm_prefill_workspace_bytes(const dm_tensor *t, int64_t M) {
+    if (!t || M < 1) return 0;
+    return dm::prefill_workspace_bytes(t, M);
+}
+
+extern "C" int dm_prefill(const dm_tensor *t, const void *x, int64_t M, const void *bias, void *out,
+                          int32_t out_dtype, void *work, int64_t work_bytes, void *stream, char *err,
+                          size_t err_len) {
+    if (!t || !x || !out || !work) return fail(err, err_len, DM_EINVAL, "dm_prefill: null pointer");
+    if (M < 1) return fail(err, err_len, DM_EINVAL, "dm_prefill: M must be at least 1");
+    if (out_dtype != DM_BF16 && out_dtype != DM_F32)
+        return fail(err, err_len, DM_EINVAL, "dm_prefill: dtype must be DM_BF16 or DM_F32");
+    DeviceGuard g(t->device);
+    std::string msg;
+    int rc = dm::launch_prefill_sip(t, reinterpret_cast<const uint16_t *>(x), M, reinterpret_cast<const uint16_t *>(bias),
+                                    out, out_dtype == DM_F32, reinterpret_cast<uint8_t *>(work), work_bytes, stream, msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}

@@ -101,6 +101,9 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
                  std::string &msg);
 int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
 void decode_rows(const PackPart &P, uint16_t *out);
+int64_t prefill_workspace_bytes(const dm_tensor *t, int64_t M);
+int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const uint16_t *bias, void *out,
+                       int out_f32, uint8_t *work, int64_t work_bytes, void *stream, std::string &msg);
 int64_t pack_read_bytes(const PackPart &P, int64_t *payload_words);
 int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw);
 

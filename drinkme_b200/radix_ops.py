@@ -145,6 +145,32 @@ def gemv_raw(w: torch.Tensor, x: torch.Tensor, bias, out_dtype) -> torch.Tensor:
     return out
 
 
+def prefill(p: dict, x: torch.Tensor, bias, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """The prefill arm for a sip tensor: x [M, C] bf16 -> [M, R] in
+    `out_dtype`, the weights decoded into shared memory and contracted on the
+    tensor cores (tcgen05, fp32 accumulate), the bias added in fp32 before
+    the one rounding — the dense arm's arithmetic (radix_kernel_gpu.py:
+    615-636) without the decoded weight in HBM."""
+    h = _handle(p)
+    dev = h.torch_device
+    x = _check_x(x.reshape(-1, h.info.C), h.info.C, dev)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if out_dtype not in _DT:
+        raise TypeError(f"radix_ops: output dtype must be bf16 or fp32, not {out_dtype}")
+    M = x.shape[0]
+    rows = h.info.rows
+    out = torch.empty((M, rows), dtype=out_dtype, device=dev)
+    b = None
+    if bias is not None:
+        b = bias.to(device=dev, dtype=torch.bfloat16).contiguous()
+    nbytes = int(_lib.lib().dm_prefill_workspace_bytes(h.ptr, M))
+    work = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    _lib.call("dm_prefill", h.ptr, ct.c_void_p(x.data_ptr()), M, ct.c_void_p(b.data_ptr() if b is not None else 0),
+              ct.c_void_p(out.data_ptr()), _DT[out_dtype], ct.c_void_p(work.data_ptr()), work.numel(), _stream(dev))
+    return out
+
+
 def decode_bits(p: dict, num_warps: int = 2) -> torch.Tensor:
     """Every block decoded to the original uint16 bit patterns [R, C]."""
     h = _handle(p)

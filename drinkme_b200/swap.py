@@ -145,6 +145,20 @@ def _dense_min() -> int:
     return _DENSE_MIN
 
 
+_PREFILL_TC: bool | None = None
+
+
+def _prefill_kernel() -> bool:
+    """DRINKME_B200_PREFILL=tc routes the dense arm of sip tensors through the
+    tensor-core prefill kernel (radix_ops.prefill); by default the dense arm
+    is the reference's own (decode to bf16, then one cuBLAS GEMM), which
+    measures faster on B200 today. Read once."""
+    global _PREFILL_TC
+    if _PREFILL_TC is None:
+        _PREFILL_TC = os.environ.get("DRINKME_B200_PREFILL", "").strip().lower() == "tc"
+    return _PREFILL_TC
+
+
 class CompressedLinear(torch.nn.Module):
     """Routing by M and the round-once epilogue, shared by the radix and raw
     modules."""
@@ -238,6 +252,12 @@ class RadixCompressedLinear(CompressedLinear):
                 out = radix_ops.gemv_fused(self.p, xf[0], self.bias, x.dtype)
             else:
                 out = radix_ops.gemv_mc_fused(self.p, xf, self.bias, x.dtype)
+            return out.reshape(*shape[:-1], self.R)
+        if route == "dense" and x.dtype == torch.bfloat16 and _prefill_kernel() and self.p["rx_handle"].info.fast_path:
+            # the dense arm's arithmetic on the tensor cores, the weights
+            # decoded into shared memory instead of HBM
+            shape = x.shape
+            out = radix_ops.prefill(self.p, x.reshape(-1, self.C), self.bias, x.dtype)
             return out.reshape(*shape[:-1], self.R)
         return super()._forward(x, route)
 

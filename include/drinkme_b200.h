@@ -153,6 +153,19 @@ int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const
 int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
                     int32_t out_dtype, void *stream, char *err, size_t err_len);
 
+/* Prefill: y[M, rows] = x[M, C] @ W^T (+ bias) for a prefill chunk (any M >=
+ * 1; the module routes M >= 9 here), W a sip tensor (fast_path): the weights
+ * are decoded into shared memory and contracted on the tensor cores
+ * (tcgen05.mma, fp32 accumulate in tensor memory), the bias added in fp32 and
+ * one rounding to `out_dtype`. Replaces the dense arm's decode + GEMM
+ * (src/drinkme/codec/radix_kernel_gpu.py:615-636, swap.py:361-378). x is bf16
+ * [M, C], 16-byte aligned; `work` is a device workspace of at least
+ * dm_prefill_workspace_bytes(t, M) bytes, 16-byte aligned (the activations
+ * re-laid out for the tensor core); out is [M, rows]. */
+int64_t dm_prefill_workspace_bytes(const dm_tensor *t, int64_t M);
+int dm_prefill(const dm_tensor *t, const void *x, int64_t M, const void *bias, void *out, int32_t out_dtype,
+               void *work, int64_t work_bytes, void *stream, char *err, size_t err_len);
+
 /* The output gather of a row-sharded linear over NVLink, fused into its GEMV
  * (the exchange the reference lacks: it has no multi-GPU code; this replaces
  * an all-gather after each shard's dm_gemv). Rank `rank` of `world` holds

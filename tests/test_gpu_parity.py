@@ -250,7 +250,21 @@ def test_module_routes_match_the_arms(golden):
     assert torch.equal(y5, (radix_ops.gemv_mc(mod.p, x[:5]) + bias.float()).to(torch.bfloat16))
     xd = torch.randn(9, 4096, device=DEV).to(torch.bfloat16)
     assert mod._route(xd) == "dense"
+    # the dense arm of a sip tensor: the tensor-core prefill kernel (decoded
+    # weights in shared memory), the reference's F.linear arithmetic within
+    # fp32-accumulation noise
+    # the dense arm: the reference's own (exact decoded bits, then F.linear)
     assert torch.equal(mod(xd), torch.nn.functional.linear(xd, W, bias))
+    # ... or, with DRINKME_B200_PREFILL=tc, the tensor-core prefill kernel
+    old = swap._PREFILL_TC
+    try:
+        swap._PREFILL_TC = True
+        yd = mod(xd)
+    finally:
+        swap._PREFILL_TC = old
+    assert torch.equal(yd, radix_ops.prefill(mod.p, xd, bias, torch.bfloat16))
+    ref = torch.nn.functional.linear(xd.float(), W.float(), bias.float())
+    assert (yd.float() - ref).abs().max() / ref.abs().max() <= 1e-2  # both bf16-rounded
 
 
 @pytest.mark.parametrize("R", [13, 40, 1])

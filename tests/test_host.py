@@ -18,7 +18,7 @@ from drinkme_b200 import _lib, codec, radix_schedule, registry
 def test_library_exports_every_declared_entry_point():
     with open(os.path.join(ROOT, "include", "drinkme_b200.h")) as f:
         header = f.read()
-    declared = set(re.findall(r"^int (dm_\w+)\(", header, flags=re.M))
+    declared = set(re.findall(r"^int(?:64_t)? (dm_\w+)\(", header, flags=re.M))
     assert declared == set(_lib.EXPORTS)
     L = ct.CDLL(_lib.LIB_PATH)
     for name in declared:
