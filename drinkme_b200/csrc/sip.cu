@@ -213,16 +213,19 @@ __device__ __forceinline__ void wait_inputs(const SipArgs &a) {
 // After this CTA's last output (called by one lane, after a __syncwarp of
 // the warp that stored them): the CTA count of the launch; the last CTA,
 // having acquired every count, raises every rank's flag of this linear to
-// the new launch count with a system-scope release.
+// the new launch count behind one system-scope fence.
 __device__ __forceinline__ void signal_outputs(const SipArgs &a) {
     if (a.world <= 0) return;
-    // the count needs GPU scope only: the last CTA's system-scope release
+    // the count needs GPU scope only: the last CTA's system-scope fence
     // below carries every CTA's stores (ordered before it here) to the peers
     if (atom_add_acq_rel_gpu(a.done, 1u) + 1u != gridDim.x) return;
     *a.done = 0u;
     const uint32_t g = *a.gen + 1u;
     *a.gen = g;
-    for (int r = 0; r < a.world; ++r) st_release_sys(a.peer_flags[r] + a.rank, g);
+    // one system-scope fence releases every flag store after it (a release
+    // store per rank would wait for the outstanding NVLink stores each time)
+    fence_acq_rel_sys();
+    for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, g);
 }
 
 __device__ __forceinline__ void group_sync(int group) {
