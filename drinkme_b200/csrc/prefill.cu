@@ -152,8 +152,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t NB = a.NB;
     const int32_t nwin = (int32_t)(NB * 16);
-    // (every CTA walks the K windows from the first; `rot` would rotate them)
-    const int32_t rot = 0;
     const int32_t ncols = a.ntiles <= 1 ? 128 : (a.ntiles == 2 ? 256 : 512);
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
@@ -218,13 +216,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
 #pragma unroll
             for (int j = 0; j < 6; ++j) c[j] = cp[j];
         };
-        // this thread's windows in CTA order w = half, half + 2, ...; window
-        // id wk = (w + rot) mod nwin, block column wk / 16, quad wk % 16
+        // this thread's windows w = half, half + 2, ...: block column w / 16,
+        // quad w % 16
         Hdr hc{}, hn{};
         uint4 Ln[4] = {};
         uint32_t cn[6] = {0, 0, 0, 0, 0, 0};
         int cur = 0;
-        const int32_t wk0 = (half + rot) % nwin;
+        const int32_t wk0 = half;
         // this thread's share of its row's staged escapes: entries
         // [32 half, 32 half + 32) of a block column's list, prefetched a
         // block column ahead and written at each block column's start
@@ -261,7 +259,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
         bool need_share = true;  // the next block column's share still to fetch
         for (int32_t w = half; w < nwin; w += 2) {
             const int s = w % kPfBStages, use = w / kPfBStages;
-            const int32_t wk = (w + rot) % nwin;
+            const int32_t wk = w;
             const int qb = wk & 15;
             uint4 L[4];
             uint32_t cw[6];
@@ -271,9 +269,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
             for (int j = 0; j < 6; ++j) cw[j] = cn[j];
             // the next window of this thread: its bytes fetched now (from the
             // next block column's row block when it starts one)
-            const int32_t wk2 = (w + 2 + rot) % nwin;
-            const bool more = w + 2 < nwin;
-            const bool newblk = more && ((wk2 >> 4) != (wk >> 4) || wk2 < wk);
+            const int32_t wk2 = w + 2;
+            const bool more = wk2 < nwin;
+            const bool newblk = more && (wk2 >> 4) != (wk >> 4);
             if (real && more) load_win(newblk ? hn : hc, wk2 & 15, Ln, cn);
             if (need_share && !newblk) {  // the next block column's escapes, a block column early
                 if (real) load_share(hn);
@@ -383,7 +381,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
                 if (use > 0 && !mbar_wait(&a_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
                 if (!ok) break;
                 mbar_arrive_expect_tx(&a_full[s], bytes);
-                bulk_g2s(atile + s * kPfMaxTiles * kATile, a.xs + (size_t)((w + rot) % nwin) * bytes, bytes, &a_full[s]);
+                bulk_g2s(atile + s * kPfMaxTiles * kATile, a.xs + (size_t)w * bytes, bytes, &a_full[s]);
             }
         }
     } else {
