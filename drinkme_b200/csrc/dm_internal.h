@@ -119,7 +119,7 @@ int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t 
                             void *stream, std::string &msg);
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg);
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int dir_cap);
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *xres_bytes, int dir_cap);
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg,

@@ -70,6 +70,7 @@ struct SipArgs {
     int *counters;    // [tiles], zero between launches
     int *err;
     int32_t slot_bytes, x_off, nslots, dir_cap;
+    int32_t xres_bytes;  // > 0: the activations of every block column resident in shared memory
     int32_t tile_split;  // 1: CTAs own whole tiles (no tile is shared), else units are split evenly
     // row-sharded outputs gathered over NVLink (world > 0): every output is
     // also stored into each rank's gathered buffer [M][world * slot] at
@@ -92,6 +93,7 @@ struct SipArgs {
 constexpr int kGroupWarps = 4;
 constexpr int kGroups = 4;
 constexpr int kTileRing = 4;  // tile slots between the groups and the epilogue warp
+constexpr int kMaxResidentCols = 32;  // block columns whose activations may stay resident
 constexpr int kSipThreads = 32 * (2 + kGroups * kGroupWarps);
 constexpr int kMaxSlots = 12;  // staging slots of the unit ring
 
@@ -228,6 +230,15 @@ __device__ __forceinline__ void signal_outputs(const SipArgs &a) {
     for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, g);
 }
 
+// Full barriers per staging slot. A group takes every 4th position of the
+// ring, so it can reach slot p % S before the slot's previous position p - S
+// (another group's) has landed; with one barrier per slot its phase parity
+// would then name an older, completed phase. Position p arms barrier set
+// (p / S) % L of its slot: a group at p has consumed p - 4, so every position
+// up to p - 4 is staged, hence (L - 1) * S >= 4 puts p - (L - 1) * S among
+// them and the set's previous use p - L * S has been consumed, and landed.
+__host__ __device__ __forceinline__ int full_sets(int S) { return S >= kGroups ? 2 : (kGroups + S - 1) / S + 1; }
+
 __device__ __forceinline__ void group_sync(int group) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(kGroupWarps * 32) : "memory");
 }
@@ -284,17 +295,23 @@ struct Seq {
     }
 };
 
-template <int MV>
+// RES: the activations of every block column are resident in shared memory
+// (loaded once per launch) instead of staged with each unit.
+template <int MV, bool RES>
 __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int kP = 16 * MV;  // floats of one tile partial [MV][16]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.nslots;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * a.slot_bytes);
-    uint64_t *empty = full + S;
+    // resident activations [NB][Mv][kXRowStride] (when xres_bytes > 0)
+    uint8_t *xres = smem + (size_t)S * a.slot_bytes;
+    const int L = full_sets(S);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xres + a.xres_bytes);  // [L][S]
+    uint64_t *empty = full + L * S;       // [S]
     uint64_t *tfull = empty + S;          // [kTileRing]: 16 warp deposits
     uint64_t *tempty = tfull + kTileRing;  // [kTileRing]: the epilogue warp's release
-    float *pwb = reinterpret_cast<float *>(tempty + kTileRing);  // [kGroups][2][kGroupWarps][kP]
+    uint64_t *x_ready = tempty + kTileRing;  // [kMaxResidentCols]: a block column's resident activations landed
+    float *pwb = reinterpret_cast<float *>(x_ready + kMaxResidentCols);  // [kGroups][2][kGroupWarps][kP]
     float *tslot = pwb + kGroups * 2 * kGroupWarps * kP;          // [kTileRing][kGroups][kP]
     float *ebuf = tslot + kTileRing * kGroups * kP;               // [kP] the epilogue's tile sum
     uint32_t *dir = reinterpret_cast<uint32_t *>(ebuf + kP);     // this CTA's unit starts
@@ -307,14 +324,14 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     q.init(cu0, cu1, NB);
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < S; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kGroupWarps);
-        }
+        for (int i = 0; i < L * S; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < S; ++i) mbar_init(&empty[i], kGroupWarps);
         for (int i = 0; i < kTileRing; ++i) {
             mbar_init(&tfull[i], kGroups * kGroupWarps);
             mbar_init(&tempty[i], 1);
         }
+        if constexpr (RES)
+            for (int i = 0; i < NB; ++i) mbar_init(&x_ready[i], 1);
         mbar_fence_init();
     }
     if (warp == 0 && dir_in_smem)
@@ -328,44 +345,87 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     if (warp == 0) {
         // ---------------------------------------------------- producer --
         if (lane == 0) {
-            auto stage_w = [&](int32_t p, int slot) {
-                const int64_t u = unit_at(p);
+            // unit u (block column col) into slot `slot`, completing on full
+            // barrier fb; positions walk units with no division: consecutive
+            // within a segment, a segment's first unit starting a tile
+            auto advance = [&](int32_t np, int64_t &u, int32_t &col) {
+                if (np == q.nA || np == q.nAB) {
+                    u = unit_at(np);
+                    col = 0;
+                } else {
+                    ++u;
+                    if (++col == NB) col = 0;
+                }
+            };
+            const int64_t u0 = unit_at(0);
+            const int32_t col0 = (int32_t)(u0 % NB);
+            auto stage_w = [&](int64_t u, int slot, uint64_t *fb) {
                 const uint32_t q0 = dir_in_smem ? dir[u - cu0] : a.unit16[u];
                 const uint32_t q1 = dir_in_smem ? dir[u + 1 - cu0] : a.unit16[u + 1];
                 const uint32_t ubytes = (q1 - q0) * 16u;
-                mbar_arrive_expect_tx(&full[slot], ubytes + (uint32_t)a.Mv * 2048u);
-                bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.data + (size_t)q0 * 16, ubytes, &full[slot]);
+                mbar_arrive_expect_tx(fb, ubytes + (RES ? 0u : (uint32_t)a.Mv * 2048u));
+                bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.data + (size_t)q0 * 16, ubytes, fb);
             };
-            auto stage_x = [&](int32_t p, int slot) {
-                const int64_t u = unit_at(p);
-                const uint16_t *xb = a.x + (size_t)(u % NB) * 1024;
+            auto stage_x = [&](int32_t col, int slot, uint64_t *fb) {
+                if constexpr (RES) return;  // the block columns' activations are resident
+                const uint16_t *xb = a.x + (size_t)col * 1024;
                 uint8_t *dst = smem + (size_t)slot * a.slot_bytes + a.x_off;
-                for (int v = 0; v < a.Mv; ++v) bulk_g2s(dst + v * kXRowStride, xb + v * a.x_stride, 2048u, &full[slot]);
+                for (int v = 0; v < a.Mv; ++v) bulk_g2s(dst + v * kXRowStride, xb + v * a.x_stride, 2048u, fb);
             };
             // the first S units' weights do not depend on the kernel before
             // this one: stage them, wait for it, then add their activations
             const int32_t first = std::min<int32_t>(S, q.n);
-            for (int32_t p = 0; p < first; ++p) stage_w(p, p);
+            {
+                int64_t u = u0;
+                int32_t col = col0;
+                for (int32_t p = 0; p < first; ++p) {
+                    if (p > 0) advance(p, u, col);
+                    stage_w(u, p, &full[p]);
+                }
+            }
             pdl_wait();
             wait_inputs(a);
-            for (int32_t p = 0; p < first; ++p) stage_x(p, p);
-            int slot = 0;
+            if constexpr (RES) {
+                // the block columns this CTA's units touch (its units are
+                // consecutive: min(n, NB) columns from A's first), each once
+                // on its own barrier, in the order the units first need them;
+                // every copy issued here is waited for by a consumer
+                int64_t b = q.a0 % NB;
+                const int64_t ncols = std::min<int64_t>(NB, q.n);
+                for (int64_t i = 0; i < ncols; ++i) {
+                    mbar_arrive_expect_tx(&x_ready[b], (uint32_t)a.Mv * 2048u);
+                    for (int v = 0; v < a.Mv; ++v)
+                        bulk_g2s(xres + (b * a.Mv + v) * kXRowStride, a.x + b * 1024 + v * a.x_stride, 2048u,
+                                 &x_ready[b]);
+                    if (++b == NB) b = 0;
+                }
+            }
+            int64_t u = u0;
+            int32_t col = col0;
+            for (int32_t p = 0; p < first; ++p) {
+                if (p > 0) advance(p, u, col);
+                stage_x(col, p, &full[p]);
+            }
+            int slot = 0, fset = L > 1 ? 1 : 0;  // position first = S: slot 0 of set 1
             uint32_t epar = 0;  // parity of the empty phase to wait for
             bool ok = true;
             for (int32_t p = first; p < q.n && ok; ++p) {
+                advance(p, u, col);
                 if (!mbar_wait(&empty[slot], epar, a.err, kErrWaitEmpty)) ok = false;
                 if (ok) {
-                    stage_w(p, slot);
-                    stage_x(p, slot);
+                    uint64_t *fb = &full[fset * S + slot];
+                    stage_w(u, slot, fb);
+                    stage_x(col, slot, fb);
                 }
                 if (++slot == S) {
                     slot = 0;
                     epar ^= 1u;
+                    if (++fset == L) fset = 0;
                 }
             }
             // drain: every copy this producer issued lands before the CTA exits
             for (int32_t p = std::max<int32_t>(0, q.n - S); p < q.n && ok; ++p)
-                mbar_wait(&full[p % S], (uint32_t)((p / S) & 1), a.err, kErrWaitDrain);
+                mbar_wait(&full[((p / S) % L) * S + p % S], (uint32_t)((p / S / L) & 1), a.err, kErrWaitDrain);
         }
         return;
     }
@@ -457,13 +517,13 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
         const uint32_t sh = (t & 1) ? 16u : 0u;
         const int q0 = 4 * wi, j0 = 4 * wi + t;
         bool ok = true;
-        int slot = gi % S;
-        uint32_t par = (uint32_t)((gi / S) & 1);
+        int slot = gi % S, set = (gi / S) % L;
+        uint32_t par = (uint32_t)((gi / S / L) & 1);
         for (int32_t p = gi; p < q.n; p += kGroups) {
             const int64_t u = unit_at(p);
             const int64_t tile = u / NB, bcol = u - tile * NB;
             const int64_t r0 = tile * kUnitRows + g, r1 = r0 + 8;
-            if (ok && !mbar_wait(&full[slot], par, a.err, kErrWaitFull)) ok = false;
+            if (ok && !mbar_wait(&full[set * S + slot], par, a.err, kErrWaitFull)) ok = false;
             const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
             const RowEntry e0 = reinterpret_cast<const RowEntry *>(base)[g];
             const RowEntry e1 = reinterpret_cast<const RowEntry *>(base)[g + 8];
@@ -514,7 +574,10 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
             slot += kGroups;
             while (slot >= S) {
                 slot -= S;
-                par ^= 1u;
+                if (++set == L) {
+                    set = 0;
+                    par ^= 1u;
+                }
             }
         }
         return;
@@ -593,16 +656,20 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     const bool has_x = g < MV;
     const int q0 = 4 * wi, j0 = 4 * wi + t;
     int32_t cur = -1;  // tile sequence number of the group's current tile
-    int slot = gi % S;
-    uint32_t par = (uint32_t)((gi / S) & 1);
+    uint32_t xin = 0;  // bit b: block column b's resident activations have landed
+    int slot = gi % S, set = (gi / S) % L;
+    uint32_t par = (uint32_t)((gi / S / L) & 1);
     int32_t cq = -1, cts = 0;  // in segment C: the unit's offset in its tile, its tile's number
     const int32_t nb = (int32_t)NB;
+    const int32_t bcA = (int32_t)(q.a0 % NB);  // block column of A's first unit
     for (int32_t p = gi; p < q.n; p += kGroups) {
-        int32_t ts;
+        int32_t ts, bc;  // the unit's tile sequence number and block column
         if (p < q.nA) {
             ts = 0;
+            bc = bcA + p;
         } else if (p < q.nAB) {
             ts = q.tsB;
+            bc = p - q.nA;
         } else {
             if (cq < 0) {
                 cq = (p - q.nAB) % nb;
@@ -615,13 +682,18 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                 }
             }
             ts = q.tsC + cts;
+            bc = cq;
         }
         if (ts != cur) {
             if (cur >= 0) flush(cur);
             for (int32_t z = cur + 1; z < ts; ++z) deposit_zero(z);
             cur = ts;
         }
-        if (ok && !mbar_wait(&full[slot], par, a.err, kErrWaitFull)) ok = false;
+        if (ok && !mbar_wait(&full[set * S + slot], par, a.err, kErrWaitFull)) ok = false;
+        if (RES && !((xin >> bc) & 1u)) {
+            if (ok && !mbar_wait(&x_ready[bc], 0u, a.err, kErrWaitFull)) ok = false;
+            xin |= 1u << bc;
+        }
         if (ok) {
             const uint8_t *base = smem + (size_t)slot * a.slot_bytes;
             // the exponent tables of the unit's part (high part th0/th1, low tl0/tl1)
@@ -633,7 +705,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
             const uint8_t *lit1 = base + (size_t)e1.off16 * 16;
             const uint32_t *t00 = reinterpret_cast<const uint32_t *>(lit0 + 1024);
             const uint32_t *t01 = reinterpret_cast<const uint32_t *>(lit1 + 1024);
-            const uint8_t *xs = base + a.x_off;
+            const uint8_t *xs = RES ? xres + bc * (MV * kXRowStride) : base + a.x_off;
             const uint8_t *xg = xs + g * kXRowStride;
             float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
             float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
@@ -658,7 +730,10 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
         slot += kGroups;
         while (slot >= S) {
             slot -= S;
-            par ^= 1u;
+            if (++set == L) {
+                set = 0;
+                par ^= 1u;
+            }
         }
     }
     if (cur >= 0) flush(cur);
@@ -666,21 +741,41 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     }
 }
 
-// Shared-memory plan for a launch: the slot size and the number of slots.
+// Staging slots of a launch with resident activations: five, six at M = 1
+// for tensors of 8 or more block columns. Fewer slots than fit: on the Qwen3
+// 8B and 32B shapes 5-6 slots beat 7-9 by 3-8 % (and 4 lose 10 %), while
+// without residency the count makes no difference.
+inline int resident_slots(int Mv, int64_t NB) { return Mv == 1 && NB >= 8 ? 6 : 5; }
+
+// Shared-memory plan for a launch: the slot size, the number of slots and
+// whether the activations of every block column stay resident (one copy per
+// launch instead of one per unit; chosen whenever they fit beside the
+// resident launch's slots). Any number of slots is correct (full_sets).
 // Fixed part: the barriers, the groups' partial buffers, the tile ring, the
 // epilogue's sum and the directory.
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int dir_cap) {
+int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *xres_bytes, int dir_cap) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
-    const int sb = unit + Mv * kXRowStride;
     const int budget = 227 * 1024;
     const int kP = 16 * Mv;
-    const int fixed = (2 * kMaxSlots + 2 * kTileRing) * 8 +
+    const int fixed = (3 * kMaxSlots + 2 * kTileRing + kMaxResidentCols) * 8 +
                       (kGroups * 2 * kGroupWarps + kTileRing * kGroups + 1) * kP * 4 + (dir_cap + 1) * 4 + 128;
-    const int n = std::min(kMaxSlots, (budget - fixed) / sb);
-    if (n < 2) return -1;
-    *slot_bytes = sb;
-    *nslots = n;
-    return n * sb + fixed;
+    const int sb1 = unit + Mv * kXRowStride;
+    const int n1 = std::min(kMaxSlots, (budget - fixed) / sb1);
+    const int64_t xr = Mv >= 1 && t->L.NB <= kMaxResidentCols
+                           ? ((t->L.NB * Mv * kXRowStride + 127) & ~(int64_t)127)
+                           : 0;
+    const int want = resident_slots(Mv, t->L.NB);
+    if (xr > 0 && (int64_t)budget - fixed - xr >= (int64_t)want * unit) {
+        *slot_bytes = unit;
+        *nslots = want;
+        *xres_bytes = (int)xr;
+        return want * unit + (int)xr + fixed;
+    }
+    if (n1 < 1) return -1;
+    *slot_bytes = sb1;
+    *nslots = n1;
+    *xres_bytes = 0;
+    return n1 * sb1 + fixed;
 }
 
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
@@ -719,25 +814,34 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     }
     const int64_t per_cta = tile_split ? (tiles + grid - 1) / grid * L.NB : perA;
     const int dir_cap = (int)std::min<int64_t>(4096, per_cta + 2);
-    int slot_bytes = 0, nslots = 0;
-    const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, dir_cap);
+    int slot_bytes = 0, nslots = 0, xres_bytes = 0;
+    const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, &xres_bytes, dir_cap);
     if (smem < 0) {
         msg = "sip kernel: a unit does not fit in shared memory";
         return DM_EINVAL;
     }
     using Kern = void (*)(SipArgs);
-    static const Kern kernels[kMaxVirtualRows + 1] = {sip_gemv_kernel<0>, sip_gemv_kernel<1>, sip_gemv_kernel<2>,
-                                                      sip_gemv_kernel<3>, sip_gemv_kernel<4>, sip_gemv_kernel<5>,
-                                                      sip_gemv_kernel<6>, sip_gemv_kernel<7>, sip_gemv_kernel<8>};
-    static bool attr_set[kMaxVirtualRows + 1] = {false};
-    const Kern kern = kernels[Mv];
-    if (!attr_set[Mv]) {
+    static const Kern kernels[2][kMaxVirtualRows + 1] = {
+        {sip_gemv_kernel<0, false>, sip_gemv_kernel<1, false>, sip_gemv_kernel<2, false>, sip_gemv_kernel<3, false>,
+         sip_gemv_kernel<4, false>, sip_gemv_kernel<5, false>, sip_gemv_kernel<6, false>, sip_gemv_kernel<7, false>,
+         sip_gemv_kernel<8, false>},
+        {nullptr, sip_gemv_kernel<1, true>, sip_gemv_kernel<2, true>, sip_gemv_kernel<3, true>,
+         sip_gemv_kernel<4, true>, sip_gemv_kernel<5, true>, sip_gemv_kernel<6, true>, sip_gemv_kernel<7, true>,
+         sip_gemv_kernel<8, true>}};
+    static bool attr_set[2][kMaxVirtualRows + 1] = {};
+    const int res = xres_bytes > 0 ? 1 : 0;
+    const Kern kern = kernels[res][Mv];
+    if (kern == nullptr) {
+        msg = "sip kernel: no resident-activation kernel without activations";
+        return DM_EINVAL;
+    }
+    if (!attr_set[res][Mv]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
-        attr_set[Mv] = true;
+        attr_set[res][Mv] = true;
     }
     SipArgs a{};
     a.data = t->d_data;
@@ -757,6 +861,7 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.counters = counters;
     a.err = err;
     a.slot_bytes = slot_bytes;
+    a.xres_bytes = xres_bytes;
     a.x_off = (L.max_unit_bytes + 127) & ~127;
     a.nslots = nslots;
     a.dir_cap = dir_cap;

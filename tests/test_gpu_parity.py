@@ -202,6 +202,34 @@ def test_mc_rows_bitwise_the_m1_call_on_tensors_spanning_every_sm(R, C):
                        radix_ops.gemv_mc(rt, x[:4].to(torch.bfloat16).float().to(DEV)))
 
 
+def test_escape_heavy_units_with_few_staging_slots():
+    """Rows whose exponents spread far outside the seven tier-0 ones escape
+    almost every weight: their 16-row units (~70 KB) leave room for only two
+    or three staging slots, so a consumer group can reach a slot whose
+    previous phase is still landing. Results stay exact and bitwise equal
+    across M."""
+    g = torch.Generator().manual_seed(77)
+    R, C = 96, 8192
+    W = torch.randn(R, C, generator=g) * 0.02
+    e = torch.randint(-60, 60, (48, C), generator=g).float()
+    sgn = torch.where(torch.rand(48, C, generator=g) < 0.5, -1.0, 1.0)
+    W[16:64] = sgn * torch.exp2(e) * (1 + torch.rand(48, C, generator=g))
+    W = W.to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, "sip")
+    rt = swap.to_device_radix(p, DEV)
+    assert radix_ops.decoder_of(rt) == radix_ops.DECODER_SIP_MMA
+    bits = codec.bits_of(W)
+    assert np.array_equal(radix_ops.decode_bits(rt).cpu().numpy().view(np.uint16), bits)
+    x = (torch.randn(8, C, generator=g) * 2.0 ** -40).to(torch.bfloat16).to(DEV)
+    ones = [radix_ops.gemv(rt, x[j]) for j in range(8)]
+    for M in (1, 2, 3, 5, 8):
+        ym = radix_ops.gemv_mc(rt, x[:M])
+        for j in range(M):
+            assert torch.equal(ym[j], ones[j]), (M, j)
+        ok, worst = _within_bound(ym.cpu().numpy(), x[:M], bits)
+        assert ok, (M, worst)
+
+
 def test_bf16_x_equals_its_fp32_widening(golden, runtimes):
     z, pins = golden
     for name, rt in runtimes.items():
