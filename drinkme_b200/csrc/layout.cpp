@@ -143,6 +143,29 @@ static int sip_escapes(const uint32_t *tier0, uint16_t *out) {
     return count;
 }
 
+// The device form of a sip block's tier-0 codes (the pack's 3-bit stream,
+// code k at bits 3k..3k+2, 96 words) for the kernels' decode: two planes in
+// the same 384 bytes. The kernels decode 16 weights k = 64q + 16t + [0, 16)
+// per lane and need their codes as nibbles; from these planes that takes a
+// mask and an OR per 8 codes instead of a bit-spreading sequence.
+//   words 0..63, word 4q + t: bits 2j, 2j + 1 = the low two bits of the code
+//     of weight j / 2 (j even) or 8 + j / 2 (j odd) of lane t's 16;
+//   words 64..95, word 64 + 2q + t / 2: bit 2 of those codes; weight w < 8
+//     at bit 4w (t even) or 4w + 2 (t odd), weight 8 + w at 4w + 1 or 4w + 3.
+static void sip_code_planes(const uint32_t *src, uint32_t *dst) {
+    for (int i = 0; i < 96; ++i) dst[i] = 0;
+    for (int k = 0; k < 1024; ++k) {
+        const int b = 3 * k;
+        const uint64_t two = (uint64_t)src[b >> 5] | ((b >> 5) + 1 < 96 ? (uint64_t)src[(b >> 5) + 1] << 32 : 0);
+        const uint32_t c = (uint32_t)(two >> (b & 31)) & 7u;
+        const int q = k >> 6, t = (k >> 4) & 3, w = k & 15;
+        const int j = w < 8 ? 2 * w : 2 * (w - 8) + 1;
+        dst[4 * q + t] |= (c & 3u) << (2 * j);
+        const int pos = w < 8 ? 4 * w + ((t & 1) ? 2 : 0) : 4 * (w - 8) + ((t & 1) ? 3 : 1);
+        dst[64 + 2 * q + (t >> 1)] |= ((c >> 2) & 1u) << pos;
+    }
+}
+
 // One block of any radix profile decoded to bf16 bit patterns (radix.py:
 // 241-278, the reference's CPU decode): the literal plane, then per
 // nonterminal tier the codes of the weights still active (an escape code
@@ -395,6 +418,11 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
             hdr[s].sched = sched[i];
             hdr[s].nesc = nesc[i];
             std::memcpy(base + at, P->data + P->offsets[gb], (size_t)words * 4);
+            if (fast && words >= 352) {
+                uint32_t planes[96];
+                sip_code_planes(P->data + P->offsets[gb] + 256, planes);
+                std::memcpy(base + at + 1024, planes, sizeof(planes));
+            }
             at += a16(words * 4);
             if (fast) {
                 std::vector<uint16_t> pos(1024);

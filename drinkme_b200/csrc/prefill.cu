@@ -103,13 +103,13 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 8 three-bit codes (bits 0..23) -> nibbles (the GEMV's spread_codes).
-__device__ __forceinline__ uint32_t spread8(uint32_t v) {
-    uint32_t x = v;
-    x += 15u * (x & 0x00FFF000u);
-    x += 3u * (x & 0x0FC00FC0u);
-    x += (x & 0x38383838u);
-    return x;
+// The selectors of 16 codes (quarter t of a quad) from the unit's code
+// planes (the GEMV's code_selectors): v = plane word 4q + t, P = bit-2 word
+// 64 + 2q + t / 2.
+__device__ __forceinline__ void selectors16(uint32_t v, uint32_t P, int t, uint32_t &s0, uint32_t &s1) {
+    const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
+    s0 = (v & 0x33333333u) | (__funnelshift_l(P, P, rl) & 0x44444444u);
+    s1 = ((v >> 2) & 0x33333333u) | (__funnelshift_l(P, P, rh) & 0x44444444u);
 }
 
 // Four weights -> two bf16 pairs (the GEMV's decode4).
@@ -212,9 +212,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
             const uint4 *lp = reinterpret_cast<const uint4 *>(h.lit + 64 * qb);
 #pragma unroll
             for (int j = 0; j < 4; ++j) L[j] = lp[j];
-            const uint32_t *cp = reinterpret_cast<const uint32_t *>(h.lit + 1024) + 6 * qb;
+            const uint32_t *cp = reinterpret_cast<const uint32_t *>(h.lit + 1024);
 #pragma unroll
-            for (int j = 0; j < 6; ++j) c[j] = cp[j];
+            for (int j = 0; j < 4; ++j) c[j] = cp[4 * qb + j];
+            c[4] = cp[64 + 2 * qb];
+            c[5] = cp[64 + 2 * qb + 1];
         };
         // this thread's windows w = half, half + 2, ...: block column w / 16,
         // quad w % 16
@@ -280,12 +282,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
             if (use > 0 && ok && !mbar_wait(&b_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
             uint8_t *rowp = btile + s * kBTile + i * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {  // 16 weights: 48 code bits from bit 48j
-                const int b0 = 48 * j;
-                const uint32_t lo32 = __funnelshift_r(cw[b0 >> 5], cw[(b0 >> 5) + 1], b0 & 31);
-                const uint32_t hi = cw[(b0 >> 5) + 1] >> (b0 & 31);
-                const uint32_t xa = spread8(lo32 & 0x00FFFFFFu);
-                const uint32_t xb = spread8(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
+            for (int j = 0; j < 4; ++j) {  // 16 weights: quarter j of the quad
+                uint32_t xa, xb;
+                selectors16(cw[j], cw[4 + (j >> 1)], j, xa, xb);
                 uint32_t p[8];
                 // code 7 decodes to sign | exponent 0 | mantissa: the escape
                 // patch below only ORs the terminal exponent in

@@ -100,16 +100,6 @@ constexpr int kMaxSlots = 12;  // staging slots of the unit ring
 __device__ __forceinline__ int64_t range_start(int64_t w, int64_t U, int64_t W) { return (w * U) / W; }
 __device__ __forceinline__ int64_t worker_of(int64_t u, int64_t U, int64_t W) { return ((u + 1) * W + U - 1) / U - 1; }
 
-// 8 three-bit codes (bits 0..23 of v, upper bits zero) -> nibble k holds code
-// k in its bits 0..2 with bit 3 clear: a PRMT selector per 4 codes.
-__device__ __forceinline__ uint32_t spread_codes(uint32_t v) {
-    uint32_t x = v;
-    x += 15u * (x & 0x00FFF000u);  // codes 4..7 up by 4 bits
-    x += 3u * (x & 0x0FC00FC0u);   // codes 2,3 and 6,7 up by 2
-    x += (x & 0x38383838u);        // codes 1,3,5,7 up by 1
-    return x;
-}
-
 // Four weights: literal word L (4 literal bytes), selector S (4 codes in
 // nibbles) -> two bf16 pairs {w0, w1}, {w2, w3}.
 __device__ __forceinline__ void decode4(uint32_t L, uint32_t S, uint32_t th0, uint32_t th1, uint32_t tl0,
@@ -124,29 +114,37 @@ __device__ __forceinline__ void decode4(uint32_t L, uint32_t S, uint32_t th0, ui
     p23 = __byte_perm(lo, hi, 0x7362);
 }
 
+// The selectors of lane t's 16 codes from the unit's code planes (the
+// loader's sip_code_planes): nibble w of s0 = code of weight w (w < 8), of
+// s1 = code of weight 8 + w. The lane's bit-2 bits sit at 4w + 2 after a
+// rotation by rl (weights 0..7) or rh (8..15): rl = t odd ? 0 : 2, rh = t
+// odd ? 31 : 1.
+__device__ __forceinline__ void code_selectors(uint32_t v, uint32_t P, uint32_t rl, uint32_t rh, uint32_t &s0,
+                                               uint32_t &s1) {
+    s0 = (v & 0x33333333u) | (__funnelshift_l(P, P, rl) & 0x44444444u);
+    s1 = ((v >> 2) & 0x33333333u) | (__funnelshift_l(P, P, rh) & 0x44444444u);
+}
+
 // One row's quad: 16 weights at k = 64q + 16t + [0, 16) -> four bf16-pair
 // registers per half (p01[j] = weights 4j, 4j+1; p23[j] = weights 4j+2, 4j+3).
-__device__ __forceinline__ void decode_quad(const uint8_t *lit, const uint32_t *tier0, int q, int t, uint32_t sh,
-                                            uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1, uint32_t p01[4],
-                                            uint32_t p23[4]) {
+__device__ __forceinline__ void decode_quad(const uint8_t *lit, const uint32_t *codes, int q, int t, uint32_t rl,
+                                            uint32_t rh, uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1,
+                                            uint32_t p01[4], uint32_t p23[4]) {
     const uint4 L = *reinterpret_cast<const uint4 *>(lit + 64 * q + 16 * t);
-    const int wi = (192 * q + 48 * t) >> 5;
-    const uint32_t w0 = tier0[wi], w1 = tier0[wi + 1];
-    const uint32_t lo32 = __funnelshift_r(w0, w1, sh);
-    const uint32_t hi = w1 >> sh;
-    const uint32_t xa = spread_codes(lo32 & 0x00FFFFFFu);
-    const uint32_t xb = spread_codes(__funnelshift_r(lo32, hi, 24) & 0x00FFFFFFu);
-    decode4(L.x, xa, th0, th1, tl0, tl1, p01[0], p23[0]);
-    decode4(L.y, xa >> 16, th0, th1, tl0, tl1, p01[1], p23[1]);
-    decode4(L.z, xb, th0, th1, tl0, tl1, p01[2], p23[2]);
-    decode4(L.w, xb >> 16, th0, th1, tl0, tl1, p01[3], p23[3]);
+    uint32_t s0, s1;
+    code_selectors(codes[4 * q + t], codes[64 + 2 * q + (t >> 1)], rl, rh, s0, s1);
+    decode4(L.x, s0, th0, th1, tl0, tl1, p01[0], p23[0]);
+    decode4(L.y, s0 >> 16, th0, th1, tl0, tl1, p01[1], p23[1]);
+    decode4(L.z, s1, th0, th1, tl0, tl1, p01[2], p23[2]);
+    decode4(L.w, s1 >> 16, th0, th1, tl0, tl1, p01[3], p23[3]);
 }
 
 // One quad of both of this lane's rows (g and g + 8) into the MMA chain: the
 // weights are the A operand (16 rows x 16 k), the activations the B operand
 // (16 k x 8 activation rows; lanes g < Mv hold activation row g).
 __device__ __forceinline__ void quad(const uint8_t *lit0, const uint32_t *t00, const uint8_t *lit1,
-                                     const uint32_t *t01, const uint8_t *xg, int q, int t, uint32_t sh, bool has_x,
+                                     const uint32_t *t01, const uint8_t *xg, int q, int t, uint32_t rl, uint32_t rh,
+                                     bool has_x,
                                      uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1, float &d0, float &d1,
                                      float &d2, float &d3) {
     uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
@@ -155,8 +153,8 @@ __device__ __forceinline__ void quad(const uint8_t *lit0, const uint32_t *t00, c
         X1 = *reinterpret_cast<const uint4 *>(xg + 128 * q + 32 * t + 16);
     }
     uint32_t a01[4], a23[4], c01[4], c23[4];
-    decode_quad(lit0, t00, q, t, sh, th0, th1, tl0, tl1, a01, a23);
-    decode_quad(lit1, t01, q, t, sh, th0, th1, tl0, tl1, c01, c23);
+    decode_quad(lit0, t00, q, t, rl, rh, th0, th1, tl0, tl1, a01, a23);
+    decode_quad(lit1, t01, q, t, rl, rh, th0, th1, tl0, tl1, c01, c23);
     mma_bf16_16816(d0, d1, d2, d3, a01[0], c01[0], a23[0], c23[0], X0.x, X0.y);
     mma_bf16_16816(d0, d1, d2, d3, a01[1], c01[1], a23[1], c23[1], X0.z, X0.w);
     mma_bf16_16816(d0, d1, d2, d3, a01[2], c01[2], a23[2], c23[2], X1.x, X1.y);
@@ -514,7 +512,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
         // failed wait, so none is left short)
         uint16_t *out = reinterpret_cast<uint16_t *>(a.out);
         const int64_t C = NB * 1024;
-        const uint32_t sh = (t & 1) ? 16u : 0u;
+        const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         const int q0 = 4 * wi, j0 = 4 * wi + t;
         bool ok = true;
         int slot = gi % S, set = (gi / S) % L;
@@ -536,8 +534,8 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     uint32_t a01[4], a23[4], c01[4], c23[4];
-                    decode_quad(lit0, t00, q0 + k, t, sh, tab.x, tab.y, tab.z, tab.w, a01, a23);
-                    decode_quad(lit1, t01, q0 + k, t, sh, tab.x, tab.y, tab.z, tab.w, c01, c23);
+                    decode_quad(lit0, t00, q0 + k, t, rl, rh, tab.x, tab.y, tab.z, tab.w, a01, a23);
+                    decode_quad(lit1, t01, q0 + k, t, rl, rh, tab.x, tab.y, tab.z, tab.w, c01, c23);
                     const int64_t col = bcol * 1024 + 64 * (q0 + k) + 16 * t;
                     if (r0 < a.rows) {
                         uint4 *d = reinterpret_cast<uint4 *>(out + r0 * C + col);
@@ -652,7 +650,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
         if (lane == 0) mbar_arrive(&tfull[ts % kTileRing]);
     };
 
-    const uint32_t sh = (t & 1) ? 16u : 0u;
+    const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
     const bool has_x = g < MV;
     const int q0 = 4 * wi, j0 = 4 * wi + t;
     int32_t cur = -1;  // tile sequence number of the group's current tile
@@ -709,10 +707,10 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
             const uint8_t *xg = xs + g * kXRowStride;
             float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
             float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
-            quad(lit0, t00, lit1, t01, xg, q0 + 0, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
-            quad(lit0, t00, lit1, t01, xg, q0 + 1, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
-            quad(lit0, t00, lit1, t01, xg, q0 + 2, t, sh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
-            quad(lit0, t00, lit1, t01, xg, q0 + 3, t, sh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 0, t, rl, rh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 1, t, rl, rh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 2, t, rl, rh, has_x, th0, th1, tl0, tl1, d0, d1, d2, d3);
+            quad(lit0, t00, lit1, t01, xg, q0 + 3, t, rl, rh, has_x, th0, th1, tl0, tl1, f0, f1, f2, f3);
             // escapes of rows g and g + 8: the group's warps take every 16th one, lane t every 4th of those
             escapes<MV>(lit0, e0, xs, j0, cg);
             escapes<MV>(lit1, e1, xs, j0, cg8);
