@@ -93,9 +93,13 @@ struct SipArgs {
 constexpr int kGroupWarps = 4;
 constexpr int kGroups = 4;
 constexpr int kTileRing = 4;  // tile slots between the groups and the epilogue warp
-constexpr int kMaxResidentCols = 32;  // block columns whose activations may stay resident
+// Block columns whose activations may stay resident: wider tensors (a 25600
+// column down projection) measured faster staging activations per unit.
+constexpr int kMaxResidentCols = 16;
 constexpr int kSipThreads = 32 * (2 + kGroups * kGroupWarps);
-constexpr int kMaxSlots = 12;  // staging slots of the unit ring
+// Staging slots of the unit ring, at most: with activations staged per unit
+// six beat five, seven and eight on the 25600-column down projection.
+constexpr int kMaxSlots = 6;
 
 __device__ __forceinline__ int64_t range_start(int64_t w, int64_t U, int64_t W) { return (w * U) / W; }
 __device__ __forceinline__ int64_t worker_of(int64_t u, int64_t U, int64_t W) { return ((u + 1) * W + U - 1) / U - 1; }
@@ -741,8 +745,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
 
 // Staging slots of a launch with resident activations: five, six at M = 1
 // for tensors of 8 or more block columns. Fewer slots than fit: on the Qwen3
-// 8B and 32B shapes 5-6 slots beat 7-9 by 3-8 % (and 4 lose 10 %), while
-// without residency the count makes no difference.
+// 8B and 32B shapes 5-6 slots beat 7-8 by 3-8 % (and 4 lose up to 10 %).
 inline int resident_slots(int Mv, int64_t NB) { return Mv == 1 && NB >= 8 ? 6 : 5; }
 
 // Shared-memory plan for a launch: the slot size, the number of slots and
