@@ -56,6 +56,8 @@
 
 namespace dm {
 
+constexpr int kMaxGrid = 160;  // CTAs of one launch, at most (one per SM)
+
 struct SipArgs {
     const uint8_t *data;
     const uint32_t *unit16;
@@ -71,7 +73,8 @@ struct SipArgs {
     int *err;
     int32_t slot_bytes, x_off, nslots, dir_cap;
     int32_t xres_bytes;  // > 0: the activations of every block column resident in shared memory
-    int32_t tile_split;  // 1: CTAs own whole tiles (no tile is shared), else units are split evenly
+    int32_t tile_split;  // 1: CTAs own whole tiles (no tile is shared), else units are split by weight
+    int32_t starts[kMaxGrid + 1];  // CTA w owns units [starts[w], starts[w + 1])
     // row-sharded outputs gathered over NVLink (world > 0): every output is
     // also stored into each rank's gathered buffer [M][world * slot] at
     // rank * slot + row; the last CTA then raises each rank's flag of this
@@ -100,9 +103,26 @@ constexpr int kSipThreads = 32 * (2 + kGroups * kGroupWarps);
 // Staging slots of the unit ring, at most: with activations staged per unit
 // six beat five, seven and eight on the 25600-column down projection.
 constexpr int kMaxSlots = 6;
+// Units fewer than the average that the last stream-K worker gets (part_sum).
+constexpr double kSkewUnits = 4.0;
 
-__device__ __forceinline__ int64_t range_start(int64_t w, int64_t U, int64_t W) { return (w * U) / W; }
-__device__ __forceinline__ int64_t worker_of(int64_t u, int64_t U, int64_t W) { return ((u + 1) * W + U - 1) / U - 1; }
+// The stream-K split: worker b's share of the U units is proportional to
+// wt(b) = 4096 for b <= b0 and 4096 - r (b - b0) after. CTAs are dispatched
+// in index order as the previous launch's CTAs leave their SMs, so the last
+// ones start after that launch has ended, too late to stage their first
+// units under it, and get a smaller share (r = 0: an even split).
+static inline int64_t part_sum(int64_t w, int64_t b0, int64_t r) {
+    const int64_t m = w - 1 - b0;
+    return 4096 * w - (m > 0 ? r * (m * (m + 1) / 2) : 0);
+}
+// The CTA that owns unit u (the last w with starts[w] <= u), from a CTA
+// whose range is near.
+__device__ __forceinline__ int64_t worker_of(const SipArgs &a, int64_t u, int64_t from, int64_t W) {
+    int64_t c = from;
+    while (c > 0 && a.starts[c] > u) --c;
+    while (c + 1 < W && a.starts[c + 1] <= u) ++c;
+    return c;
+}
 
 // Four weights: literal word L (4 literal bytes), selector S (4 codes in
 // nibbles) -> two bf16 pairs {w0, w1}, {w2, w3}.
@@ -319,8 +339,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     uint32_t *dir = reinterpret_cast<uint32_t *>(ebuf + kP);     // this CTA's unit starts
     const int64_t U = a.units, W = gridDim.x, NB = a.NB;
     const int64_t T = (U + NB - 1) / NB;
-    const int64_t cu0 = a.tile_split ? range_start(blockIdx.x, T, W) * NB : range_start(blockIdx.x, U, W);
-    const int64_t cu1 = a.tile_split ? range_start(blockIdx.x + 1, T, W) * NB : range_start(blockIdx.x + 1, U, W);
+    const int64_t cu0 = a.starts[blockIdx.x], cu1 = a.starts[blockIdx.x + 1];
     const bool dir_in_smem = (cu1 - cu0 + 1) <= a.dir_cap;
     Seq q;
     q.init(cu0, cu1, NB);
@@ -469,7 +488,8 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                     // the warp's partial, released by lane 0's count; the last to
                     // count acquires every other CTA's partial with it
                     __syncwarp();
-                    const int64_t cf = worker_of(tl * NB, U, W), cl = worker_of((tl + 1) * NB - 1, U, W);
+                    const int64_t cf = worker_of(a, tl * NB, blockIdx.x, W);
+                    const int64_t cl = worker_of(a, (tl + 1) * NB - 1, blockIdx.x, W);
                     int last = 0;
                     if (lane == 0) {
                         const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + tl), 1u);
@@ -479,7 +499,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                     last = __shfl_sync(0xffffffffu, last, 0);
                     if (last) {
                         for (int64_t c = cf; c <= cl; ++c) {
-                            const int sc = (tl == range_start(c, U, W) / NB) ? 0 : 1;
+                            const int sc = (tl == a.starts[c] / NB) ? 0 : 1;
                             const float *pp = a.partials + (c * 2 + sc) * 128;
     #pragma unroll
                             for (int i = 0; i < (kP + 31) / 32; ++i)
@@ -808,12 +828,24 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     const int64_t roundsB = (tiles + gridB - 1) / gridB * ((L.NB + kGroups - 1) / kGroups);
     const int tile_split = roundsB <= roundsA ? 1 : 0;
     const int64_t grid = tile_split ? gridB : gridA;
-    if (grid > max_workers) {
+    if (grid > max_workers || grid > kMaxGrid) {
         msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
-              std::to_string(max_workers);
+              std::to_string(max_workers) + " (or the launch's " + std::to_string(kMaxGrid) + ")";
         return DM_EINVAL;
     }
-    const int64_t per_cta = tile_split ? (tiles + grid - 1) / grid * L.NB : perA;
+    // the stream-K split's weights: the last 40 % of the CTAs down to
+    // kSkewUnits fewer units than the average for the very last (none when
+    // the average is under 8 units)
+    int32_t part_b0 = 0, part_r = 0;
+    if (!tile_split && grid > 8 && perA >= 8) {
+        part_b0 = (int32_t)(grid * 6 / 10);
+        const double delta = std::min(0.5, kSkewUnits * (double)grid / (double)L.units);
+        part_r = (int32_t)std::llround(4096.0 * delta / (double)(grid - 1 - part_b0));
+    }
+    const int64_t per_cta =
+        tile_split ? (tiles + grid - 1) / grid * L.NB
+                   : (part_r ? (L.units * 4096 + part_sum(grid, part_b0, part_r) - 1) / part_sum(grid, part_b0, part_r) + 1
+                             : perA);
     const int dir_cap = (int)std::min<int64_t>(4096, per_cta + 2);
     int slot_bytes = 0, nslots = 0, xres_bytes = 0;
     const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, &xres_bytes, dir_cap);
@@ -867,6 +899,9 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.nslots = nslots;
     a.dir_cap = dir_cap;
     a.tile_split = tile_split;
+    for (int64_t w = 0; w <= grid; ++w)
+        a.starts[w] = (int32_t)(tile_split ? (w * tiles / grid) * L.NB
+                                           : L.units * part_sum(w, part_b0, part_r) / part_sum(grid, part_b0, part_r));
     if (gather) {
         a.world = gather->world;
         a.rank = gather->rank;
