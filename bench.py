@@ -687,11 +687,20 @@ def main():
             c8 = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head, fuse=fuse)
             ms8, _ = time_graph(c8, a.steps, a.warmup, 1, 0, device)
             pk8, b8, t8, _ = kernel_times(c8, device)
+            # the raw bf16 lm_head alone: this package's raw GEMV and cuBLAS
+            from drinkme_b200 import radix_ops
+            xh = torch.randn((1, head.shape[1]), generator=g, device=device).to(torch.bfloat16)
+            hb = head.numel() * 2 + xh.numel() * 2 + head.shape[0] * 2
+            h_us = _graph_us(lambda: radix_ops.gemv_raw(head, xh, None, torch.bfloat16), device)
+            h_cublas = _graph_us(lambda: torch.nn.functional.linear(xh, head), device)
             result["qwen3_8b_chain"] = {"config": "BASELINE configs[1]: 36 layers + raw lm_head 151936x4096",
                                         "tokens_per_s": round(1e3 / ms8, 3), "ms_per_step": round(ms8, 4),
                                         "fused_gemv_gbs": round(b8 / (t8 * 1e-3) / 1e9, 1),
                                         "frac_of_peak": round(b8 / (t8 * 1e-3) / 1e9 / peak, 4),
-                                        "per_linear": pk8}
+                                        "per_linear": pk8,
+                                        "lm_head_raw": {"us": round(h_us, 2), "gbs": round(hb / h_us * 1e-3, 1),
+                                                        "frac_of_peak": round(hb / h_us * 1e-3 / peak, 4),
+                                                        "cublas_us": round(h_cublas, 2)}}
         if not a.no_configs:
             result["config3_gulp_mc"] = config3_gulp_mc(device, peak)
             result["config5_prefill"] = config5_prefill(device)

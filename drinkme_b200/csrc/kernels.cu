@@ -253,65 +253,78 @@ __global__ void split_f32_kernel(const float *x, int64_t C, int64_t M, uint16_t 
     out[(3 * m + 2) * C + c] = lo;
 }
 
-// Raw bf16 GEMV: one warp per output row, 16-byte loads along the row, up to
-// 8 activation rows per pass over the weights, a fixed butterfly reduction.
-template <int XF32>
-__global__ void __launch_bounds__(256) gemv_raw_kernel(const uint16_t *w, int64_t R, int64_t C, const void *x, int M,
+// Raw bf16 GEMV: one warp per output row, 16-byte loads along the row, MM
+// activation rows (1..8) per pass over the weights, a fixed butterfly
+// reduction.
+template <int XF32, int MM>
+__global__ void __launch_bounds__(256) gemv_raw_kernel(const uint16_t *w, int64_t R, int64_t C, const void *x,
                                                        const uint16_t *bias, void *out, int out_f32) {
+    constexpr int M = MM;
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * 8;
     for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < R; r += nwarps) {
         const uint16_t *row = w + r * C;
-        float acc[kMaxVirtualRows];
+        float acc[MM];
 #pragma unroll
-        for (int m = 0; m < kMaxVirtualRows; ++m) acc[m] = 0.f;
+        for (int m = 0; m < MM; ++m) acc[m] = 0.f;
         const bool vec = (C % 8) == 0;
         if (vec) {
-            for (int64_t c = (int64_t)lane * 8; c < C; c += 256) {
-                uint4 wv = __ldg(reinterpret_cast<const uint4 *>(row + c));
-                uint32_t wp[4] = {wv.x, wv.y, wv.z, wv.w};
+            // 16 weights of the row at c times the activations, in c order
+            auto step = [&](int64_t c, uint4 wv) {
+                const uint32_t wp[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                for (int m = 0; m < kMaxVirtualRows; ++m) {
-                    if (m < M) {
-                        float xs[8];
-                        if (XF32) {
-                            const float4 *xp = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) +
-                                                                                 m * C + c);
-                            float4 a = __ldg(xp), b = __ldg(xp + 1);
-                            xs[0] = a.x; xs[1] = a.y; xs[2] = a.z; xs[3] = a.w;
-                            xs[4] = b.x; xs[5] = b.y; xs[6] = b.z; xs[7] = b.w;
-                        } else {
-                            uint4 xv = __ldg(reinterpret_cast<const uint4 *>(
-                                reinterpret_cast<const uint16_t *>(x) + m * C + c));
-                            uint32_t xp[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                xs[2 * k] = __uint_as_float(xp[k] << 16);
-                                xs[2 * k + 1] = __uint_as_float(xp[k] & 0xFFFF0000u);
-                            }
-                        }
+                for (int m = 0; m < MM; ++m) {
+                    float xs[8];
+                    if (XF32) {
+                        const float4 *xp =
+                            reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + m * C + c);
+                        const float4 a = __ldg(xp), b = __ldg(xp + 1);
+                        xs[0] = a.x; xs[1] = a.y; xs[2] = a.z; xs[3] = a.w;
+                        xs[4] = b.x; xs[5] = b.y; xs[6] = b.z; xs[7] = b.w;
+                    } else {
+                        const uint4 xv =
+                            __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + m * C + c));
+                        const uint32_t xp[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
-                            acc[m] = fmaf(xs[2 * k], __uint_as_float(wp[k] << 16), acc[m]);
-                            acc[m] = fmaf(xs[2 * k + 1], __uint_as_float(wp[k] & 0xFFFF0000u), acc[m]);
+                            xs[2 * k] = __uint_as_float(xp[k] << 16);
+                            xs[2 * k + 1] = __uint_as_float(xp[k] & 0xFFFF0000u);
                         }
                     }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        acc[m] = fmaf(xs[2 * k], __uint_as_float(wp[k] << 16), acc[m]);
+                        acc[m] = fmaf(xs[2 * k + 1], __uint_as_float(wp[k] & 0xFFFF0000u), acc[m]);
+                    }
                 }
+            };
+            // four 16-byte weight loads in flight per lane (streamed: the
+            // weights are read once, the activations stay cached)
+            int64_t c = (int64_t)lane * 8;
+            for (; c + 3 * 256 < C; c += 4 * 256) {
+                const uint4 w0 = __ldcs(reinterpret_cast<const uint4 *>(row + c));
+                const uint4 w1 = __ldcs(reinterpret_cast<const uint4 *>(row + c + 256));
+                const uint4 w2 = __ldcs(reinterpret_cast<const uint4 *>(row + c + 512));
+                const uint4 w3 = __ldcs(reinterpret_cast<const uint4 *>(row + c + 768));
+                step(c, w0);
+                step(c + 256, w1);
+                step(c + 512, w2);
+                step(c + 768, w3);
             }
+            for (; c < C; c += 256) step(c, __ldcs(reinterpret_cast<const uint4 *>(row + c)));
         } else {
             for (int64_t c = lane; c < C; c += 32) {
                 float wf = bf16_bits_to_f32(row[c]);
 #pragma unroll
-                for (int m = 0; m < kMaxVirtualRows; ++m)
-                    if (m < M) {
-                        float xv = XF32 ? reinterpret_cast<const float *>(x)[m * C + c]
-                                        : bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(x)[m * C + c]);
-                        acc[m] = fmaf(xv, wf, acc[m]);
-                    }
+                for (int m = 0; m < MM; ++m) {
+                    const float xv = XF32 ? reinterpret_cast<const float *>(x)[m * C + c]
+                                          : bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(x)[m * C + c]);
+                    acc[m] = fmaf(xv, wf, acc[m]);
+                }
             }
         }
 #pragma unroll
-        for (int m = 0; m < kMaxVirtualRows; ++m) {
+        for (int m = 0; m < MM; ++m) {
             float v = acc[m];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -320,14 +333,13 @@ __global__ void __launch_bounds__(256) gemv_raw_kernel(const uint16_t *w, int64_
         if (lane == 0) {
             const float bv = bias ? bf16_bits_to_f32(bias[r]) : 0.f;
 #pragma unroll
-            for (int m = 0; m < kMaxVirtualRows; ++m)
-                if (m < M) {
-                    float y = acc[m] + bv;
-                    if (out_f32)
-                        reinterpret_cast<float *>(out)[m * R + r] = y;
-                    else
-                        reinterpret_cast<uint16_t *>(out)[m * R + r] = f32_to_bf16_bits(y);
-                }
+            for (int m = 0; m < MM; ++m) {
+                const float y = acc[m] + bv;
+                if (out_f32)
+                    reinterpret_cast<float *>(out)[m * R + r] = y;
+                else
+                    reinterpret_cast<uint16_t *>(out)[m * R + r] = f32_to_bf16_bits(y);
+            }
         }
     }
 }
@@ -396,13 +408,26 @@ int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f3
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int64_t blocks = std::min<int64_t>((R + 7) / 8, (int64_t)sms * 8);
-    if (x_f32)
-        gemv_raw_kernel<1><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-            reinterpret_cast<const uint16_t *>(w), R, C, x, (int)M, bias, out, out_f32);
-    else
-        gemv_raw_kernel<0><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-            reinterpret_cast<const uint16_t *>(w), R, C, x, (int)M, bias, out, out_f32);
+    using Kern = void (*)(const uint16_t *, int64_t, int64_t, const void *, const uint16_t *, void *, int);
+    static const Kern kernels[2][8] = {
+        {gemv_raw_kernel<0, 1>, gemv_raw_kernel<0, 2>, gemv_raw_kernel<0, 3>, gemv_raw_kernel<0, 4>,
+         gemv_raw_kernel<0, 5>, gemv_raw_kernel<0, 6>, gemv_raw_kernel<0, 7>, gemv_raw_kernel<0, 8>},
+        {gemv_raw_kernel<1, 1>, gemv_raw_kernel<1, 2>, gemv_raw_kernel<1, 3>, gemv_raw_kernel<1, 4>,
+         gemv_raw_kernel<1, 5>, gemv_raw_kernel<1, 6>, gemv_raw_kernel<1, 7>, gemv_raw_kernel<1, 8>}};
+    if (M < 1 || M > 8) {
+        msg = "gemv_raw: 1..8 activation rows";
+        return DM_EINVAL;
+    }
+    // one wave: as many blocks as stay resident on every SM (the blocks loop
+    // over rows), no second partial wave
+    const Kern kern = kernels[x_f32 ? 1 : 0][M - 1];
+    static int resident[2][8] = {};
+    int &per_sm = resident[x_f32 ? 1 : 0][M - 1];
+    if (per_sm == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess)
+        per_sm = 4;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, (int64_t)sms * std::max(per_sm, 1)));
+    kern<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint16_t *>(w), R, C, x, bias, out, out_f32);
     return cuda_check(cudaGetLastError(), "gemv_raw_kernel", msg);
 }
 
