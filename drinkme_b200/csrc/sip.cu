@@ -817,18 +817,17 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         return DM_EINVAL;
     }
     // One CTA per SM, each a stream-K worker owning at least one unit; or,
-    // when the units are too few for the CTAs to own whole tiles (every tile
-    // would be shared and every launch would end in the cross-CTA fixup),
-    // CTAs that own whole tiles whenever that costs no more decode rounds
-    // than the fixup. The split depends on the tensor alone.
+    // CTAs that own whole tiles when the busiest of them would decode fewer
+    // units than a stream-K worker plus its cross-CTA fixup (worth about
+    // three units when a CTA's range holds under two tiles, four under one;
+    // measured on the Qwen3 8B and 32B shapes). The split depends on the
+    // tensor alone.
     const int64_t tiles = L.tiles;
     const int64_t gridA = std::min<int64_t>(t->sms, L.units), gridB = std::min<int64_t>(t->sms, tiles);
     const int64_t perA = (L.units + gridA - 1) / gridA;
-    const int64_t roundsA = (perA + kGroups - 1) / kGroups + (perA < 2 * L.NB ? 2 : 0);  // + the fixup at the end
-    const int64_t roundsB = (tiles + gridB - 1) / gridB * ((L.NB + kGroups - 1) / kGroups);
-    // (measured: with 12 or more units per CTA the stream-K split is 3-8 %
-    // faster even where whole tiles cost no more rounds)
-    const int tile_split = perA < 12 && roundsB <= roundsA ? 1 : 0;
+    const int64_t costA = perA + (perA < L.NB ? 4 : (perA < 2 * L.NB ? 3 : 0));
+    const int64_t costB = (tiles + gridB - 1) / gridB * L.NB;
+    const int tile_split = costB < costA ? 1 : 0;
     const int64_t grid = tile_split ? gridB : gridA;
     if (grid > max_workers || grid > kMaxGrid) {
         msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
