@@ -228,7 +228,6 @@ __device__ __forceinline__ void wait_inputs(const SipArgs &a) {
                 atomicExch(a.abort, 1u);
                 return;
             }
-            __nanosleep(128);
         }
     }
     fence_proxy_async_global();
