@@ -11,25 +11,28 @@
 //   * A CTA = 1 producer warp, 4 groups of 4 consumer warps and 1 epilogue
 //     warp, one CTA per SM. The CTA is a stream-K WORKER: the units (16 rows x
 //     1 block column, see layout.cpp) of the tensor in tile-major order are
-//     split evenly over the CTAs. Consecutive CTAs therefore share at most one
-//     tile at each boundary; the CTA processes those (at most two) PARTIAL
-//     tiles first and its whole tiles after them.
+//     split over the CTAs by a table of starts (the last CTAs to be
+//     dispatched get a little less). Consecutive CTAs therefore share at most
+//     one tile at each boundary; the CTA processes those (at most two)
+//     PARTIAL tiles first and its whole tiles after them. Small tensors use
+//     whole tiles per CTA instead.
 //   * The producer stages each unit with ONE 1-D bulk copy (the TMA engine)
-//     plus one 2 KB bulk copy per activation row of the unit's block column,
-//     into a ring of shared-memory slots, completing an mbarrier. Unit i of
-//     the CTA's sequence goes to group i mod 4; the 4 warps of the group
-//     share it, each decoding a quarter of its k range.
+//     into a ring of shared-memory slots, completing an mbarrier; the
+//     activations of every block column are either resident for the launch
+//     (RES) or staged with each unit (one 2 KB bulk copy per activation
+//     row). Unit i of the CTA's sequence goes to group i mod 4; the 4 warps
+//     of the group share it, each decoding a quarter of its k range.
 //   * A consumer decodes its unit straight into MMA operands: the weights
 //     are the A operand (m = 16 output rows) of mma.m16n8k16 bf16 with fp32
 //     accumulate, the activations the B operand (n = 8 = up to 8 activation
 //     rows). Lane (g, t) decodes rows g and g + 8 of the unit at
 //     k = 64q + 16t + [0, 16); warp w of a group takes q in [4w, 4w + 4).
-//   * Decode is byte-parallel: the 3-bit tier-0 codes are spread into
-//     nibbles with three AND + IMAD steps (the IMADs run on the FMA pipe,
-//     idle otherwise), then one PRMT per 4 weights looks four exponents up
-//     in an 8-byte table, and two LOP3 + two PRMT merge sign, exponent and
-//     mantissa into the bf16 pairs of the MMA operand. The table's escape
-//     entry makes a weight whose code is 7 decode to exactly +0.
+//   * Decode is byte-parallel: the tier-0 codes come from the loader's two
+//     code planes as PRMT selectors (a mask, a rotate and an OR per 8 codes),
+//     then one PRMT per 4 weights looks four exponents up in an 8-byte
+//     table, and two LOP3 + two PRMT merge sign, exponent and mantissa into
+//     the bf16 pairs of the MMA operand. The table's escape entry makes a
+//     weight whose code is 7 decode to exactly +0.
 //   * Escaped weights (about 2% of a N(0, 0.02) tensor) are added back as
 //     fp32 corrections: the loader's escape index lists each block's escape
 //     positions; the group's lanes split each row's escapes between them.
