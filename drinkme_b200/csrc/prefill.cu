@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <string>
 
 #include "dm_device.cuh"
@@ -453,14 +454,16 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
         return DM_EINVAL;
     }
     const int smem = kPfBStages * kBTile + kPfAStages * kPfMaxTiles * kATile + kPfRows * kPfEsc * 4 + 1024 + 256;
-    static bool attr = false;
-    if (!attr) {
+    // a per-device attribute: one bit per device (64 and up: every launch)
+    static std::atomic<uint64_t> attr{0};
+    const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
+    if (!dev_bit || !(attr.load() & dev_bit)) {
         cudaError_t e = cudaFuncSetAttribute(prefill_sip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
-        attr = true;
+        attr.fetch_or(dev_bit);
     }
     const int64_t grid = (L.rows + kPfRows - 1) / kPfRows;
     for (int64_t m0 = 0; m0 < M; m0 += (int64_t)kPfMaxTiles * kPfTok) {

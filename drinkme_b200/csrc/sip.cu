@@ -52,6 +52,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <string>
 
 #include "dm_device.cuh"
@@ -864,20 +865,23 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         {nullptr, sip_gemv_kernel<1, true>, sip_gemv_kernel<2, true>, sip_gemv_kernel<3, true>,
          sip_gemv_kernel<4, true>, sip_gemv_kernel<5, true>, sip_gemv_kernel<6, true>, sip_gemv_kernel<7, true>,
          sip_gemv_kernel<8, true>}};
-    static bool attr_set[2][kMaxVirtualRows + 1] = {};
+    // the shared-memory limit is a per-device attribute of each kernel: one
+    // bit per device (devices 64 and up set it on every launch)
+    static std::atomic<uint64_t> attr_set[2][kMaxVirtualRows + 1];
     const int res = xres_bytes > 0 ? 1 : 0;
+    const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
     const Kern kern = kernels[res][Mv];
     if (kern == nullptr) {
         msg = "sip kernel: no resident-activation kernel without activations";
         return DM_EINVAL;
     }
-    if (!attr_set[res][Mv]) {
+    if (!dev_bit || !(attr_set[res][Mv].load() & dev_bit)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
-        attr_set[res][Mv] = true;
+        attr_set[res][Mv].fetch_or(dev_bit);
     }
     SipArgs a{};
     a.data = t->d_data;
