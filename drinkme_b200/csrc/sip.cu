@@ -60,7 +60,7 @@
 
 namespace dm {
 
-constexpr int kMaxGrid = 160;  // CTAs of one launch, at most (one per SM)
+constexpr int kMaxGrid = 256;  // CTAs of one launch, at most (one per SM)
 
 struct SipArgs {
     const uint8_t *data;
