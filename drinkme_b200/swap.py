@@ -11,8 +11,12 @@ drop-in for the reference's ``drinkme.codec.swap`` module classes and loader
   RadixCompressedLinear           swap.py:395-456
   RawLinear                       swap.py:459-497
   NarrowLinear                    swap.py:530-626
+  stock_linear, StockLinear,      swap.py:660-849  the raw bf16 Linears'
+  stock_gemv_mode, raw_gemv_mode,                  one-row GEMV choice
+  install_stock_gemv, codec_tree
   make_module(pack, bias, device) swap.py:900-919
-  eligible                        swap.py:850-854
+  eligible, eligible_linears,     swap.py:850-897
+  swap_linears
 
 Routing (swap.py:302-335): M == 1 -> "gemv"; 2 <= M <= MC_MAX -> "mc"
 unless DRINKME_PREFILL_DENSE_MIN says dense; M >= GEMM_MIN_ROWS (9) ->
@@ -263,8 +267,12 @@ class RadixCompressedLinear(CompressedLinear):
 
 
 class RawLinear(CompressedLinear):
-    """The raw fallback (bf16 bits verbatim): the raw GEMV for 1..MC_MAX rows,
+    """The raw fallback (bf16 bits verbatim): stock_linear under the module's
+    stock GEMV mode — by default this package's raw GEMV for 1..MC_MAX rows,
     cuBLAS (F.linear) above."""
+
+    stock_gemv = "b200"
+    raw_gemv = None  # raw_gemv_dict's dict once install_stock_gemv has given one
 
     def __init__(self, runtime: dict, bias):
         if runtime.get("codec") != "raw":
@@ -277,18 +285,134 @@ class RawLinear(CompressedLinear):
 
     def forward(self, x):
         self._route(x)
-        return stock_linear(x, self.p["weight"], self.bias)
+        return stock_linear(x, self.p["weight"], self.bias, self.stock_gemv, self.raw_gemv)
 
 
-def stock_linear(x, weight, bias):
-    """A raw bf16 Linear's forward: up to MC_MAX rows through the raw GEMV
-    (fp32 accumulate, bias in fp32, one rounding), else F.linear."""
-    M = x.numel() // x.shape[-1]
-    if (x.device.type == "cuda" and 1 <= M <= MC_MAX and weight.dtype == torch.bfloat16
-            and x.dtype in (torch.bfloat16, torch.float32)):
+# The stock GEMV of a raw bf16 Linear's small-M call (swap.py:660-708): the
+# reference picks it per AMD gfx target ("linear", "mv", "triton"; "linear"
+# elsewhere). On B200 the default is "b200", this package's raw GEMV (the
+# Qwen3-8B lm_head, 151936 x 4096, one row: 180.8 us against cuBLAS's
+# 203.1 us); "triton", the reference's twin kernel, maps to the same kernel.
+# DRINKME_STOCK_GEMV overrides, with the reference's name and check.
+STOCK_GEMV_ENV = "DRINKME_STOCK_GEMV"
+STOCK_GEMV_MODES = ("linear", "mv", "triton", "b200")
+RAW_GEMV_ENV = "DRINKME_RAW_GEMV"
+RAW_GEMV_MODES = ("stock", "twin")
+
+
+def stock_gemv_mode(device) -> str:
+    """DRINKME_STOCK_GEMV when set to a mode, else "b200"; always "linear"
+    off the accelerator (swap.py:665-679)."""
+    spec = os.environ.get(STOCK_GEMV_ENV, "auto").strip() or "auto"
+    if spec not in ("auto",) + STOCK_GEMV_MODES:
+        raise ValueError(f"{STOCK_GEMV_ENV}={spec!r}: one of auto, {', '.join(STOCK_GEMV_MODES)}")
+    if not str(device).startswith("cuda"):
+        return "linear"
+    return "b200" if spec == "auto" else spec
+
+
+def raw_gemv_mode(device) -> str:
+    """DRINKME_RAW_GEMV when set to a mode, else "stock"; always "stock" off
+    the accelerator (swap.py:768-781). "twin" sends a codec tree's raw
+    Linears through this package's raw GEMV whatever the stock mode."""
+    spec = os.environ.get(RAW_GEMV_ENV, "auto").strip() or "auto"
+    if spec not in ("auto",) + RAW_GEMV_MODES:
+        raise ValueError(f"{RAW_GEMV_ENV}={spec!r}: one of auto, {', '.join(RAW_GEMV_MODES)}")
+    if not str(device).startswith("cuda"):
+        return "stock"
+    return "stock" if spec == "auto" else spec
+
+
+def codec_tree(model) -> bool:
+    """Does the tree hold a codec module (swap.py:784-789)?"""
+    return any(isinstance(m, CompressedLinear) for m in model.modules())
+
+
+def raw_gemv_dict(R: int, C: int) -> dict:
+    """The descriptor a raw [R, C] Linear's small-M call runs the raw GEMV
+    under (swap.py:792-803: the reference's twin-kernel launch row; this
+    kernel needs no schedule, so only the shape and the kernel's name)."""
+    return {"R": int(R), "C": int(C), "codec": "raw", "kernel": "gemv_raw_sm100a"}
+
+
+def stock_linear(x, weight, bias, mode: str = "b200", raw: dict | None = None):
+    """A raw bf16 Linear's forward under the stock GEMV `mode`
+    (swap.py:681-707): "b200" / "triton", or any `raw` descriptor, sends
+    1..MC_MAX rows on the accelerator through the raw GEMV (fp32 accumulate,
+    the bias added in fp32, one rounding); "mv" sends one row through
+    torch.mv (torch.addmv with a bias) with cuBLASLt preferred for the call;
+    everything else is F.linear."""
+    M = x.numel() // x.shape[-1] if x.numel() else 0
+    kernel = raw is not None or mode in ("b200", "triton")
+    if (kernel and x.device.type == "cuda" and 1 <= M <= MC_MAX and weight.dtype == torch.bfloat16
+            and x.dtype in (torch.bfloat16, torch.float32) and weight.is_contiguous()):
         y = radix_ops.gemv_raw(weight, x.reshape(M, -1), bias, x.dtype)
         return y.reshape(*x.shape[:-1], weight.shape[0])
-    return torch.nn.functional.linear(x, weight, bias)
+    if mode != "mv" or x.device.type != "cuda" or x.numel() != weight.shape[1]:
+        return torch.nn.functional.linear(x, weight, bias)
+    prev = torch._C._get_blas_preferred_backend()
+    torch._C._set_blas_preferred_backend(torch._C._BlasBackend.Cublaslt)
+    try:
+        v = x.reshape(-1)
+        y = torch.mv(weight, v) if bias is None else torch.addmv(bias, weight, v)
+    finally:
+        torch._C._set_blas_preferred_backend(prev)
+    return y.reshape(*x.shape[:-1], weight.shape[0])
+
+
+class StockLinear(torch.nn.Linear):
+    """A raw bf16 Linear with both dims >= 1024 (a tied lm_head, the stock
+    arm's Linears) whose forward is stock_linear's (swap.py:710-742): the
+    checkpoint's own Parameters, adopted without a copy."""
+
+    stock_gemv = "b200"
+    raw_gemv = None
+    MIN_DIM = 1024
+
+    @classmethod
+    def wants(cls, mod) -> bool:
+        if type(mod) is not torch.nn.Linear:
+            return False
+        w = mod.weight
+        return w.dtype == torch.bfloat16 and w.device.type == "cuda" and min(w.shape) >= cls.MIN_DIM
+
+    @classmethod
+    def adopt(cls, lin: torch.nn.Linear, mode: str) -> "StockLinear":
+        new = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, device="meta")
+        new.weight = lin.weight
+        new.bias = lin.bias
+        new.stock_gemv = mode
+        return new
+
+    def forward(self, x):
+        return stock_linear(x, self.weight, self.bias, self.stock_gemv, self.raw_gemv)
+
+
+def install_stock_gemv(model, device, mode: str, raw: str = "stock") -> int:
+    """The stock GEMV `mode` onto the tree (swap.py:806-847): every raw
+    Linear StockLinear wants is adopted and every StockLinear / RawLinear
+    told the mode; under "triton", or "twin" in a codec tree, each also gets
+    its raw_gemv_dict. Returns how many modules run a route; nothing off the
+    accelerator, or for "linear" without the raw GEMV."""
+    if not str(device).startswith("cuda"):
+        return 0
+    twin = mode == "triton" or (raw == "twin" and codec_tree(model))
+    if mode == "linear" and not twin:
+        return 0
+    done = 0
+    for _, parent in list(model.named_modules()):
+        for child_name, child in list(parent.named_children()):
+            if StockLinear.wants(child):
+                child = StockLinear.adopt(child, mode)
+                setattr(parent, child_name, child)
+            elif isinstance(child, (StockLinear, RawLinear)):
+                child.stock_gemv = mode
+            else:
+                continue
+            R, C = (child.out_features, child.in_features) if isinstance(child, StockLinear) else (child.R, child.C)
+            child.raw_gemv = raw_gemv_dict(R, C) if twin else None
+            done += 1
+    return done
 
 
 class NarrowLinear(torch.nn.Linear):
@@ -330,6 +454,41 @@ def eligible(child) -> bool:
         return False
     w = child.weight.data
     return w.dtype == torch.bfloat16 and w.shape[1] % 4 == 0 and min(w.shape) >= 1024
+
+
+def eligible_linears(model):
+    """(qualified name, parent, child name, module) of every Linear the codec
+    takes: eligible, and not weight-tied to an Embedding (swap.py:857-882).
+    Tied by Parameter identity (meta models: every storage pointer is 0),
+    or by storage on real ones; root-level names carry no leading dot."""
+    embs = [m.weight for m in model.modules() if isinstance(m, torch.nn.Embedding)]
+    tied_ids = {id(w) for w in embs}
+    tied_ptrs = {w.data_ptr() for w in embs if not w.is_meta}
+    for parent_name, parent in model.named_modules():
+        for child_name, child in list(parent.named_children()):
+            if not eligible(child):
+                continue
+            w = child.weight
+            if id(w) in tied_ids or (not w.is_meta and w.data_ptr() in tied_ptrs):
+                continue
+            yield (f"{parent_name}.{child_name}" if parent_name else child_name), parent, child_name, child
+
+
+def swap_linears(model, make, device="cuda"):
+    """Replace every eligible Linear with make(cpu_weight, bias) -> (module,
+    stat), dropping the old weight's storage (swap.py:885-897). Returns the
+    stats, each named."""
+    stats = []
+    for name, parent, child_name, child in list(eligible_linears(model)):
+        w = child.weight.data
+        bias = child.bias.data.to(device) if child.bias is not None else None
+        mod, stat = make(w, bias)
+        setattr(parent, child_name, mod)
+        child.weight.data = torch.empty(0)
+        if stat:
+            stat["name"] = name
+            stats.append(stat)
+    return stats
 
 
 def make_module(pack: dict, bias, device="cuda", row_begin: int = 0, row_end: int | None = None):

@@ -206,3 +206,69 @@ def test_cpu_inputs_are_refused_not_served():
         m(torch.zeros(1, 8))
     with pytest.raises(ValueError, match="CUDA"):
         swap.to_device_radix({"R": 1}, "cpu")
+
+
+def test_stock_and_raw_gemv_modes(monkeypatch):
+    """The reference's mode parsing (swap.py:665-781): an unknown mode is a
+    ValueError naming the variable; off the accelerator the stock GEMV is
+    F.linear and the raw GEMV "stock"; on it the defaults are this
+    package's raw kernel ("b200") and "stock"."""
+    from drinkme_b200 import swap
+
+    monkeypatch.delenv(swap.STOCK_GEMV_ENV, raising=False)
+    monkeypatch.delenv(swap.RAW_GEMV_ENV, raising=False)
+    assert swap.stock_gemv_mode("cpu") == "linear"
+    assert swap.stock_gemv_mode("cuda:0") == "b200"
+    assert swap.raw_gemv_mode("cpu") == "stock" and swap.raw_gemv_mode("cuda:1") == "stock"
+    monkeypatch.setenv(swap.STOCK_GEMV_ENV, "mv")
+    assert swap.stock_gemv_mode("cuda:0") == "mv" and swap.stock_gemv_mode("cpu") == "linear"
+    monkeypatch.setenv(swap.STOCK_GEMV_ENV, "fast")
+    with pytest.raises(ValueError, match="DRINKME_STOCK_GEMV"):
+        swap.stock_gemv_mode("cuda:0")
+    monkeypatch.setenv(swap.RAW_GEMV_ENV, "twin")
+    assert swap.raw_gemv_mode("cuda:0") == "twin"
+    monkeypatch.setenv(swap.RAW_GEMV_ENV, "x")
+    with pytest.raises(ValueError, match="DRINKME_RAW_GEMV"):
+        swap.raw_gemv_mode("cuda:0")
+
+
+def test_stock_linear_off_the_accelerator_is_f_linear():
+    import torch
+
+    from drinkme_b200 import swap
+
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(64, 1024, generator=g).to(torch.bfloat16)
+    b = torch.randn(64, generator=g).to(torch.bfloat16)
+    x = torch.randn(2, 1024, generator=g).to(torch.bfloat16)
+    want = torch.nn.functional.linear(x, w, b)
+    for mode in swap.STOCK_GEMV_MODES:
+        assert torch.equal(swap.stock_linear(x, w, b, mode), want)
+    assert torch.equal(swap.stock_linear(x, w, b, "b200", swap.raw_gemv_dict(64, 1024)), want)
+
+
+def test_eligible_linears_skip_tied_heads_and_swap_replaces():
+    """The tied-lm_head rule by Parameter identity (works on meta models too)
+    and the swap walker (swap.py:857-897)."""
+    import torch
+
+    from drinkme_b200 import swap
+
+    class Tiny(torch.nn.Module):
+        def __init__(self, device):
+            super().__init__()
+            self.embed = torch.nn.Embedding(2048, 1024, device=device, dtype=torch.bfloat16)
+            self.proj = torch.nn.Linear(1024, 1024, bias=True, device=device, dtype=torch.bfloat16)
+            self.small = torch.nn.Linear(1024, 64, device=device, dtype=torch.bfloat16)
+            self.lm_head = torch.nn.Linear(1024, 2048, bias=False, device=device, dtype=torch.bfloat16)
+            self.lm_head.weight = self.embed.weight
+
+    for device in ("meta", "cpu"):
+        names = [n for n, *_ in swap.eligible_linears(Tiny(device))]
+        assert names == ["proj"], (device, names)
+    m = Tiny("cpu")
+    stats = swap.swap_linears(m, lambda w, b: (torch.nn.Identity(), {"rows": w.shape[0]}), device="cpu")
+    assert isinstance(m.proj, torch.nn.Identity) and isinstance(m.lm_head, torch.nn.Linear)
+    assert stats == [{"rows": 1024, "name": "proj"}]
+    assert not swap.codec_tree(m)
+    assert swap.install_stock_gemv(m, "cpu", "b200") == 0
