@@ -10,7 +10,7 @@ drop-in for the reference's ``drinkme.codec.swap`` module classes and loader
   CompressedLinear                swap.py:228-392  routing by M, epilogue
   RadixCompressedLinear           swap.py:395-456
   RawLinear                       swap.py:459-497
-  NarrowLinear                    swap.py:530-626
+  NarrowLinear, install_narrow    swap.py:530-626
   stock_linear, StockLinear,      swap.py:660-849  the raw bf16 Linears'
   stock_gemv_mode, raw_gemv_mode,                  one-row GEMV choice
   install_stock_gemv, codec_tree
@@ -447,6 +447,21 @@ class NarrowLinear(torch.nn.Linear):
             return torch.nn.functional.linear(x, self.weight, self.bias)
         y = radix_ops.gemv_narrow(self.weight, xm, self.bias, self.BLOCK, self.NUM_WARPS)
         return y.reshape(*shape[:-1], self.out_features)
+
+
+def install_narrow(model, device) -> list[tuple[str, tuple[int, int]]]:
+    """Every raw Linear NarrowLinear wants, adopted in place; the (name,
+    (R, C)) list of what was done (swap.py:613-626). Nothing off the
+    accelerator, nothing the codec holds."""
+    if not str(device).startswith("cuda"):
+        return []
+    done = []
+    for parent_name, parent in list(model.named_modules()):
+        for child_name, child in list(parent.named_children()):
+            if NarrowLinear.wants(child):
+                setattr(parent, child_name, NarrowLinear.adopt(child))
+                done.append((f"{parent_name}.{child_name}" if parent_name else child_name, tuple(child.weight.shape)))
+    return done
 
 
 def eligible(child) -> bool:

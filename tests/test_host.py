@@ -272,3 +272,4 @@ def test_eligible_linears_skip_tied_heads_and_swap_replaces():
     assert stats == [{"rows": 1024, "name": "proj"}]
     assert not swap.codec_tree(m)
     assert swap.install_stock_gemv(m, "cpu", "b200") == 0
+    assert swap.install_narrow(m, "cpu") == []
