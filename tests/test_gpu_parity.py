@@ -410,3 +410,30 @@ def test_repeated_calls_are_bitwise_deterministic(runtimes, golden):
 def test_no_device_errors_recorded(runtimes):
     for name, rt in runtimes.items():
         assert rt["rx_handle"].device_error() == 0, name
+
+
+def test_stock_linear_modes_on_the_gpu(monkeypatch):
+    """The raw Linears' one-row routes (swap.py:681-742): "b200" / "triton"
+    and a raw descriptor run the raw GEMV (fp32 accumulate, bias, one
+    rounding: bitwise dm_gemv_raw), "mv" torch.mv under cuBLASLt, "linear"
+    F.linear; all within bf16 rounding of a float64 reference, and M = 9
+    always F.linear. StockLinear adopts a Linear without a copy."""
+    g = torch.Generator().manual_seed(9)
+    w = (torch.randn(2048, 1024, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    b = (torch.randn(2048, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    x = torch.randn(1, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    ref = (x.double() @ w.double().t() + b.double()).float()
+    raw = radix_ops.gemv_raw(w, x, b, torch.bfloat16)
+    for mode, r in (("b200", None), ("triton", None), ("linear", swap.raw_gemv_dict(2048, 1024))):
+        assert torch.equal(swap.stock_linear(x, w, b, mode, r), raw), mode
+    for mode in ("mv", "linear"):
+        y = swap.stock_linear(x, w, b, mode)
+        assert y.shape == (1, 2048) and y.dtype == torch.bfloat16
+        assert torch.allclose(y.float(), ref, rtol=2 ** -7, atol=1e-3), mode
+    x9 = torch.randn(9, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    assert torch.equal(swap.stock_linear(x9, w, b, "b200"), torch.nn.functional.linear(x9, w, b))
+    lin = torch.nn.Linear(1024, 2048, device=DEV, dtype=torch.bfloat16)
+    model = torch.nn.Sequential(lin)
+    assert swap.install_stock_gemv(model, DEV, "b200") == 1
+    assert isinstance(model[0], swap.StockLinear) and model[0].weight is lin.weight
+    assert torch.equal(model[0](x), swap.stock_linear(x, lin.weight, lin.bias, "b200"))
