@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import all_patterns, pack_of, radix_names, sha
+from conftest import all_patterns, pack_of, sha
 from drinkme_b200 import codec
 
 
