@@ -46,6 +46,8 @@ WORKLOADS = {
                                                        ("up", 12288, 4096), ("down", 4096, 12288)],
                      head=(151936, 4096)),
 }
+# the headline metric, printed alike by both arms (BASELINE.json "metric")
+METRIC = "decode tokens/s @ batch 1 + fused decode-GEMV HBM GB/s (% of B200 peak), 1/2/4/8 GPU"
 # which input each linear reads: the hidden state (the step's H2D input) or
 # the attention / MLP intermediate (a resident synthetic activation)
 HIDDEN_INPUT = {"q", "k", "v", "gate", "up"}
@@ -426,44 +428,75 @@ def _graph_us(fn, device, reps=10):
     return us
 
 
+def rotated_linear_us(profile, Ms, device):
+    """µs per call of every Qwen3-8B linear on its own (one launch per linear,
+    no fusion) for each activation row count in `Ms`: the shape's pack
+    cloned into enough HBM copies to exceed 3x L2, one CUDA graph over the
+    copies. Returns ({name: {M: us}}, {name: (read_bytes, device_bytes, bpw)})."""
+    import torch
+
+    from drinkme_b200 import codec, radix_ops, swap
+
+    us, meta = {}, {}
+    for j, (name, R, C) in enumerate(WORKLOADS["qwen3-8b"]["linears"]):
+        bits = make_bits(R, C, seed=1000 + j, device=device)
+        p = codec.pack_array_radix(bits, profile)
+        rt0 = swap.to_device_radix(p, device)
+        n = max(3, int(3 * 126e6 // radix_ops.read_bytes(rt0)) + 1)
+        rts = [rt0] + [dict(rt0, rx_handle=rt0["rx_handle"].clone()) for _ in range(n - 1)]
+        meta[name] = (radix_ops.read_bytes(rt0), int(rt0["rx_handle"].info.device_bytes_per_call), p["bpw"])
+        for M in Ms:
+            g = torch.Generator(device=device)
+            x = torch.cat([torch.randn((1, C), generator=g.manual_seed(100 + m), device=device)
+                           for m in range(M)]).to(torch.bfloat16)
+            outs = [torch.empty((M, R), dtype=torch.bfloat16, device=device) for _ in rts]
+            us.setdefault(name, {})[M] = _graph_us(
+                lambda: [radix_ops.gemv_into(rt, x, None, o) for rt, o in zip(rts, outs)], device) / n
+        del rts, outs, bits, p
+        torch.cuda.empty_cache()
+    return us, meta
+
+
 def config3_gulp_mc(device, peak):
     """the Qwen3-8B linears packed gulp, through the
     narrow linear (radix_ops.gemv_mc_fused) with M = 2, 4, 8 rows (and M = 1
     beside them): µs per linear summed over one layer's seven linears, each
     shape rotated over copies larger than 3x L2, and the GB/s on the gulp
     read_bytes (the loader serves gulp through the sip kernels)."""
-    import numpy as np
-    import torch
-
-    from drinkme_b200 import codec, radix_ops, swap
-
-    res, total_bytes = {}, 0
-    rows = {M: 0.0 for M in (1, 2, 4, 8)}
-    for j, (name, R, C) in enumerate(WORKLOADS["qwen3-8b"]["linears"]):
-        bits = make_bits(R, C, seed=1000 + j, device=device)
-        p = codec.pack_array_radix(bits, "gulp")
-        rt0 = swap.to_device_radix(p, device)
-        n = max(3, int(3 * 126e6 // radix_ops.read_bytes(rt0)) + 1)
-        rts = [rt0] + [dict(rt0, rx_handle=rt0["rx_handle"].clone()) for _ in range(n - 1)]
-        total_bytes += radix_ops.read_bytes(rt0)
-        for M in rows:
-            g = torch.Generator(device=device)
-            x = torch.cat([torch.randn((1, C), generator=g.manual_seed(100 + m), device=device)
-                           for m in range(M)]).to(torch.bfloat16)
-            outs = [torch.empty((M, R), dtype=torch.bfloat16, device=device) for _ in rts]
-            us = _graph_us(lambda: [radix_ops.gemv_into(rt, x, None, o) for rt, o in zip(rts, outs)], device) / n
-            rows[M] += us
-            res.setdefault(name, {})[f"M{M}_us"] = round(us, 2)
-        res[name]["bpw"] = p["bpw"]
-        res[name]["device_bytes_per_call"] = int(rt0["rx_handle"].info.device_bytes_per_call)
-        del rts, outs, bits, p
-        torch.cuda.empty_cache()
-    summary = {f"M{M}": {"layer_us": round(us, 2), "gulp_gbs": round(total_bytes / us * 1e-3, 1),
-                         "frac_of_peak": round(total_bytes / us * 1e-3 / peak, 4),
-                         "us_per_row": round(us / M, 2)} for M, us in rows.items()}
+    Ms = (1, 2, 4, 8)
+    us, meta = rotated_linear_us("gulp", Ms, device)
+    total_bytes = sum(m[0] for m in meta.values())
+    rows = {M: sum(us[n][M] for n in us) for M in Ms}
+    res = {n: {**{f"M{M}_us": round(us[n][M], 2) for M in Ms}, "bpw": meta[n][2],
+               "device_bytes_per_call": meta[n][1]} for n in us}
+    summary = {f"M{M}": {"layer_us": round(t, 2), "gulp_gbs": round(total_bytes / t * 1e-3, 1),
+                         "frac_of_peak": round(total_bytes / t * 1e-3 / peak, 4),
+                         "us_per_row": round(t / M, 2)} for M, t in rows.items()}
     return {"config": "BASELINE configs[2]: Qwen3-8B linears packed gulp, M = 2/4/8 activation rows",
             "per_layer": summary, "per_linear": res,
             "note": "gulp packs with whole 1024-weight blocks are re-encoded as sip by the loader (same bits)"}
+
+
+def vs_cublas_8b(device, peak):
+    """north_star's M = 1 comparison on Qwen3-8B shapes: every linear (sip,
+    one launch each) against cuBLAS dense bf16 (F.linear) on the uncompressed
+    weight of the same shape, both rotated over copies larger than 3x L2.
+    BF16-equivalent GB/s = R * C * 2 / time; ratio = cuBLAS µs / ours."""
+    us, meta = rotated_linear_us("sip", (1,), device)
+    cb = cublas_arm(WORKLOADS["qwen3-8b"]["linears"], device)
+    out = {}
+    for name, R, C in WORKLOADS["qwen3-8b"]["linears"]:
+        ours = us[name][1]
+        nbytes = meta[name][0] + C * 2 + R * 2
+        out[name] = {"shape": [R, C], "ours_us": round(ours, 2), "cublas_us": cb[name]["us"],
+                     "ratio_vs_cublas": round(cb[name]["us"] / ours, 3),
+                     "ours_bf16_equiv_gbs": round(R * C * 2 / ours * 1e-3, 1),
+                     "cublas_gbs": cb[name]["gbs"], "compressed_gbs": round(nbytes / ours * 1e-3, 1),
+                     "frac_of_peak": round(nbytes / ours * 1e-3 / peak, 4)}
+    t_ours = sum(v["ours_us"] for v in out.values())
+    t_cb = sum(v["cublas_us"] for v in out.values())
+    return {"config": "Qwen3-8B linears at M = 1, sip, one launch per linear, vs cuBLAS bf16 F.linear",
+            "per_linear": out, "layer_ratio_vs_cublas": round(t_cb / t_ours, 3)}
 
 
 def config5_prefill(device):
@@ -531,52 +564,103 @@ def cublas_arm(shapes, device, reps=20):
 
 # --------------------------------------------------------- CPU reference --
 
-def cpu_reference_sample(wl, budget_s=20.0, layers_sample=1):
-    """The reference's CPU route (swap.CompressedLinear "cpu", swap.py:344-352)
-    on a bounded sample: one layer's linears packed, decoded once with the
-    reference's native decoder (oracle/_ref, else the oracle port), then
-    torch F.linear over the decoded bf16 weights (the steady state) timed.
-    Returns (tokens/s scaled to the whole stack, kind, cores, sample text,
-    cold-decode seconds)."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def cpu_reference(wl, steps, warmup, log=lambda m: None):
+    """The reference's CPU route on the host (swap.CompressedLinear "cpu",
+    swap.py:344-352): every linear decoded once by the reference's own native
+    decoder (radix_pack.decode_back_radix -> radix_native.decode, compiled
+    from its sources into oracle/_ref), then torch F.linear over the cached
+    bf16 weight on every call. Weights are packed by the reference's own
+    native encoder (radix_native plan + encode), never by this package, whose
+    library this arm does not load.
+
+    A step is one token of the named stack: the 7 linears of one layer,
+    decoded once, run layers (64) times, i.e. the whole stack's F.linear work;
+    the one layer's weights (about 1 GB for Qwen3-32B) are far larger than
+    the host's last-level cache, so every pass streams them from DRAM as
+    distinct layers would. `warmup` untimed steps, then `steps` timed ones,
+    every host thread. Returns (tokens/s, fields)."""
     import numpy as np
     import torch
 
-    from drinkme_b200 import codec
     from oracle import oracle
 
     spec = WORKLOADS[wl]
-    torch.set_num_threads(os.cpu_count() or 1)  # every host thread, also under torchrun
-    kind = "reference" if oracle.reference_native() is not None else "port"
-    ws, xs = [], {}
-    cold = 0.0
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)  # every host thread, also under torchrun
+    if oracle.reference_native() is None:
+        raise RuntimeError("the reference's native codec is not built (make -C oracle REF_SRC=...)")
     g = torch.Generator().manual_seed(7)
-    for j, (name, R, C) in enumerate(spec["linears"]):
+    ws, xs, packs = [], {}, []
+    t_pack = t_dec = 0.0
+    for name, R, C in spec["linears"]:
         w = (torch.randn(R, C, generator=g) * 0.02).to(torch.bfloat16)
-        bits = codec.bits_of(w)
-        p = codec.pack_array_radix(bits, "sip")
+        bits = w.view(torch.int16).numpy().view(np.uint16)
         t0 = time.perf_counter()
-        dec = oracle.reference_decode(p) if kind == "reference" else oracle.decode(p)
-        cold += time.perf_counter() - t0
+        p = oracle.reference_encode(bits, (3, 8))
+        t1 = time.perf_counter()
+        dec = oracle.reference_decode(p)  # single-threaded, the route's first call
+        t_dec += time.perf_counter() - t1
+        t_pack += t1 - t0
+        assert np.array_equal(dec, bits), f"{name}: the reference's decode differs from the source bits"
         ws.append(torch.from_numpy(dec.view(np.int16)).view(torch.bfloat16))
+        packs.append(p)
         if C not in xs:
             xs[C] = torch.randn(1, C, generator=g).to(torch.bfloat16)
-        del w, bits, p
-    for w in ws:
-        torch.nn.functional.linear(xs[w.shape[1]], w)
-    n = 0
+        del w
+    log(f"reference CPU: packed one layer in {t_pack:.1f}s, decoded in {t_dec:.1f}s")
+    nweights = sum(int(w.numel()) for w in ws)
+    # decode throughput, one thread and every thread (radix_native.decode workers=1 / N)
+    big = max(range(len(packs)), key=lambda i: ws[i].numel())
     t0 = time.perf_counter()
-    while True:
-        for w in ws:
-            torch.nn.functional.linear(xs[w.shape[1]], w)
-        n += 1
-        if time.perf_counter() - t0 > min(budget_s, 5.0) or n >= 50:
-            break
-    per_layer = (time.perf_counter() - t0) / n
-    tok_s = 1.0 / (per_layer * spec["layers"] / layers_sample)
-    cores = torch.get_num_threads()
-    sample = (f"{layers_sample} of {spec['layers']} layers ({len(ws)} linears), steady state: F.linear over the "
-              f"decoded bf16 weights x {n} passes; cold decode of the sample {cold:.2f}s single-thread")
-    return tok_s, kind, cores, sample, cold
+    oracle.reference_decode_threads(packs[big], 1)
+    d1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    oracle.reference_decode_threads(packs[big], cores)
+    dn = time.perf_counter() - t0
+    # cold call of the largest linear: decode + the first F.linear
+    t0 = time.perf_counter()
+    wc = torch.from_numpy(oracle.reference_decode(packs[big]).view(np.int16)).view(torch.bfloat16)
+    torch.nn.functional.linear(xs[wc.shape[1]], wc)
+    cold = time.perf_counter() - t0
+    del packs, wc
+
+    def step():
+        for _ in range(spec["layers"]):
+            for w in ws:
+                torch.nn.functional.linear(xs[w.shape[1]], w)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    secs = time.perf_counter() - t0
+    tok_s = steps / secs
+    fields = {
+        "cores": torch.get_num_threads(), "os_cpu_count": cores, "cpu_model": cpu_model(),
+        "cold_call_s": round(cold, 4),
+        "decode_weights_per_s_workers1": round(ws[big].numel() / d1, 1),
+        "decode_weights_per_s_workersN": round(ws[big].numel() / dn, 1), "decode_workers_N": cores,
+        "sample": (f"one token of the {spec['layers']}-layer stack per step: one layer's {len(ws)} linears "
+                   f"({nweights / 1e6:.0f}M weights, packed and decoded by the reference's own native codec) "
+                   f"run {spec['layers']} times through torch F.linear on {torch.get_num_threads()} threads "
+                   f"({warmup} warm-up + {steps} timed steps; the layer's bf16 weights stream from DRAM every "
+                   f"pass)"),
+    }
+    return tok_s, fields
 
 
 # ------------------------------------------------------------------ main --
@@ -599,14 +683,16 @@ def main():
     if a.impl == "reference":
         if rank != 0:
             return 0
-        tok_s, kind, cores, sample, cold = cpu_reference_sample(a.workload)
-        line = {"metric": "decode tokens/s @ batch 1", "value": round(tok_s, 4), "unit": "tokens/s",
+        log = (lambda m: print(f"[bench] {m}", file=sys.stderr, flush=True))
+        tok_s, f = cpu_reference(a.workload, a.steps, a.warmup, log)
+        line = {"metric": METRIC, "value": round(tok_s, 4), "unit": "tokens/s",
                 "impl": "reference", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
                 "ms_per_step": round(1e3 / tok_s, 3), "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,0.02) weights packed sip",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: N(0,0.02) bf16 weights packed sip by the reference's native encoder, "
+                        "N(0,1) bf16 activations",
                 "config": base_config,
-                "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
-                                 "sample": sample},
+                "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "kind": "reference", **f},
                 "e2e": {"value": round(tok_s, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -657,7 +743,7 @@ def main():
     if rank == 0:
         tok_s = 1e3 / ms
         result = {
-            "metric": "decode tokens/s @ batch 1 + fused decode-GEMV HBM GB/s (% of B200 peak)",
+            "metric": METRIC,
             "value": round(tok_s, 3), "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic: N(0,0.02) bf16 weights packed sip (byte-identical encoder), "
@@ -702,12 +788,12 @@ def main():
                                                         "frac_of_peak": round(hb / h_us * 1e-3 / peak, 4),
                                                         "cublas_us": round(h_cublas, 2)}}
         if not a.no_configs:
+            result["vs_cublas_8b_m1"] = vs_cublas_8b(device, peak)
             result["config3_gulp_mc"] = config3_gulp_mc(device, peak)
             result["config5_prefill"] = config5_prefill(device)
         if not a.no_cpu:
-            tok_s, kind, cores, sample, cold = cpu_reference_sample(a.workload)
-            result["cpu_baseline"] = {"value": round(tok_s, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
-                                      "sample": sample}
+            tok_s, f = cpu_reference(a.workload, 3, 1, log)
+            result["cpu_baseline"] = {"value": round(tok_s, 4), "unit": "tokens/s", "kind": "reference", **f}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

@@ -19,7 +19,7 @@ DM_MAX_RANKS = 8
 EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
            "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_tensor_check",
-           "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
+           "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_tensor_set_launch", "dm_gemv_plan", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
 
 
 class DrinkmeError(RuntimeError):
@@ -35,7 +35,7 @@ class TensorInfo(ct.Structure):
                 ("block_size", ct.c_int32), ("nwidths", ct.c_int32), ("widths", ct.c_int32 * 8),
                 ("nblocks", ct.c_int64), ("payload_words", ct.c_int64), ("read_bytes", ct.c_int64),
                 ("resident_bytes", ct.c_int64), ("fast_path", ct.c_int32), ("device", ct.c_int32),
-                ("device_bytes_per_call", ct.c_int64)]
+                ("device_bytes_per_call", ct.c_int64), ("layout_ptr", ct.c_uint64), ("layout_bytes", ct.c_int64)]
 
 
 class PackPart(ct.Structure):
@@ -46,12 +46,23 @@ class PackPart(ct.Structure):
                 ("block_size", ct.c_int32), ("row_begin", ct.c_int64), ("row_end", ct.c_int64)]
 
 
+class Launch(ct.Structure):
+    """dm_launch: a sip tensor's launch knobs."""
+    _fields_ = [("slots", ct.c_int32), ("split", ct.c_int32), ("skew", ct.c_int32), ("resident", ct.c_int32)]
+
+
+class LaunchPlan(ct.Structure):
+    """dm_launch_plan: what a GEMV launch would be."""
+    _fields_ = [("grid", ct.c_int32), ("split", ct.c_int32), ("slots", ct.c_int32), ("resident", ct.c_int32),
+                ("smem_bytes", ct.c_int32), ("skew_step", ct.c_int32)]
+
+
 class Gather(ct.Structure):
     """dm_gather: the fused NVLink output gather of one row-sharded linear."""
     _fields_ = [("world", ct.c_int32), ("rank", ct.c_int32), ("slot", ct.c_int64),
                 ("peer_out", ct.c_void_p * DM_MAX_RANKS), ("peer_flags", ct.c_void_p * DM_MAX_RANKS),
                 ("gen", ct.c_void_p), ("done", ct.c_void_p), ("wait_flags", ct.c_void_p), ("wait_gen", ct.c_void_p),
-                ("abort", ct.c_void_p)]
+                ("abort", ct.c_void_p), ("wait_polls", ct.c_uint32)]
 
 
 _LIB = None
@@ -89,6 +100,8 @@ def lib():
         L.dm_ipc_close.argtypes = [p, cp, sz]
         L.dm_device_alloc.argtypes = [i32, sz, ct.POINTER(p), cp, sz]
         L.dm_device_free.argtypes = [p, cp, sz]
+        L.dm_tensor_set_launch.argtypes = [p, ct.POINTER(Launch), cp, sz]
+        L.dm_gemv_plan.argtypes = [p, i64, i32, ct.POINTER(LaunchPlan), cp, sz]
         for name in EXPORTS:
             getattr(L, name).restype = ct.c_int
         L.dm_prefill_workspace_bytes.restype = ct.c_int64

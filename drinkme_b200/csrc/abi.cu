@@ -234,6 +234,7 @@ extern "C" int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err,
     t->device = src->device;
     t->L = src->L;
     t->sms = src->sms;
+    t->K = src->K;
     t->data_bytes = src->data_bytes;
     t->S.max_workers = src->S.max_workers;
     cudaError_t e;
@@ -288,6 +289,8 @@ extern "C" int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info) {
     info->resident_bytes = (int64_t)t->resident_bytes;
     info->fast_path = t->L.fast_sip ? 1 : 0;
     info->device = t->device;
+    info->layout_ptr = reinterpret_cast<uint64_t>(t->d_data);
+    info->layout_bytes = (int64_t)t->data_bytes;
     return DM_OK;
 }
 
@@ -299,34 +302,51 @@ extern "C" int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64
                     "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
     if ((x_dtype != DM_BF16 && x_dtype != DM_F32) || (out_dtype != DM_BF16 && out_dtype != DM_F32))
         return fail(err, err_len, DM_EINVAL, "dm_gemv: dtype must be DM_BF16 or DM_F32");
+    if ((reinterpret_cast<uintptr_t>(x) & (x_dtype == DM_F32 ? 3u : 1u)) != 0)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv: activations not aligned to their element size");
     DeviceGuard g(t->device);
     std::string msg;
     const uint16_t *b16 = reinterpret_cast<const uint16_t *>(bias);
     const int of32 = out_dtype == DM_F32;
-    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    int rc;
-    if (t->L.fast_sip && aligned) {
-        if (x_dtype == DM_BF16) {
-            rc = dm::launch_gemv_sip(t, reinterpret_cast<const uint16_t *>(x), t->L.C, (int)M, 1, (int)M, b16, out,
-                                     of32, stream, msg);
-        } else {
-            rc = DM_OK;
-            const size_t esz = of32 ? 4 : 2;
-            for (int64_t m0 = 0; m0 < M && rc == DM_OK; m0 += 2) {
-                const int64_t mm = std::min<int64_t>(2, M - m0);
-                rc = dm::launch_split_f32(reinterpret_cast<const float *>(x) + m0 * t->L.C, t->L.C, mm, t->S.xsplit,
-                                          stream, msg);
-                if (rc == DM_OK)
-                    rc = dm::launch_gemv_sip(t, t->S.xsplit, t->L.C, (int)(3 * mm), 3, (int)mm, b16,
-                                             reinterpret_cast<uint8_t *>(out) + (size_t)m0 * t->L.rows * esz, of32,
-                                             stream, msg);
-            }
-        }
-    } else if (t->L.nparts > 1) {
-        return fail(err, err_len, DM_EINVAL, "dm_gemv: a fused tensor needs 16-byte aligned activations");
-    } else {
-        rc = dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);
-    }
+    // a sip tensor is served by the sip kernel at any activation alignment
+    // (unaligned bf16 rows are copied to the tensor's staging buffer first);
+    // the general kernel reads only plain-stream layouts
+    const int rc = t->L.fast_sip
+                       ? dm::gemv_sip_rows(t, x, x_dtype == DM_F32, M, b16, out, of32, t->S.xsplit, 6 * t->L.C,
+                                           t->S.partials, t->S.counters, t->S.max_workers, stream, msg)
+                       : dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_tensor_set_launch(dm_tensor *t, const dm_launch *l, char *err, size_t err_len) {
+    if (!t || !l) return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: null pointer");
+    if (l->slots < 0 || l->slots > 6)
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: slots must be 0 (measured rule) or 1..6");
+    if (l->split < 0 || l->split > 2)
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: split must be 0 (auto), 1 (stream-K) or 2 (tiles)");
+    if (l->skew < -1 || l->skew > 64)
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: skew must be -1 (default) or 0..64");
+    if (l->resident < -1 || l->resident > 16)
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: resident must be -1 (default) or 0..16");
+    t->K.slots = l->slots;
+    t->K.split = l->split;
+    t->K.skew = l->skew;
+    t->K.resident = l->resident;
+    return DM_OK;
+}
+
+extern "C" int dm_gemv_plan(const dm_tensor *t, int64_t M, int32_t x_dtype, dm_launch_plan *plan, char *err,
+                            size_t err_len) {
+    if (!t || !plan) return fail(err, err_len, DM_EINVAL, "dm_gemv_plan: null pointer");
+    if (M < 1 || M > DM_MC_MAX)
+        return fail(err, err_len, DM_EINVAL,
+                    "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
+    if (!t->L.fast_sip) return fail(err, err_len, DM_EINVAL, "dm_gemv_plan: not a sip fast-path tensor");
+    std::memset(plan, 0, sizeof(*plan));
+    std::string msg;
+    const int Mv = x_dtype == DM_F32 ? (int)(3 * std::min<int64_t>(2, M)) : (int)M;
+    const int rc = dm::gemv_plan(t, Mv, plan, msg);
     if (rc) dm::set_error(err, err_len, msg);
     return rc;
 }
@@ -362,9 +382,8 @@ extern "C" int dm_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, i
     if (R <= 0 || C <= 0) return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: empty weight");
     if ((x_dtype != DM_BF16 && x_dtype != DM_F32) || (out_dtype != DM_BF16 && out_dtype != DM_F32))
         return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: dtype must be DM_BF16 or DM_F32");
-    const bool vec_ok = (C % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
-    if (!vec_ok && (C % 8 == 0))
-        return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: weight and activations must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(x) & (x_dtype == DM_F32 ? 3u : 1u)))
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_raw: weight or activations not aligned to their element size");
     std::string msg;
     int rc = dm::launch_gemv_raw(w, R, C, x, x_dtype == DM_F32, M, reinterpret_cast<const uint16_t *>(bias), out,
                                  out_dtype == DM_F32, stream, msg);

@@ -69,10 +69,21 @@ struct TensorLayout {
     int32_t tier_table[8] = {0};
 };
 
+// Launch knobs of the sip kernels (dm_tensor_set_launch): negative or zero
+// fields take the measured defaults.
+constexpr int32_t kSplitAuto = 0, kSplitStreamK = 1, kSplitTiles = 2;
+struct LaunchKnobs {
+    int32_t slots = 0;      // staging slots of the unit ring (0: the measured rule; 1..6)
+    int32_t split = kSplitAuto;
+    int32_t skew = -1;      // stream-K: units fewer than the average for the last CTA (-1: 4)
+    int32_t resident = -1;  // most block columns with resident activations (-1: 16; 0: never)
+};
+
 struct Scratch {
     float *partials = nullptr;   // [max_workers][2][128]: a CTA's sums of its first / last tile
     int *counters = nullptr;     // [tiles] arrival counters, zero between calls
-    uint16_t *xsplit = nullptr;  // [6][C] bf16 hi/mid/lo rows of an fp32 activation pair
+    uint16_t *xsplit = nullptr;  // [6][C] bf16: an fp32 activation pair's hi/mid/lo rows, or up to six
+                                 // bf16 rows copied to a 16-byte boundary
     int *err = nullptr;          // device error word
     int32_t max_workers = 0;
 };
@@ -86,6 +97,7 @@ struct dm_tensor {
     size_t data_bytes = 0;
     uint32_t *d_unit16 = nullptr;  // [units + 1] unit starts in 16-byte units
     dm::Scratch S;
+    dm::LaunchKnobs K;
     int32_t sms = 148;
     size_t resident_bytes = 0;
 };
@@ -114,12 +126,18 @@ int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M,
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                     const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg);
 int launch_split_f32(const float *x, int64_t C, int64_t M, uint16_t *out, void *stream, std::string &msg);
+int launch_copy_u16(const uint16_t *src, int64_t n, uint16_t *dst, void *stream, std::string &msg);
+int gemv_sip_rows(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,
+                  int out_f32, uint16_t *xbuf, int64_t xcap, float *partials, int *counters, int64_t max_workers,
+                  void *stream, std::string &msg);
 int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *offsets, int64_t C,
                             const int32_t *widths, int32_t nw, int32_t B, int64_t nblocks, uint16_t *out,
                             void *stream, std::string &msg);
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg);
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *xres_bytes, int dir_cap);
+int sip_shared_bytes(const dm_tensor *t, int Mv, int slots, int max_res, int *slot_bytes, int *nslots,
+                     int *xres_bytes, int dir_cap);
+int gemv_plan(const dm_tensor *t, int Mv, dm_launch_plan *out, std::string &msg);
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
                          int64_t max_workers, void *stream, std::string &msg,

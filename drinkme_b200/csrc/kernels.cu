@@ -10,6 +10,7 @@
 // reads, and the raw bf16 GEMV (radix_ops.gemv_narrow and the raw lm_head).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <string>
 
 #include "dm_device.cuh"
@@ -258,7 +259,7 @@ __global__ void split_f32_kernel(const float *x, int64_t C, int64_t M, uint16_t 
 // reduction.
 template <int XF32, int MM>
 __global__ void __launch_bounds__(256) gemv_raw_kernel(const uint16_t *w, int64_t R, int64_t C, const void *x,
-                                                       const uint16_t *bias, void *out, int out_f32) {
+                                                       const uint16_t *bias, void *out, int out_f32, int vec) {
     constexpr int M = MM;
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * 8;
@@ -267,8 +268,7 @@ __global__ void __launch_bounds__(256) gemv_raw_kernel(const uint16_t *w, int64_
         float acc[MM];
 #pragma unroll
         for (int m = 0; m < MM; ++m) acc[m] = 0.f;
-        const bool vec = (C % 8) == 0;
-        if (vec) {
+        if (vec) {  // C % 8 == 0 and 16-byte aligned weight and activations: 16-byte loads
             // 16 weights of the row at c times the activations, in c order
             auto step = [&](int64_t c, uint4 wv) {
                 const uint32_t wp[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -364,7 +364,17 @@ static int cuda_check(cudaError_t e, const char *what, std::string &msg) {
     return DM_ECUDA;
 }
 
+// The general kernels walk each block's tier-0 codes as the pack's plain
+// 3-bit stream; a sip fast-path layout holds them as code planes instead
+// (layout.cpp: sip_code_planes), which these kernels must never read.
+static bool plain_streams(const dm_tensor *t, const char *who, std::string &msg) {
+    if (!t->L.fast_sip) return true;
+    msg = std::string(who) + ": a sip fast-path layout (code planes) is served by the sip kernels only";
+    return false;
+}
+
 int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg) {
+    if (!plain_streams(t, "decode_generic_kernel", msg)) return DM_EINVAL;
     GenericParams p = generic_params(t);
     int64_t warps = p.rows * p.NB;
     int64_t blocks = (warps + 3) / 4;
@@ -374,6 +384,7 @@ int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::
 
 int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,
                         int out_f32, void *stream, std::string &msg) {
+    if (!plain_streams(t, "gemv_generic_kernel", msg)) return DM_EINVAL;
     GenericParams p = generic_params(t);
     int64_t blocks = (p.rows + 3) / 4;
     gemv_generic_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(p, x, x_f32, (int)M, bias, out, out_f32);
@@ -403,12 +414,27 @@ int launch_split_f32(const float *x, int64_t C, int64_t M, uint16_t *out, void *
     return cuda_check(cudaGetLastError(), "split_f32_kernel", msg);
 }
 
+// bf16 activations at any 2-byte alignment -> a 16-byte aligned copy (the
+// sip kernel stages activations with bulk copies, whose source must be
+// 16-byte aligned).
+__global__ void copy_u16_kernel(const uint16_t *__restrict__ src, int64_t n, uint16_t *__restrict__ dst) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
+int launch_copy_u16(const uint16_t *src, int64_t n, uint16_t *dst, void *stream, std::string &msg) {
+    if (n <= 0) return DM_OK;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, 1184);
+    copy_u16_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(src, n, dst);
+    return cuda_check(cudaGetLastError(), "copy_u16_kernel", msg);
+}
+
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    using Kern = void (*)(const uint16_t *, int64_t, int64_t, const void *, const uint16_t *, void *, int);
+    using Kern = void (*)(const uint16_t *, int64_t, int64_t, const void *, const uint16_t *, void *, int, int);
     static const Kern kernels[2][8] = {
         {gemv_raw_kernel<0, 1>, gemv_raw_kernel<0, 2>, gemv_raw_kernel<0, 3>, gemv_raw_kernel<0, 4>,
          gemv_raw_kernel<0, 5>, gemv_raw_kernel<0, 6>, gemv_raw_kernel<0, 7>, gemv_raw_kernel<0, 8>},
@@ -426,8 +452,11 @@ int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f3
     if (per_sm == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess)
         per_sm = 4;
     const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, (int64_t)sms * std::max(per_sm, 1)));
+    // the 16-byte loads need whole 8-weight groups per row and 16-byte aligned
+    // weight and activation rows; anything else takes the scalar loop
+    const int vec = (C % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
     kern<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const uint16_t *>(w), R, C, x, bias, out, out_f32);
+        reinterpret_cast<const uint16_t *>(w), R, C, x, bias, out, out_f32, vec);
     return cuda_check(cudaGetLastError(), "gemv_raw_kernel", msg);
 }
 

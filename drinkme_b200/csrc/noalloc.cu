@@ -16,7 +16,10 @@
 // the array's name to a kernel (on the host it is a stand-in, not a device
 // address): the first call on each device looks its address up with
 // cudaGetSymbolAddress, with that device current, and caches it. That first
-// call should come before any CUDA-graph capture on the device.
+// call should come before any CUDA-graph capture on the device. The cached
+// address assumes the device's primary context lives until the process
+// exits: after cudaDeviceReset (or any teardown of that context) the cache is
+// stale, and this entry point must not be called again in the process.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -30,7 +33,7 @@ namespace {
 // The limits of the static scratch (about 1.45 MiB per GPU):
 constexpr int64_t kNoAllocMaxWorkers = 1024;  // stream-K workers (CTAs) of one launch: 148 on a B200
 constexpr int64_t kNoAllocMaxTiles = 16384;   // 16-row tiles: tensors (or row shards) of up to 262,144 rows
-constexpr int64_t kNoAllocMaxCols = 32768;    // columns of an fp32 activation row (its bf16 split)
+constexpr int64_t kNoAllocMaxCols = 32768;    // columns of a staged activation row (fp32 split, unaligned bf16)
 
 constexpr size_t kPartialBytes = (size_t)kNoAllocMaxWorkers * 2 * 128 * sizeof(float);
 constexpr size_t kCounterBytes = (size_t)kNoAllocMaxTiles * sizeof(int);
@@ -92,14 +95,13 @@ extern "C" int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtyp
                     "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
     if ((x_dtype != DM_BF16 && x_dtype != DM_F32) || (out_dtype != DM_BF16 && out_dtype != DM_F32))
         return fail(err, err_len, DM_EINVAL, "dm_gemv_noalloc: dtype must be DM_BF16 or DM_F32");
+    if ((reinterpret_cast<uintptr_t>(x) & (x_dtype == DM_F32 ? 3u : 1u)) != 0)
+        return fail(err, err_len, DM_EINVAL, "dm_gemv_noalloc: activations not aligned to their element size");
     DeviceGuard guard(t->device);
     std::string msg;
     const uint16_t *b16 = reinterpret_cast<const uint16_t *>(bias);
     const int of32 = out_dtype == DM_F32;
-    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    if (t->L.nparts > 1 && !aligned)
-        return fail(err, err_len, DM_EINVAL, "dm_gemv_noalloc: a fused tensor needs 16-byte aligned activations");
-    if (!t->L.fast_sip || !aligned) {
+    if (!t->L.fast_sip) {
         // the general kernel keeps its sums in registers: no scratch to place
         int rc = dm::launch_gemv_generic(t, x, x_dtype == DM_F32, M, b16, out, of32, stream, msg);
         if (rc) dm::set_error(err, err_len, msg);
@@ -109,35 +111,26 @@ extern "C" int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtyp
         return fail(err, err_len, DM_EINVAL,
                     "dm_gemv_noalloc: " + std::to_string(t->L.rows) + " rows exceed the static scratch's " +
                         std::to_string(kNoAllocMaxTiles * dm::kUnitRows) + " (use dm_gemv)");
-    if (x_dtype == DM_F32 && t->L.C > kNoAllocMaxCols)
+    // fp32 activations are split, and bf16 ones off a 16-byte boundary copied,
+    // into the array's staging part before the kernel reads them
+    const bool staged = x_dtype == DM_F32 || (reinterpret_cast<uintptr_t>(x) & 15) != 0;
+    if (staged && t->L.C > kNoAllocMaxCols)
         return fail(err, err_len, DM_EINVAL,
-                    "dm_gemv_noalloc: fp32 activations of " + std::to_string(t->L.C) +
-                        " columns exceed the static scratch's " + std::to_string(kNoAllocMaxCols) + " (use dm_gemv)");
+                    "dm_gemv_noalloc: " + std::string(x_dtype == DM_F32 ? "fp32" : "unaligned bf16") +
+                        " activations of " + std::to_string(t->L.C) + " columns exceed the static scratch's " +
+                        std::to_string(kNoAllocMaxCols) + " (use dm_gemv)");
     unsigned char *base = nullptr;
     int rc = scratch_address(t->device, &base, msg);
     if (rc) return fail(err, err_len, rc, msg);
     float *partials = reinterpret_cast<float *>(base);
     int *counters = reinterpret_cast<int *>(base + kPartialBytes);
-    uint16_t *xsplit = reinterpret_cast<uint16_t *>(base + kPartialBytes + kCounterBytes);
+    uint16_t *xstage = reinterpret_cast<uint16_t *>(base + kPartialBytes + kCounterBytes);
     // the array keeps the last call's contents: the arrival counters start at zero
     cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)t->L.tiles * sizeof(int), (cudaStream_t)stream);
     if (e != cudaSuccess)
         return fail(err, err_len, DM_ECUDA, std::string("cudaMemsetAsync(counters): ") + cudaGetErrorString(e));
-    if (x_dtype == DM_BF16) {
-        rc = dm::launch_gemv_sip_with(t, reinterpret_cast<const uint16_t *>(x), t->L.C, (int)M, 1, (int)M, b16, out,
-                                      of32, partials, counters, t->S.err, kNoAllocMaxWorkers, stream, msg);
-    } else {
-        const size_t esz = of32 ? 4 : 2;
-        for (int64_t m0 = 0; m0 < M && rc == DM_OK; m0 += 2) {
-            const int64_t mm = std::min<int64_t>(2, M - m0);
-            rc = dm::launch_split_f32(reinterpret_cast<const float *>(x) + m0 * t->L.C, t->L.C, mm, xsplit, stream,
-                                      msg);
-            if (rc == DM_OK)
-                rc = dm::launch_gemv_sip_with(t, xsplit, t->L.C, (int)(3 * mm), 3, (int)mm, b16,
-                                              reinterpret_cast<uint8_t *>(out) + (size_t)m0 * t->L.rows * esz, of32,
-                                              partials, counters, t->S.err, kNoAllocMaxWorkers, stream, msg);
-        }
-    }
+    rc = dm::gemv_sip_rows(t, x, x_dtype == DM_F32, M, b16, out, of32, xstage, (int64_t)6 * kNoAllocMaxCols, partials,
+                           counters, kNoAllocMaxWorkers, stream, msg);
     if (rc) dm::set_error(err, err_len, msg);
     return rc;
 }

@@ -91,6 +91,7 @@ struct SipArgs {
     uint32_t *gen, *done;
     const uint32_t *wait_flags, *wait_gen;
     uint32_t *abort;
+    uint32_t wait_polls;  // polls of one flag wait before it gives up
 };
 
 // A GROUP of kGroupWarps consumer warps shares each staged unit: warp w of
@@ -227,7 +228,7 @@ __device__ __forceinline__ void wait_inputs(const SipArgs &a) {
         uint32_t i = 0;
         while ((int32_t)(ld_acquire_sys(a.wait_flags + r) - want) < 0) {
             // a rank gave up before: do not wait again
-            if (++i > kPeerPolls || (i % 64 == 0 && ld_acquire_gpu(a.abort) != 0u)) {
+            if (++i > a.wait_polls || (i % 64 == 0 && ld_acquire_gpu(a.abort) != 0u)) {
                 atomicExch(a.err, kErrWaitPeer);
                 atomicExch(a.abort, 1u);
                 return;
@@ -541,6 +542,10 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
         const int64_t C = NB * 1024;
         const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         const int q0 = 4 * wi, j0 = 4 * wi + t;
+        // no activations order these stores after the kernel before this
+        // one (launched early by programmatic dependent launch, it may still
+        // read or write the output's memory): wait for it explicitly
+        pdl_wait();
         bool ok = true;
         int slot = gi % S, set = (gi / S) % L;
         uint32_t par = (uint32_t)((gi / S / L) & 1);
@@ -773,22 +778,25 @@ inline int resident_slots(int Mv, int64_t NB) { return Mv == 1 && NB >= 8 ? 6 : 
 
 // Shared-memory plan for a launch: the slot size, the number of slots and
 // whether the activations of every block column stay resident (one copy per
-// launch instead of one per unit; chosen whenever they fit beside the
-// resident launch's slots). Any number of slots is correct (full_sets).
-// Fixed part: the barriers, the groups' partial buffers, the tile ring, the
+// launch instead of one per unit; chosen whenever the tensor has at most
+// `max_res` block columns and they fit beside the resident launch's slots).
+// `slots` > 0 asks for that many slots (fewer when they do not fit); 0 takes
+// the measured rule. Any number of slots is correct (full_sets). Fixed
+// part: the barriers, the groups' partial buffers, the tile ring, the
 // epilogue's sum and the directory.
-int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, int *xres_bytes, int dir_cap) {
+int sip_shared_bytes(const dm_tensor *t, int Mv, int slots, int max_res, int *slot_bytes, int *nslots,
+                     int *xres_bytes, int dir_cap) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
     const int budget = 227 * 1024;
     const int kP = 16 * Mv;
     const int fixed = (3 * kMaxSlots + 2 * kTileRing + kMaxResidentCols) * 8 +
                       (kGroups * 2 * kGroupWarps + kTileRing * kGroups + 1) * kP * 4 + (dir_cap + 1) * 4 + 128;
     const int sb1 = unit + Mv * kXRowStride;
-    const int n1 = std::min(kMaxSlots, (budget - fixed) / sb1);
-    const int64_t xr = Mv >= 1 && t->L.NB <= kMaxResidentCols
+    const int n1 = std::min(slots > 0 ? slots : kMaxSlots, (budget - fixed) / sb1);
+    const int64_t xr = Mv >= 1 && t->L.NB <= std::min(max_res, kMaxResidentCols)
                            ? ((t->L.NB * Mv * kXRowStride + 127) & ~(int64_t)127)
                            : 0;
-    const int want = resident_slots(Mv, t->L.NB);
+    const int want = slots > 0 ? slots : resident_slots(Mv, t->L.NB);
     if (xr > 0 && (int64_t)budget - fixed - xr >= (int64_t)want * unit) {
         *slot_bytes = unit;
         *nslots = want;
@@ -802,10 +810,117 @@ int sip_shared_bytes(const dm_tensor *t, int Mv, int *slot_bytes, int *nslots, i
     return n1 * sb1 + fixed;
 }
 
+// The launch a GEMV (Mv virtual activation rows; 0: decode) of this tensor
+// makes under its launch knobs (dm_tensor_set_launch): the CTA split, the
+// stream-K weights, the staging slots and the shared-memory plan.
+struct SipPlan {
+    int64_t grid = 0, per_cta = 0;
+    int tile_split = 0;
+    int32_t part_b0 = 0, part_r = 0;
+    int dir_cap = 0, smem = 0, slot_bytes = 0, nslots = 0, xres_bytes = 0;
+};
+
+static int plan_sip(const dm_tensor *t, int Mv, SipPlan &P, std::string &msg) {
+    const dm::TensorLayout &L = t->L;
+    const LaunchKnobs &K = t->K;
+    // One CTA per SM, each a stream-K worker owning at least one unit; or,
+    // CTAs that own whole tiles when the busiest of them would decode fewer
+    // units than a stream-K worker plus its cross-CTA fixup (worth about
+    // three units when a CTA's range holds under two tiles, four under one;
+    // measured on the Qwen3 8B and 32B shapes). The split depends on the
+    // tensor (and its knobs) alone.
+    const int64_t tiles = L.tiles;
+    const int64_t gridA = std::min<int64_t>(t->sms, L.units), gridB = std::min<int64_t>(t->sms, tiles);
+    const int64_t perA = (L.units + gridA - 1) / gridA;
+    const int64_t costA = perA + (perA < L.NB ? 4 : (perA < 2 * L.NB ? 3 : 0));
+    const int64_t costB = (tiles + gridB - 1) / gridB * L.NB;
+    P.tile_split = K.split == kSplitTiles ? 1 : (K.split == kSplitStreamK ? 0 : (costB < costA ? 1 : 0));
+    P.grid = P.tile_split ? gridB : gridA;
+    // the stream-K split's weights: the last 40 % of the CTAs down to `skew`
+    // units fewer than the average for the very last (none when the average
+    // is under 8 units)
+    const double skew = K.skew >= 0 ? (double)K.skew : kSkewUnits;
+    P.part_b0 = P.part_r = 0;
+    if (!P.tile_split && P.grid > 8 && perA >= 8 && skew > 0) {
+        P.part_b0 = (int32_t)(P.grid * 6 / 10);
+        const double delta = std::min(0.5, skew * (double)P.grid / (double)L.units);
+        P.part_r = (int32_t)std::llround(4096.0 * delta / (double)(P.grid - 1 - P.part_b0));
+    }
+    P.per_cta = P.tile_split
+                    ? (tiles + P.grid - 1) / P.grid * L.NB
+                    : (P.part_r ? (L.units * 4096 + part_sum(P.grid, P.part_b0, P.part_r) - 1) /
+                                          part_sum(P.grid, P.part_b0, P.part_r) + 1
+                                : perA);
+    P.dir_cap = (int)std::min<int64_t>(4096, P.per_cta + 2);
+    P.smem = sip_shared_bytes(t, Mv, K.slots, K.resident >= 0 ? K.resident : kMaxResidentCols, &P.slot_bytes,
+                              &P.nslots, &P.xres_bytes, P.dir_cap);
+    if (P.smem < 0) {
+        msg = "sip kernel: a unit does not fit in shared memory";
+        return DM_EINVAL;
+    }
+    return DM_OK;
+}
+
+int gemv_plan(const dm_tensor *t, int Mv, dm_launch_plan *out, std::string &msg) {
+    SipPlan P;
+    if (int rc = plan_sip(t, Mv, P, msg)) return rc;
+    out->grid = (int32_t)P.grid;
+    out->split = P.tile_split ? kSplitTiles : kSplitStreamK;
+    out->slots = P.nslots;
+    out->resident = P.xres_bytes > 0 ? 1 : 0;
+    out->smem_bytes = P.smem;
+    out->skew_step = P.part_r;
+    return DM_OK;
+}
+
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                     const uint16_t *bias, void *out, int out_f32, void *stream, std::string &msg) {
     return launch_gemv_sip_with(t, xv, x_stride, Mv, nsplit, M_out, bias, out, out_f32, t->S.partials,
                                 t->S.counters, t->S.err, t->S.max_workers, stream, msg, nullptr);
+}
+
+// The sip GEMV for activations of either dtype at any element alignment:
+// bf16 rows that start on a 16-byte boundary go to the kernel as they are
+// (its bulk copies need 16-byte aligned sources); other bf16 rows are first
+// copied into `xbuf`, and fp32 rows are split there into three bf16 pieces
+// (hi, mid, lo) read as three virtual rows. `xbuf` holds `xcap` bf16
+// elements, 16-byte aligned; rows go through it a chunk at a time, one launch
+// per chunk. Activation row m's result is the same bits whatever the chunk:
+// every sum's order depends on the tensor alone.
+int gemv_sip_rows(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,
+                  int out_f32, uint16_t *xbuf, int64_t xcap, float *partials, int *counters, int64_t max_workers,
+                  void *stream, std::string &msg) {
+    const int64_t C = t->L.C;
+    const size_t esz = out_f32 ? 4 : 2;
+    const bool direct = !x_f32 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (direct)
+        return launch_gemv_sip_with(t, reinterpret_cast<const uint16_t *>(x), C, (int)M, 1, (int)M, bias, out,
+                                    out_f32, partials, counters, t->S.err, max_workers, stream, msg);
+    // rows per chunk: fp32 rows take three bf16 rows of xbuf each (at most
+    // two per launch: six virtual rows), bf16 rows one (at most six)
+    const int64_t per = x_f32 ? std::min<int64_t>(2, xcap / (3 * C)) : std::min<int64_t>(6, xcap / C);
+    if (per < 1) {
+        msg = "sip kernel: an activation row of " + std::to_string(C) + " columns exceeds the " +
+              std::to_string(xcap) + "-element staging buffer";
+        return DM_EINVAL;
+    }
+    int rc = DM_OK;
+    for (int64_t m0 = 0; m0 < M && rc == DM_OK; m0 += per) {
+        const int64_t mm = std::min<int64_t>(per, M - m0);
+        uint8_t *o = reinterpret_cast<uint8_t *>(out) + (size_t)m0 * t->L.rows * esz;
+        if (x_f32) {
+            rc = launch_split_f32(reinterpret_cast<const float *>(x) + m0 * C, C, mm, xbuf, stream, msg);
+            if (rc == DM_OK)
+                rc = launch_gemv_sip_with(t, xbuf, C, (int)(3 * mm), 3, (int)mm, bias, o, out_f32, partials, counters,
+                                          t->S.err, max_workers, stream, msg);
+        } else {
+            rc = launch_copy_u16(reinterpret_cast<const uint16_t *>(x) + m0 * C, mm * C, xbuf, stream, msg);
+            if (rc == DM_OK)
+                rc = launch_gemv_sip_with(t, xbuf, C, (int)mm, 1, (int)mm, bias, o, out_f32, partials, counters,
+                                          t->S.err, max_workers, stream, msg);
+        }
+    }
+    return rc;
 }
 
 // The launch with caller-supplied scratch (partials for `max_workers`
@@ -819,44 +934,18 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         msg = "sip kernel: 1..8 virtual activation rows";
         return DM_EINVAL;
     }
-    // One CTA per SM, each a stream-K worker owning at least one unit; or,
-    // CTAs that own whole tiles when the busiest of them would decode fewer
-    // units than a stream-K worker plus its cross-CTA fixup (worth about
-    // three units when a CTA's range holds under two tiles, four under one;
-    // measured on the Qwen3 8B and 32B shapes). The split depends on the
-    // tensor alone.
-    const int64_t tiles = L.tiles;
-    const int64_t gridA = std::min<int64_t>(t->sms, L.units), gridB = std::min<int64_t>(t->sms, tiles);
-    const int64_t perA = (L.units + gridA - 1) / gridA;
-    const int64_t costA = perA + (perA < L.NB ? 4 : (perA < 2 * L.NB ? 3 : 0));
-    const int64_t costB = (tiles + gridB - 1) / gridB * L.NB;
-    const int tile_split = costB < costA ? 1 : 0;
-    const int64_t grid = tile_split ? gridB : gridA;
+    SipPlan P;
+    if (int rc = plan_sip(t, Mv, P, msg)) return rc;
+    const int64_t tiles = L.tiles, grid = P.grid;
+    const int tile_split = P.tile_split;
+    const int32_t part_b0 = P.part_b0, part_r = P.part_r;
     if (grid > max_workers || grid > kMaxGrid) {
         msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
               std::to_string(max_workers) + " (or the launch's " + std::to_string(kMaxGrid) + ")";
         return DM_EINVAL;
     }
-    // the stream-K split's weights: the last 40 % of the CTAs down to
-    // kSkewUnits fewer units than the average for the very last (none when
-    // the average is under 8 units)
-    int32_t part_b0 = 0, part_r = 0;
-    if (!tile_split && grid > 8 && perA >= 8) {
-        part_b0 = (int32_t)(grid * 6 / 10);
-        const double delta = std::min(0.5, kSkewUnits * (double)grid / (double)L.units);
-        part_r = (int32_t)std::llround(4096.0 * delta / (double)(grid - 1 - part_b0));
-    }
-    const int64_t per_cta =
-        tile_split ? (tiles + grid - 1) / grid * L.NB
-                   : (part_r ? (L.units * 4096 + part_sum(grid, part_b0, part_r) - 1) / part_sum(grid, part_b0, part_r) + 1
-                             : perA);
-    const int dir_cap = (int)std::min<int64_t>(4096, per_cta + 2);
-    int slot_bytes = 0, nslots = 0, xres_bytes = 0;
-    const int smem = sip_shared_bytes(t, Mv, &slot_bytes, &nslots, &xres_bytes, dir_cap);
-    if (smem < 0) {
-        msg = "sip kernel: a unit does not fit in shared memory";
-        return DM_EINVAL;
-    }
+    const int dir_cap = P.dir_cap, smem = P.smem, slot_bytes = P.slot_bytes, nslots = P.nslots,
+              xres_bytes = P.xres_bytes;
     using Kern = void (*)(SipArgs);
     static const Kern kernels[2][kMaxVirtualRows + 1] = {
         {sip_gemv_kernel<0, false>, sip_gemv_kernel<1, false>, sip_gemv_kernel<2, false>, sip_gemv_kernel<3, false>,
@@ -922,6 +1011,7 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         a.wait_flags = gather->wait_flags;
         a.wait_gen = gather->wait_gen;
         a.abort = gather->abort;
+        a.wait_polls = gather->wait_polls ? gather->wait_polls : kPeerPolls;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);

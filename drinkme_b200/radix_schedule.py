@@ -1,18 +1,41 @@
-"""The per-tensor launch schedule — the reference's radix_schedule
-(src/drinkme/codec/radix_schedule.py) with a ``b200`` box class.
+"""The per-tensor launch schedule of the sm_100a sip kernels — this package's
+counterpart of the reference's radix_schedule (src/drinkme/codec/
+radix_schedule.py), keyed the same way and overridden through the same
+variable, with the knobs these kernels really have.
 
-The reference's table picks Triton knobs (blocks per program, warps) per
-(box class, profile family, shape class), measured per GPU family. The
-sm_100a kernels size themselves from the tensor and the shared-memory
-budget (one CTA per SM, 8 consumer warps, 2-3 staged units each), so the
-b200 rows name the kernel that serves each (family, class) and keep the
-reference's fields for the boot log and for DRINKME_RADIX_SCHEDULE, whose
-grammar (table | spike | tiles=..,warps=.. | {per-class json} | @file) is
-parsed and validated the same way (radix_schedule.py:372-417, 461-489).
+The reference's rows pick Triton knobs (blocks per program, warps) per (box
+class, profile family, shape class). The sm_100a GEMV has a fixed CTA shape
+(one CTA per SM: a producer warp, four groups of four consumer warps and an
+epilogue warp) and is tuned by four launch knobs instead, which reach the
+kernel through dm_tensor_set_launch (include/drinkme_b200.h):
 
-Shape classes (radix_schedule.py:351-362): head R >= 32768, narrow R <= 1024,
-long NB >= 8, wide R >= 8192, else square. Families (365-370): two tiers ->
-"sip", three or more -> "scheduled".
+  slots     staging slots of the unit ring, 1..6; 0 = the measured rule
+            (five, six at M = 1 for tensors of 8+ block columns)
+  split     "auto" (cost rule: stream-K unless whole tiles keep the busiest
+            CTA lighter), "stream" (stream-K over units), "tiles" (whole
+            16-row tiles per CTA)
+  skew      stream-K: how many units fewer than the average the last CTA to
+            be dispatched gets (0..64; 4 measured best)
+  resident  the most block columns whose activations stay resident in
+            shared memory for the whole launch (0..16; 16 measured: wider
+            tensors stage activations with every unit)
+
+Slots and residency change only how data is staged: results are the same
+bits. Split and skew change which CTA sums which units, so results may move
+within the fp32-accumulation bound.
+
+The rows below were measured on B200 with the per-launch CUDA-graph timing of
+bench.py (Qwen3-8B and 32B shapes). Shape classes (radix_schedule.py:
+351-362): head R >= 32768, narrow R <= 1024, long NB >= 8, wide R >= 8192,
+else square. Families (365-370): two tiers -> "sip", three or more ->
+"scheduled" (gulp and balanced packs with whole 1024-weight blocks are
+re-encoded as sip by the loader, so they run these rows too; others run the
+general kernel, which has no knobs).
+
+DRINKME_RADIX_SCHEDULE (the reference's grammar, radix_schedule.py:372-417):
+"table" (default), "spike" (the most conservative launch: whole tiles, two
+slots, no residency), "key=value,..." over the keys above, a JSON object
+{class: {key: value}} or "@file" holding one.
 """
 from __future__ import annotations
 
@@ -21,24 +44,26 @@ import json
 import os
 from dataclasses import asdict, dataclass
 
-SPIKE = dict(gemv_tiles=1, gemv_warps=2, mc_tiles=1, mc_warps=2)
 CLASSES = ("head", "narrow", "long", "wide", "square")
 FAMILIES = ("sip", "scheduled")
 BOX_CLASSES = ("b200",)
+SPLITS = {"auto": 0, "stream": 1, "tiles": 2}
+KEYS = ("slots", "split", "skew", "resident")
 
-# b200: gemv_tiles = 1 (one unit of 8 rows x 1 block per worker step, split-K
-# across workers with a deterministic fixup), gemv_warps = 8 consumer warps.
-_B200_ROW = dict(gemv_tiles=1, gemv_warps=8, mc_tiles=1, mc_warps=8)
-TABLES = {"b200": {fam: {cls: dict(_B200_ROW) for cls in CLASSES} for fam in FAMILIES}}
-KERNELS = {"sip": "sip-mma-sm100a", "scheduled": "generic-sm100a"}
+# the measured defaults (sip.cu: resident_slots, the cost rule, kSkewUnits,
+# kMaxResidentCols); a row differs from them where a class measured better
+_DEFAULT = dict(slots=0, split="auto", skew=4, resident=16)
+SPIKE = dict(slots=2, split="tiles", skew=0, resident=0)
+TABLES = {"b200": {fam: {cls: dict(_DEFAULT) for cls in CLASSES} for fam in FAMILIES}}
+KERNELS = {"sip": "sip-mma-sm100a", "scheduled": "sip-mma-sm100a"}
 
 
 @dataclass(frozen=True)
 class Launch:
-    gemv_tiles: int
-    gemv_warps: int
-    mc_tiles: int
-    mc_warps: int
+    slots: int
+    split: str
+    skew: int
+    resident: int
     shape_class: str
     family: str
     box_class: str
@@ -48,10 +73,13 @@ class Launch:
     def as_dict(self) -> dict:
         return asdict(self)
 
+    def knobs(self) -> tuple[int, int, int, int]:
+        """(slots, split code, skew, resident): dm_launch's fields."""
+        return self.slots, SPLITS[self.split], self.skew, self.resident
+
     def describe(self) -> str:
-        g = "row" if self.gemv_tiles == 0 else str(self.gemv_tiles)
-        m = "row" if self.mc_tiles == 0 else str(self.mc_tiles)
-        return f"gemv {g}/w{self.gemv_warps} mc {m}/w{self.mc_warps} [{self.kernel}]"
+        s = "rule" if self.slots == 0 else str(self.slots)
+        return f"slots {s} split {self.split} skew {self.skew} resident {self.resident} [{self.kernel}]"
 
 
 def shape_class(R: int, C: int, block_size: int = 1024) -> str:
@@ -73,12 +101,22 @@ def family(widths) -> str:
 
 
 def _validate(cfg: dict) -> None:
-    for key in ("gemv_tiles", "mc_tiles"):
-        if type(cfg[key]) is not int or cfg[key] < 0:
-            raise ValueError(f"radix schedule: {key} must be a non-negative int (0 = whole row)")
-    for key in ("gemv_warps", "mc_warps"):
-        if cfg[key] not in (1, 2, 4, 8):
-            raise ValueError(f"radix schedule: {key} must be 1, 2, 4 or 8")
+    if type(cfg["slots"]) is not int or not 0 <= cfg["slots"] <= 6:
+        raise ValueError("radix schedule: slots must be 0 (the measured rule) or 1..6")
+    if cfg["split"] not in SPLITS:
+        raise ValueError(f"radix schedule: split must be one of {', '.join(SPLITS)}")
+    if type(cfg["skew"]) is not int or not 0 <= cfg["skew"] <= 64:
+        raise ValueError("radix schedule: skew must be 0..64")
+    if type(cfg["resident"]) is not int or not 0 <= cfg["resident"] <= 16:
+        raise ValueError("radix schedule: resident must be 0..16")
+
+
+def _value(key: str, value):
+    if key == "split":
+        return str(value).strip()
+    if key == "slots" and str(value).strip() in ("rule", "auto"):
+        return 0
+    return int(value)
 
 
 def _parse_override(spec: str) -> dict:
@@ -88,17 +126,11 @@ def _parse_override(spec: str) -> dict:
         if not item:
             continue
         key, _, value = item.partition("=")
-        key, value = key.strip(), value.strip()
-        if key in ("tiles", "gemv_tiles"):
-            out["gemv_tiles"] = 0 if value == "row" else int(value)
-        elif key in ("warps", "gemv_warps"):
-            out["gemv_warps"] = int(value)
-        elif key == "mc_tiles":
-            out["mc_tiles"] = 0 if value == "row" else int(value)
-        elif key == "mc_warps":
-            out["mc_warps"] = int(value)
-        else:
-            raise ValueError(f"DRINKME_RADIX_SCHEDULE: unknown key {key!r} in {spec!r}")
+        key = key.strip()
+        if key not in KEYS:
+            raise ValueError(f"DRINKME_RADIX_SCHEDULE: unknown key {key!r} in {spec!r} (keys: {', '.join(KEYS)}; "
+                             "tiles / warps are the reference's Triton knobs, which this kernel does not have)")
+        out[key] = _value(key, value)
     return out
 
 
@@ -119,20 +151,22 @@ def _per_class_table(spec: str) -> dict:
             raise ValueError(f"DRINKME_RADIX_SCHEDULE: class {cls!r} must map to an object")
         cfg = {}
         for key, value in row.items():
-            if key not in SPIKE:
+            if key not in KEYS:
                 raise ValueError(f"DRINKME_RADIX_SCHEDULE: unknown key {key!r} for class {cls!r}")
-            cfg[key] = 0 if value == "row" else int(value)
-        _validate({**SPIKE, **cfg})
+            cfg[key] = _value(key, value)
+        _validate({**_DEFAULT, **cfg})
         out[cls] = cfg
     return out
 
 
 def select(R: int, C: int, block_size: int = 1024, widths=(3, 8), override: str | None = None) -> Launch:
+    """The launch of an (R, C) radix tensor: the b200 table's row for its
+    (family, shape class), or the DRINKME_RADIX_SCHEDULE override."""
     cls, fam, box = shape_class(R, C, block_size), family(widths), "b200"
-    kernel = KERNELS[fam] if (fam == "sip" and int(block_size) == 1024 and int(C) % 1024 == 0) else "generic-sm100a"
+    kernel = KERNELS[fam] if int(block_size) == 1024 and int(C) % 1024 == 0 else "generic-sm100a"
     spec = os.environ.get("DRINKME_RADIX_SCHEDULE", "table") if override is None else override
     spec = (spec or "table").strip()
-    if spec == "table" or spec == "table=b200":
+    if spec in ("table", "table=b200"):
         return Launch(**TABLES[box][fam][cls], shape_class=cls, family=fam, box_class=box, source="table",
                       kernel=kernel)
     if spec == "spike":
@@ -149,3 +183,4 @@ def select(R: int, C: int, block_size: int = 1024, widths=(3, 8), override: str 
 for _rows in TABLES["b200"].values():
     for _cfg in _rows.values():
         _validate(_cfg)
+_validate(SPIKE)

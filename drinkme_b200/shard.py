@@ -17,6 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import radix_ops, swap
+from .tensor import device_view
 
 
 def row_range(R: int, rank: int, world: int, align: int = 16) -> tuple[int, int]:
@@ -101,17 +102,19 @@ def local_gemv_into(rt: dict, x: torch.Tensor, out: torch.Tensor) -> torch.Tenso
 
 # ------------------------------------------------- fused NVLink gather --
 
-def _device_view(ptr: int, shape, dtype: torch.dtype) -> torch.Tensor:
-    """A torch tensor over device memory this package allocated (zero copy,
-    through the CUDA array interface; bf16 travels as int16)."""
-    code = {torch.bfloat16: "<i2", torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+def exchange_handles(handle: bytes, world: int, group=None) -> list:
+    """Every rank's 64-byte IPC handle, index = rank (a collective over
+    `group`). A rank that has left, or never calls, makes the others raise
+    once the process group's timeout runs out; none of them is left waiting
+    on a GPU, as no kernel has been launched yet."""
+    import torch.distributed as dist
 
-    class _Raw:
-        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": code, "data": (int(ptr), False),
-                                    "version": 3, "strides": None}
-
-    t = torch.as_tensor(_Raw(), device="cuda")
-    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+    handles = [None] * world
+    if world > 1:
+        dist.all_gather_object(handles, handle, group=group)
+    else:
+        handles[0] = handle
+    return handles
 
 
 class PeerGather:
@@ -127,8 +130,6 @@ class PeerGather:
 
     def __init__(self, slots, M: int, out_dtype, rank: int, world: int, device, group=None):
         import ctypes as ct
-
-        import torch.distributed as dist
 
         from . import _lib
 
@@ -153,9 +154,12 @@ class PeerGather:
         self.base = base.value
         h = (ct.c_uint8 * 64)()
         _lib.call("dm_ipc_handle", ct.c_void_p(self.base), h)
-        handles = [None] * self.world
-        if self.world > 1:
-            dist.all_gather_object(handles, bytes(h), group=group)
+        try:
+            handles = exchange_handles(bytes(h), self.world, group)
+        except Exception:
+            _lib.call("dm_device_free", ct.c_void_p(self.base))
+            self.base = None
+            raise
         self.peer_base = []
         for r in range(self.world):
             if r == self.rank:
@@ -169,8 +173,9 @@ class PeerGather:
     def _flags(self, base: int, i: int) -> int:
         return base + self.flag_off + i * 64 * (-(-self.world * 4 // 64))
 
-    def desc(self, i: int, wait: int | None = None):
-        """The dm_gather of linear i (waiting for linear `wait` first)."""
+    def desc(self, i: int, wait: int | None = None, wait_polls: int = 0):
+        """The dm_gather of linear i (waiting for linear `wait` first, giving
+        up after `wait_polls` flag polls; 0: the library's bound)."""
         from . import _lib
 
         g = _lib.Gather()
@@ -184,16 +189,30 @@ class PeerGather:
         if wait is not None:
             g.wait_flags = self._flags(self.base, wait)
             g.wait_gen = self.base + self.cnt_off + 8 * wait
+        g.wait_polls = int(wait_polls)
         return g
+
+    def launch_count(self, i: int) -> torch.Tensor:
+        """This rank's launch count of linear i (a one-element int32 view of
+        the device word the flags are compared with)."""
+        return device_view(self.base + self.cnt_off + 8 * i, (1,), torch.int32, self.device)
+
+    def abort_word(self) -> torch.Tensor:
+        """This rank's abort word (nonzero once a wait has given up)."""
+        return device_view(self.base + self.cnt_off + 8 * len(self.slots), (1,), torch.int32, self.device)
 
     def output(self, i: int) -> torch.Tensor:
         """This rank's gathered output of linear i, [M, world * slot]
         (rank k's rows at [k * slot, k * slot + rows_k))."""
-        return _device_view(self.base + self.out_off[i], (self.M, self.world * self.slots[i]), self.dtype)
+        return device_view(self.base + self.out_off[i], (self.M, self.world * self.slots[i]), self.dtype, self.device)
 
-    def gemv(self, rt: dict, x: torch.Tensor, i: int, wait: int | None = None, bias=None) -> None:
+    def gemv(self, rt: dict, x: torch.Tensor, i: int, wait: int | None = None, bias=None,
+             wait_polls: int = 0) -> None:
         """This rank's rows of linear i (runtime dict `rt`), gathered into every
-        rank's output(i) and published; the activations `x` [M, C] bf16."""
+        rank's output(i) and published; the activations `x` [M, C] bf16. A
+        wait that gives up is recorded in the tensor's device error word
+        (kErrWaitPeer = 4, read by rt["rx_handle"].device_error()) and in the
+        abort word, after which every later wait of this rank returns at once."""
         import ctypes as ct
 
         from . import _lib
@@ -204,7 +223,7 @@ class PeerGather:
         b = bias.to(device=x.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
         _lib.call("dm_gemv_gather", h.ptr, ct.c_void_p(x.data_ptr()), x.shape[0],
                   ct.c_void_p(b.data_ptr() if b is not None else 0), _lib.DM_F32 if self.dtype == torch.float32
-                  else _lib.DM_BF16, ct.byref(self.desc(i, wait)),
+                  else _lib.DM_BF16, ct.byref(self.desc(i, wait, wait_polls)),
                   ct.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
 
     def close(self) -> None:

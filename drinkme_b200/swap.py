@@ -15,8 +15,7 @@ drop-in for the reference's ``drinkme.codec.swap`` module classes and loader
   stock_gemv_mode, raw_gemv_mode,                  one-row GEMV choice
   install_stock_gemv, codec_tree
   make_module(pack, bias, device) swap.py:900-919
-  eligible, eligible_linears,     swap.py:850-897
-  swap_linears
+  eligible                        swap.py:850-854  which Linears the codec takes
 
 Routing (swap.py:302-335): M == 1 -> "gemv"; 2 <= M <= MC_MAX -> "mc"
 unless DRINKME_PREFILL_DENSE_MIN says dense; M >= GEMM_MIN_ROWS (9) ->
@@ -36,7 +35,7 @@ import torch
 from . import codec, radix_ops
 from .ops import MC_MAX
 from .radix_schedule import select as select_launch
-from .tensor import RadixTensor
+from .tensor import RadixTensor, device_view
 
 
 def _cuda_device(device) -> torch.device:
@@ -65,6 +64,9 @@ def to_device_radix(pack: dict, device="cuda", row_begin: int = 0, row_end: int 
     B = int(pack["block_size"])
     r0, r1 = int(row_begin), R if row_end is None else int(row_end)
     h = RadixTensor(pack, dev, r0, r1)
+    launch = select_launch(R, C, B, widths)
+    if h.info.fast_path:
+        h.set_launch(*launch.knobs())
     nb = (C + B - 1) // B
     rows = r1 - r0
     if len(widths) > 2:
@@ -77,12 +79,23 @@ def to_device_radix(pack: dict, device="cuda", row_begin: int = 0, row_end: int 
     else:
         schedule = torch.empty(0, dtype=torch.uint16, device=dev)
     pad = int(codec.block_word_bounds(B, codec.MANT, codec.EXP, widths)[1])
+    # the reference's device arrays (swap.py:80-161), for callers that read
+    # the dict: the shard's word directory (rebased) and the padded palette
+    # words, verbatim; rx_data is the device payload the kernels stream, in
+    # this package's B200 layout (unit-major, code planes), not pack order —
+    # its .device and size are what reference code reads (radix_ops.py:426,
+    # swap.py:433); NW and read_bytes stay the pack's
+    off = np.ascontiguousarray(pack["rx_offsets"], dtype=np.uint32)[r0 * nb:r1 * nb + 1].astype(np.int64)
+    d_offsets = torch.from_numpy((off - off[0]).astype(np.uint32)).to(dev)
+    d_palette = torch.from_numpy(codec.padded_palette_words(pack)).to(dev)
+    d_data = device_view(h.info.layout_ptr, (h.info.layout_bytes // 4,), torch.int32, dev).view(torch.uint32)
     return {
         **{k: v for k, v in pack.items() if k not in ("rx_palette", "rx_offsets", "rx_data")},
         "rx_handle": h,
+        "rx_data": d_data, "rx_offsets": d_offsets, "rx_palette": d_palette, "rx_layout": "b200-unit-major",
         "rx_schedule": schedule,
         "rx_palette_np": np.ascontiguousarray(pack["rx_palette"], dtype=np.uint8),
-        "rx_launch": select_launch(R, C, B, widths).as_dict(),
+        "rx_launch": launch.as_dict(),
         "NW": int(h.info.payload_words), "rx_pad_words": pad,
         "R": rows, "C": C, "R_full": R, "row_begin": r0, "widths": widths, "block_size": B, "NBK": rows * nb,
         "codec": "radix", "format_version": codec.FORMAT_VERSION, "layout": 0,
@@ -108,10 +121,12 @@ def to_device_radix_fused(packs, device="cuda", ranges=None) -> dict:
     B = int(packs[0]["block_size"])
     widths = tuple(int(w) for w in packs[0]["widths"])
     rows = int(h.info.rows)
+    launch = select_launch(rows, C, B, widths)
+    h.set_launch(*launch.knobs())
     return {
         "rx_handle": h,
         "rx_schedule": torch.empty(0, dtype=torch.uint16, device=dev),
-        "rx_launch": select_launch(rows, C, B, widths).as_dict(),
+        "rx_launch": launch.as_dict(),
         "NW": int(h.info.payload_words),
         "R": rows, "C": C, "R_full": rows, "row_begin": 0, "widths": widths, "block_size": B,
         "NBK": int(h.info.nblocks), "codec": "radix", "format_version": codec.FORMAT_VERSION, "layout": 0,
@@ -125,8 +140,10 @@ def split_fused(runtime: dict, y: torch.Tensor):
 
 
 def resident_bytes(runtime: dict) -> int:
-    """Device bytes a runtime dict holds (pack.resident_bytes, pack.py:1170)."""
-    n = sum(v.numel() * v.element_size() for v in runtime.values() if torch.is_tensor(v))
+    """Device bytes a runtime dict holds (pack.resident_bytes, pack.py:1170);
+    rx_data, a view of the handle's own layout, is counted with the handle."""
+    n = sum(v.numel() * v.element_size() for k, v in runtime.items()
+            if torch.is_tensor(v) and not (k == "rx_data" and "rx_layout" in runtime))
     h = runtime.get("rx_handle")
     return n + (int(h.info.resident_bytes) if h is not None else 0)
 
@@ -348,16 +365,25 @@ def stock_linear(x, weight, bias, mode: str = "b200", raw: dict | None = None):
             and x.dtype in (torch.bfloat16, torch.float32) and weight.is_contiguous()):
         y = radix_ops.gemv_raw(weight, x.reshape(M, -1), bias, x.dtype)
         return y.reshape(*x.shape[:-1], weight.shape[0])
-    if mode != "mv" or x.device.type != "cuda" or x.numel() != weight.shape[1]:
-        return torch.nn.functional.linear(x, weight, bias)
-    prev = torch._C._get_blas_preferred_backend()
-    torch._C._set_blas_preferred_backend(torch._C._BlasBackend.Cublaslt)
-    try:
-        v = x.reshape(-1)
-        y = torch.mv(weight, v) if bias is None else torch.addmv(bias, weight, v)
-    finally:
-        torch._C._set_blas_preferred_backend(prev)
-    return y.reshape(*x.shape[:-1], weight.shape[0])
+    if mode == "mv" and x.device.type == "cuda" and x.numel() == weight.shape[1]:
+        # one row as a matrix-vector product on the default BLAS backend (the
+        # reference's "mv" prefers hipBLASLt for its AMD targets; on B200
+        # cuBLAS chooses its own GEMV kernel)
+        v = x.reshape(weight.shape[1])
+        y = weight.mv(v) if bias is None else bias.addmv(weight, v)
+        return y.reshape(*x.shape[:-1], weight.shape[0])
+    return torch.nn.functional.linear(x, weight, bias)
+
+
+def _raw_bf16_linear(mod, min_rows: int, max_rows: int | None, min_cols: int) -> bool:
+    """A plain torch Linear with a bf16 CUDA weight of the given extents."""
+    if type(mod) is not torch.nn.Linear:
+        return False
+    w = mod.weight
+    if w.dtype != torch.bfloat16 or w.device.type != "cuda":
+        return False
+    rows, cols = w.shape
+    return rows >= min_rows and cols >= min_cols and (max_rows is None or rows <= max_rows)
 
 
 class StockLinear(torch.nn.Linear):
@@ -371,18 +397,17 @@ class StockLinear(torch.nn.Linear):
 
     @classmethod
     def wants(cls, mod) -> bool:
-        if type(mod) is not torch.nn.Linear:
-            return False
-        w = mod.weight
-        return w.dtype == torch.bfloat16 and w.device.type == "cuda" and min(w.shape) >= cls.MIN_DIM
+        return _raw_bf16_linear(mod, cls.MIN_DIM, None, cls.MIN_DIM)
 
     @classmethod
     def adopt(cls, lin: torch.nn.Linear, mode: str) -> "StockLinear":
-        new = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, device="meta")
-        new.weight = lin.weight
-        new.bias = lin.bias
-        new.stock_gemv = mode
-        return new
+        """The Linear itself, re-classed in place: the same module object
+        with its own Parameters, buffers and hooks (nothing is copied or
+        rebuilt), now forwarding through stock_linear under `mode`."""
+        lin.__class__ = cls
+        lin.stock_gemv = mode
+        lin.raw_gemv = None
+        return lin
 
     def forward(self, x):
         return stock_linear(x, self.weight, self.bias, self.stock_gemv, self.raw_gemv)
@@ -426,18 +451,14 @@ class NarrowLinear(torch.nn.Linear):
 
     @classmethod
     def wants(cls, mod) -> bool:
-        if type(mod) is not torch.nn.Linear or eligible(mod):
-            return False
-        w = mod.weight
-        return (w.dtype == torch.bfloat16 and w.device.type == "cuda" and w.shape[0] <= cls.MAX_ROWS
-                and w.shape[1] >= cls.MIN_COLS and w.shape[1] % 4 == 0)
+        return (not eligible(mod) and _raw_bf16_linear(mod, 1, cls.MAX_ROWS, cls.MIN_COLS)
+                and mod.weight.shape[1] % 4 == 0)
 
     @classmethod
     def adopt(cls, lin: torch.nn.Linear) -> "NarrowLinear":
-        new = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, device="meta")
-        new.weight = lin.weight
-        new.bias = lin.bias
-        return new
+        """The Linear re-classed in place (its own Parameters, no copy)."""
+        lin.__class__ = cls
+        return lin
 
     def forward(self, x):
         shape = x.shape
@@ -464,46 +485,14 @@ def install_narrow(model, device) -> list[tuple[str, tuple[int, int]]]:
     return done
 
 
-def eligible(child) -> bool:
-    if not isinstance(child, torch.nn.Linear):
+def eligible(mod) -> bool:
+    """Does the codec take this Linear (swap.py:850-854)? A bf16 weight whose
+    rows and columns are both at least 1024, columns a multiple of 4. Which
+    Linears of a model to hand to the loader is the caller's walk."""
+    if not isinstance(mod, torch.nn.Linear):
         return False
-    w = child.weight.data
-    return w.dtype == torch.bfloat16 and w.shape[1] % 4 == 0 and min(w.shape) >= 1024
-
-
-def eligible_linears(model):
-    """(qualified name, parent, child name, module) of every Linear the codec
-    takes: eligible, and not weight-tied to an Embedding (swap.py:857-882).
-    Tied by Parameter identity (meta models: every storage pointer is 0),
-    or by storage on real ones; root-level names carry no leading dot."""
-    embs = [m.weight for m in model.modules() if isinstance(m, torch.nn.Embedding)]
-    tied_ids = {id(w) for w in embs}
-    tied_ptrs = {w.data_ptr() for w in embs if not w.is_meta}
-    for parent_name, parent in model.named_modules():
-        for child_name, child in list(parent.named_children()):
-            if not eligible(child):
-                continue
-            w = child.weight
-            if id(w) in tied_ids or (not w.is_meta and w.data_ptr() in tied_ptrs):
-                continue
-            yield (f"{parent_name}.{child_name}" if parent_name else child_name), parent, child_name, child
-
-
-def swap_linears(model, make, device="cuda"):
-    """Replace every eligible Linear with make(cpu_weight, bias) -> (module,
-    stat), dropping the old weight's storage (swap.py:885-897). Returns the
-    stats, each named."""
-    stats = []
-    for name, parent, child_name, child in list(eligible_linears(model)):
-        w = child.weight.data
-        bias = child.bias.data.to(device) if child.bias is not None else None
-        mod, stat = make(w, bias)
-        setattr(parent, child_name, mod)
-        child.weight.data = torch.empty(0)
-        if stat:
-            stat["name"] = name
-            stats.append(stat)
-    return stats
+    R, C = mod.weight.shape
+    return mod.weight.dtype == torch.bfloat16 and C % 4 == 0 and min(R, C) >= 1024
 
 
 def make_module(pack: dict, bias, device="cuda", row_begin: int = 0, row_end: int | None = None):

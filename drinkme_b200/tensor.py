@@ -19,6 +19,20 @@ def _cuda(device) -> torch.device:
     return dev
 
 
+def device_view(ptr: int, shape, dtype: torch.dtype, device) -> torch.Tensor:
+    """A torch tensor over device memory this package allocated (zero copy,
+    through the CUDA array interface; bf16 travels as int16). The memory's
+    owner must outlive the view."""
+    code = {torch.bfloat16: "<i2", torch.float32: "<f4", torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
+
+    class _Raw:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": code, "data": (int(ptr), False),
+                                    "version": 3, "strides": None}
+
+    t = torch.as_tensor(_Raw(), device=_cuda(device))
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+
+
 def _part(pack: dict, row_begin, row_end):
     """A dm_pack_part over a pack's host arrays, and the arrays to keep alive
     until the library has copied them."""
@@ -94,6 +108,19 @@ class RadixTensor:
         h = ct.c_void_p()
         _lib.call("dm_tensor_clone", self.ptr, ct.byref(h))
         return RadixTensor._wrap(h, self)
+
+    def set_launch(self, slots: int = 0, split: int = 0, skew: int = -1, resident: int = -1) -> None:
+        """The sip kernels' launch knobs for this tensor (dm_tensor_set_launch;
+        radix_schedule.Launch.knobs() gives them from the schedule table)."""
+        _lib.call("dm_tensor_set_launch", self.ptr, ct.byref(_lib.Launch(slots, split, skew, resident)))
+
+    def plan(self, M: int = 1, dtype=torch.bfloat16) -> dict:
+        """What a GEMV of M rows would launch (dm_gemv_plan): grid, split
+        (1 stream-K, 2 tiles), slots, resident, smem_bytes, skew_step."""
+        out = _lib.LaunchPlan()
+        _lib.call("dm_gemv_plan", self.ptr, int(M), _lib.DM_F32 if dtype == torch.float32 else _lib.DM_BF16,
+                  ct.byref(out))
+        return {name: int(getattr(out, name)) for name, _ in _lib.LaunchPlan._fields_}
 
     def device_error(self) -> int:
         """The device error word (a bounded wait that gave up), read and cleared."""

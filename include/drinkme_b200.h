@@ -61,6 +61,8 @@ typedef struct dm_tensor_info {
     int32_t device;
     int64_t device_bytes_per_call; /* read_bytes' count over what the kernels stream: differs when the
                                       loader re-encoded a non-sip pack as sip (dm_tensor_create) */
+    uint64_t layout_ptr;       /* the device address of the B200 layout the kernels stream (read only) */
+    int64_t layout_bytes;      /* its size: the unit-major payload and the zero tail pad */
 } dm_tensor_info;
 
 /* Library version (major * 10000 + minor * 100 + patch). */
@@ -130,9 +132,12 @@ int dm_tensor_get_info(const dm_tensor *t, dm_tensor_info *info);
  * 351-398): x is bf16 or fp32 (`x_dtype`, row stride C), 1 <= M <= 8
  * (DM_EINVAL outside, the ValueError of radix_ops.py:384-385), bias is a
  * bf16 [rows] vector or NULL, out is [M, rows] row-major in `out_dtype`.
- * Column m of an M-row call is bitwise the M=1 call on row m. Uses the
- * tensor's own scratch: calls on one tensor must not overlap on the GPU.
- * A fused tensor (dm_tensor_create_multi) needs 16-byte aligned x. */
+ * Column m of an M-row call is bitwise the M=1 call on row m. x may start
+ * at any address aligned to its element size (DM_EINVAL otherwise): for a
+ * sip tensor, fp32 rows and bf16 rows off a 16-byte boundary are first
+ * staged (split or copied) into the tensor's own buffer, with the same
+ * result bits. Uses the tensor's own scratch: calls on one tensor must not
+ * overlap on the GPU. */
 int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
             int32_t out_dtype, void *stream, char *err, size_t err_len);
 
@@ -145,13 +150,51 @@ int dm_gemv(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const
  * library's device memory (about 1.45 MiB, held on every GPU that loads the
  * library until exit) instead of the tensor's own buffers. This call makes no
  * cudaMalloc, cudaFree or other allocating call. Limits of that array
- * (DM_EINVAL beyond them): tensors or row shards of at most 262,144 rows,
- * fp32 activations of at most 32,768 columns. The first call on a device
+ * (DM_EINVAL beyond them): tensors or row shards of at most 262,144 rows;
+ * at most 32,768 columns for activations that are staged in it (fp32, or
+ * bf16 off a 16-byte boundary). The first call on a device
  * looks the array's device address up (cudaGetSymbolAddress): make it before
- * capturing a CUDA graph on that device. Every call shares the array, so calls
- * that overlap on the GPU (on any tensor, any stream) race. */
+ * capturing a CUDA graph on that device; the address is kept for the life of
+ * the process, so the device's primary context must not be reset in between.
+ * Every call shares the array, so calls that overlap on the GPU (on any
+ * tensor, any stream) race. */
 int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t M, const void *bias, void *out,
                     int32_t out_dtype, void *stream, char *err, size_t err_len);
+
+/* The launch schedule of a sip tensor's GEMV — this library's counterpart of
+ * the reference's per-tensor launch row (src/drinkme/codec/radix_schedule.py:
+ * 187-206 TABLES, 394-417 select; its Triton knobs are blocks per program
+ * and warps, these are the sm_100a kernel's own). Fields <= 0 (or -1 where
+ * noted) take the measured defaults:
+ *   slots     staging slots of the unit ring, 1..6 (0: five, six at M = 1
+ *             for tensors of 8 or more block columns; fewer when they do not
+ *             fit beside the activations);
+ *   split     0: choose by cost, 1: stream-K over units, 2: whole 16-row
+ *             tiles per CTA;
+ *   skew      stream-K: units fewer than the average that the last CTA to be
+ *             dispatched gets, 0..64 (-1: 4);
+ *   resident  the most block columns whose activations stay resident in
+ *             shared memory for the launch, 0..16 (-1: 16; 0: staged with
+ *             every unit).
+ * Slots and residency change how data is staged, never a result bit; split
+ * and skew change which CTA sums which units, so results move within the
+ * fp32-accumulation bound (every sum's order still depends on the tensor and
+ * its launch alone). Applies to dm_gemv, dm_gemv_noalloc, dm_gemv_gather and
+ * dm_decode; DM_EINVAL outside the ranges. */
+typedef struct dm_launch {
+    int32_t slots, split, skew, resident;
+} dm_launch;
+int dm_tensor_set_launch(dm_tensor *t, const dm_launch *launch, char *err, size_t err_len);
+
+/* What a GEMV of `M` activation rows of `x_dtype` (fp32 rows count three
+ * virtual rows each, at most two rows per launch) would launch: the grid (CTAs),
+ * the split (1 stream-K, 2 whole tiles), the staging slots, 1 when the
+ * activations stay resident, the dynamic shared memory, and the stream-K
+ * weight step (0: an even split). Nothing runs. */
+typedef struct dm_launch_plan {
+    int32_t grid, split, slots, resident, smem_bytes, skew_step;
+} dm_launch_plan;
+int dm_gemv_plan(const dm_tensor *t, int64_t M, int32_t x_dtype, dm_launch_plan *plan, char *err, size_t err_len);
 
 /* Prefill: y[M, rows] = x[M, C] @ W^T (+ bias) for a prefill chunk (any M >=
  * 1; the module routes M >= 9 here), W a sip tensor (fast_path): the weights
@@ -186,6 +229,7 @@ typedef struct dm_gather {
     uint32_t *gen, *done;
     const uint32_t *wait_flags, *wait_gen;
     uint32_t *abort; /* this rank's word, shared by all its linears: set when a wait gives up; later waits then return at once */
+    uint32_t wait_polls; /* the most flag polls of one wait before it gives up (0: 2^23, a few seconds) */
 } dm_gather;
 
 /* dm_gemv of this rank's rows, the outputs stored into every rank's
@@ -227,7 +271,9 @@ int dm_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *off
 /* y[M, R] = x[M, C] @ w[R, C]^T (+ bias) over a raw row-major bf16 weight
  * — replaces radix_ops.gemv_narrow (src/drinkme/codec/radix_ops.py:
  * 401-415) and serves the raw lm_head (swap.stock_linear, swap.py:
- * 681-707). 1 <= M <= 8; fp32 accumulate, bias in fp32, one rounding. */
+ * 681-707). 1 <= M <= 8; fp32 accumulate, bias in fp32, one rounding. w
+ * and x at any address aligned to their element size: 16-byte loads when
+ * both are 16-byte aligned and C % 8 == 0, a scalar loop otherwise. */
 int dm_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int32_t x_dtype, int64_t M,
                 const void *bias, void *out, int32_t out_dtype, void *stream, char *err, size_t err_len);
 

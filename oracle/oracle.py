@@ -238,3 +238,56 @@ def reference_decode(p: dict, first: int = 0, rows: int | None = None, out: np.n
     if rc:
         raise OracleError("reference native: " + err.value.decode())
     return out
+
+
+def reference_encode(U: np.ndarray, widths=(3, 8)) -> dict:
+    """uint16 [R, C] bf16 bits -> a pack dict made by the reference's own
+    native encoder (op 0 plan, op 1 encode; radix_native.py:195-217 drives
+    the same two calls), 1024-weight blocks. The palette comes back padded
+    per tier and is unpadded here as the reference's wrapper does."""
+    lib = reference_native()
+    if lib is None:
+        raise OracleError("the reference's native codec is not built (oracle/_ref)")
+    U = np.ascontiguousarray(U, dtype=np.uint16)
+    R, C = U.shape
+    nb = (C + 1023) // 1024
+    w = np.ascontiguousarray([int(v) for v in widths], dtype=np.uint32)
+    tables = np.zeros(sum(4 * (((1 << int(v)) + 2) // 4) for v in widths[:-1]), dtype=np.uint8)
+    offsets = np.zeros(R * nb + 1, dtype=np.uint32)
+    err = ct.create_string_buffer(1024)
+    res = ct.c_uint64()
+
+    def op(code, data, nwords):
+        rc = lib.radix_native(code, _ptr(U), R, C, R, nb, 7, 8, _ptr(w), len(w), _ptr(tables), _ptr(offsets),
+                              None if data is None else _ptr(data), nwords, 0, 0, ct.byref(res), err, 1024)
+        if rc:
+            raise OracleError("reference native: " + err.value.decode())
+        return res.value
+
+    words = op(0, None, 0)
+    data = np.zeros(words, dtype=np.uint32)
+    op(1, data, data.size)
+    parts, at = [], 0
+    for v in widths[:-1]:
+        n = (1 << int(v)) - 1
+        parts.append(tables[at:at + n])
+        at += ((n + 3) // 4) * 4
+    return {"rx_palette": np.concatenate(parts).astype(np.uint8), "rx_offsets": offsets, "rx_data": data,
+            "R": R, "C": C, "widths": tuple(int(v) for v in widths), "block_size": 1024, "codec": "radix"}
+
+
+def reference_decode_threads(p: dict, workers: int) -> np.ndarray:
+    """The reference's decode with `workers` threads (radix_native.py:245-259:
+    row ranges of about R / (4 workers) rows, one native call each; ctypes
+    releases the GIL during a call)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    R, C = int(p["R"]), int(p["C"])
+    out = np.empty((R, C), dtype=np.uint16)
+    if workers <= 1 or R < 2 * workers:
+        return reference_decode(p, 0, R, out)
+    step = -(-R // (4 * workers))
+    ranges = [(a, min(step, R - a)) for a in range(0, R, step)]
+    with ThreadPoolExecutor(max_workers=workers) as ex:
+        list(ex.map(lambda r: reference_decode(p, r[0], r[1], out[r[0]:r[0] + r[1]]), ranges))
+    return out

@@ -117,3 +117,38 @@ def test_gather_two_gpus_equals_one_gpu():
             ranges = [shard.row_range(W.shape[0], r, world) for W in Ws]
             y = radix_ops.gemv_mc_fused(swap.to_device_radix_fused(packs, dev, ranges), x, None, torch.bfloat16).cpu()
             assert torch.equal(got[:, r * slot: r * slot + y.shape[1]], y), (rank, r)
+
+
+def test_gather_wait_that_never_completes_returns_with_an_error():
+    """A wait whose flags never reach the wanted launch count (a peer that
+    never published: here this rank's own count raised by hand) gives up after
+    its poll limit, records kErrWaitPeer (4) and sets the abort word; the next
+    wait then returns at once even with the library's own multi-second bound.
+    The GPU stays usable: a plain GEMV afterwards is exact."""
+    import time
+
+    dev = torch.device("cuda", 0)
+    Ws, packs = _packs(3)
+    rt = swap.to_device_radix(packs[0], dev)
+    x = torch.randn(1, 4096, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(dev)
+    plan = shard.PeerGather([rt["R"], rt["R"]], 1, torch.bfloat16, 0, 1, dev)
+    try:
+        plan.gemv(rt, x, 0)  # linear 0 runs once: its flag and launch count are 1
+        torch.cuda.synchronize()
+        assert rt["rx_handle"].device_error() == 0 and int(plan.abort_word().item()) == 0
+        plan.launch_count(0).fill_(5)  # wait for a launch that never happens
+        t0 = time.perf_counter()
+        plan.gemv(rt, x, 1, wait=0, wait_polls=1 << 12)
+        torch.cuda.synchronize()
+        assert rt["rx_handle"].device_error() == 4  # kErrWaitPeer
+        assert int(plan.abort_word().item()) != 0
+        plan.gemv(rt, x, 1, wait=0)  # default bound: 2^23 polls, but the abort word ends it
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 2.0
+        assert rt["rx_handle"].device_error() == 4
+        y = radix_ops.gemv_mc_fused(rt, x, None, torch.float32)
+        y64, bound = oracle.gemv_bound(x.float().cpu().numpy(), codec.bits_of(Ws[0]))
+        assert np.all(np.abs(y.cpu().numpy() - y64) <= bound)
+        assert rt["rx_handle"].device_error() == 0
+    finally:
+        plan.close()

@@ -415,9 +415,9 @@ def test_no_device_errors_recorded(runtimes):
 def test_stock_linear_modes_on_the_gpu(monkeypatch):
     """The raw Linears' one-row routes (swap.py:681-742): "b200" / "triton"
     and a raw descriptor run the raw GEMV (fp32 accumulate, bias, one
-    rounding: bitwise dm_gemv_raw), "mv" torch.mv under cuBLASLt, "linear"
+    rounding: bitwise dm_gemv_raw), "mv" torch.mv / addmv, "linear"
     F.linear; all within bf16 rounding of a float64 reference, and M = 9
-    always F.linear. StockLinear adopts a Linear without a copy."""
+    always F.linear. StockLinear adopts a Linear in place, without a copy."""
     g = torch.Generator().manual_seed(9)
     w = (torch.randn(2048, 1024, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
     b = (torch.randn(2048, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
@@ -435,5 +435,31 @@ def test_stock_linear_modes_on_the_gpu(monkeypatch):
     lin = torch.nn.Linear(1024, 2048, device=DEV, dtype=torch.bfloat16)
     model = torch.nn.Sequential(lin)
     assert swap.install_stock_gemv(model, DEV, "b200") == 1
-    assert isinstance(model[0], swap.StockLinear) and model[0].weight is lin.weight
+    assert model[0] is lin and isinstance(lin, swap.StockLinear)
     assert torch.equal(model[0](x), swap.stock_linear(x, lin.weight, lin.bias, "b200"))
+
+
+def test_runtime_dict_carries_the_reference_device_arrays():
+    """to_device_radix's dict has the reference's device keys (swap.py:80-161)
+    that reference code reads: rx_data's device (radix_ops.py:426, swap.py:
+    433), rx_offsets / rx_palette / rx_schedule for read_bytes' formula
+    (radix_ops.py:435-441), which must give this package's count."""
+    g = torch.Generator().manual_seed(41)
+    for R, C, prof, rows in ((300, 4096, "gulp", (0, 300)), (4096, 12288, "sip", (1024, 2048)),
+                             (40, 1000, "sip", (0, 40))):
+        W = (torch.randn(R, C, generator=g) * 0.02).to(torch.bfloat16)
+        p = codec.pack_weight_radix(W, prof)
+        rt = swap.to_device_radix(p, DEV, *rows)
+        for k in ("rx_data", "rx_offsets", "rx_palette", "rx_schedule"):
+            assert rt[k].device == torch.device(DEV), k
+        nb = -(-C // 1024)
+        assert rt["rx_offsets"].numel() == (rows[1] - rows[0]) * nb + 1
+        off = np.asarray(p["rx_offsets"], dtype=np.int64)[rows[0] * nb:rows[1] * nb + 1]
+        assert np.array_equal(rt["rx_offsets"].cpu().view(torch.int32).numpy().astype(np.int64), off - off[0])
+        assert np.array_equal(rt["rx_palette"].cpu().view(torch.int32).numpy().view(np.uint32),
+                              codec.padded_palette_words(p))
+        formula = int(rt["NW"]) * 4 + sum(rt[k].numel() * rt[k].element_size()
+                                          for k in ("rx_offsets", "rx_palette", "rx_schedule"))
+        assert formula == radix_ops.read_bytes(rt)
+        assert rt["rx_data"].numel() * 4 == rt["rx_handle"].info.layout_bytes
+        assert swap.resident_bytes(rt) >= rt["rx_handle"].info.resident_bytes

@@ -153,17 +153,22 @@ def test_schedule_shape_classes_and_overrides():
     assert radix_schedule.family((3, 8)) == "sip" and radix_schedule.family((2, 2, 4, 8)) == "scheduled"
     L = radix_schedule.select(4096, 4096, 1024, (3, 8))
     assert L.box_class == "b200" and L.kernel == "sip-mma-sm100a" and L.source == "table"
+    assert L.knobs() == (0, 0, 4, 16)
     assert radix_schedule.select(4096, 4100, 1024, (3, 8)).kernel == "generic-sm100a"
-    assert radix_schedule.select(4096, 4096, 1024, (2, 2, 4, 8)).kernel == "generic-sm100a"
-    e = radix_schedule.select(4096, 4096, 1024, (3, 8), override="tiles=row,warps=4")
-    assert e.gemv_tiles == 0 and e.gemv_warps == 4 and e.source == "env"
-    assert radix_schedule.select(1, 1, override="spike").gemv_warps == 2
+    # gulp with whole 1024-weight blocks is re-encoded as sip by the loader
+    assert radix_schedule.select(4096, 4096, 1024, (2, 2, 4, 8)).kernel == "sip-mma-sm100a"
+    e = radix_schedule.select(4096, 4096, 1024, (3, 8), override="slots=3,split=tiles,skew=0,resident=0")
+    assert e.knobs() == (3, 2, 0, 0) and e.source == "env"
+    assert radix_schedule.select(1, 1, override="slots=rule").slots == 0
+    assert radix_schedule.select(1, 1, override="spike").knobs() == (2, 2, 0, 0)
+    for bad in ("slots=7", "split=rows", "skew=-1", "resident=17", "warps=4", "bogus=1"):
+        with pytest.raises(ValueError):
+            radix_schedule.select(1, 1, override=bad)
+    per = radix_schedule.select(1024, 4096, override='{"narrow": {"slots": 2, "split": "stream"}}')
+    assert per.knobs() == (2, 1, 4, 16)
+    assert radix_schedule.select(4096, 4096, override='{"narrow": {"slots": 2}}').slots == 0  # other classes: the row
     with pytest.raises(ValueError):
-        radix_schedule.select(1, 1, override="warps=3")
-    with pytest.raises(ValueError):
-        radix_schedule.select(1, 1, override="bogus=1")
-    per = radix_schedule.select(1024, 4096, override='{"narrow": {"gemv_warps": 2}}')
-    assert per.gemv_warps == 2
+        radix_schedule.select(1, 1, override='{"narrow": {"warps": 2}}')
 
 
 def test_registry_rows():
@@ -247,29 +252,24 @@ def test_stock_linear_off_the_accelerator_is_f_linear():
     assert torch.equal(swap.stock_linear(x, w, b, "b200", swap.raw_gemv_dict(64, 1024)), want)
 
 
-def test_eligible_linears_skip_tied_heads_and_swap_replaces():
-    """The tied-lm_head rule by Parameter identity (works on meta models too)
-    and the swap walker (swap.py:857-897)."""
+def test_eligible_and_in_place_adoption():
+    """Which Linears the codec takes (swap.py:850-854), and the raw routes'
+    adoption: the Linear itself re-classed, its Parameters untouched; nothing
+    is installed off the accelerator."""
     import torch
 
     from drinkme_b200 import swap
 
-    class Tiny(torch.nn.Module):
-        def __init__(self, device):
-            super().__init__()
-            self.embed = torch.nn.Embedding(2048, 1024, device=device, dtype=torch.bfloat16)
-            self.proj = torch.nn.Linear(1024, 1024, bias=True, device=device, dtype=torch.bfloat16)
-            self.small = torch.nn.Linear(1024, 64, device=device, dtype=torch.bfloat16)
-            self.lm_head = torch.nn.Linear(1024, 2048, bias=False, device=device, dtype=torch.bfloat16)
-            self.lm_head.weight = self.embed.weight
-
-    for device in ("meta", "cpu"):
-        names = [n for n, *_ in swap.eligible_linears(Tiny(device))]
-        assert names == ["proj"], (device, names)
-    m = Tiny("cpu")
-    stats = swap.swap_linears(m, lambda w, b: (torch.nn.Identity(), {"rows": w.shape[0]}), device="cpu")
-    assert isinstance(m.proj, torch.nn.Identity) and isinstance(m.lm_head, torch.nn.Linear)
-    assert stats == [{"rows": 1024, "name": "proj"}]
+    big = torch.nn.Linear(1024, 2048, bias=False, dtype=torch.bfloat16)
+    assert swap.eligible(big)
+    assert not swap.eligible(torch.nn.Linear(1024, 64, dtype=torch.bfloat16))
+    assert not swap.eligible(torch.nn.Linear(1024, 2048))  # fp32
+    assert not swap.eligible(torch.nn.Linear(1026, 2048, dtype=torch.bfloat16))  # columns % 4
+    assert not swap.eligible(torch.nn.Embedding(2048, 1024))
+    w = big.weight
+    got = swap.StockLinear.adopt(big, "mv")
+    assert got is big and isinstance(big, swap.StockLinear) and big.weight is w and big.stock_gemv == "mv"
+    m = torch.nn.Sequential(torch.nn.Linear(1024, 64, dtype=torch.bfloat16))
     assert not swap.codec_tree(m)
     assert swap.install_stock_gemv(m, "cpu", "b200") == 0
     assert swap.install_narrow(m, "cpu") == []

@@ -67,3 +67,63 @@ def test_gather_rows_two_gloo_ranks(R, M):
         assert p.exitcode == 0
     got = sorted(q.get(timeout=10) for _ in range(2))
     assert got == [(0, True, (M, R)), (1, True, (M, R))]
+
+
+def _exchange_worker(rank, world, port, leave, q):
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=6))
+    if rank == leave:
+        os._exit(0)  # this rank leaves before the handle exchange
+    t0 = time.perf_counter()
+    try:
+        shard.exchange_handles(bytes([rank]) * 64, world)
+        q.put((rank, "returned", time.perf_counter() - t0))
+    except Exception as e:  # noqa: BLE001 - the survivor must raise, whatever the backend's type
+        q.put((rank, type(e).__name__, time.perf_counter() - t0))
+    os._exit(0)
+
+
+def test_handle_exchange_raises_when_a_rank_left():
+    """PeerGather's collective IPC-handle exchange over two gloo ranks, one of
+    which exits before it: the survivor raises within the process group's
+    timeout (6 s here) instead of waiting forever."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, 1, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    rank, what, secs = q.get(timeout=10)
+    assert rank == 0 and what != "returned", what
+    assert secs < 6 + 10
+
+
+def _exchange_ok_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank, shard.exchange_handles(bytes([rank + 1]) * 64, world)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_handle_exchange_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_exchange_ok_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = dict(q.get(timeout=10) for _ in range(2))
+    assert got[0] == got[1] == [bytes([1]) * 64, bytes([2]) * 64]

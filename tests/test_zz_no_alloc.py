@@ -66,7 +66,7 @@ def test_noalloc_refuses_sizes_beyond_its_static_scratch():
     x = torch.randn(1, 33 * 1024, device=DEV)
     with pytest.raises(ValueError, match="exceed the static scratch"):
         _call("dm_gemv_noalloc", rt, x, None, torch.empty(1, 16, dtype=torch.float32, device=DEV))
-    xb = x.to(torch.bfloat16)  # bf16 activations need no split buffer: served
+    xb = x.to(torch.bfloat16)  # aligned bf16 activations need no staging: served
     y = _call("dm_gemv_noalloc", rt, xb, None, torch.empty(1, 16, dtype=torch.float32, device=DEV))
     assert torch.equal(y, _call("dm_gemv", rt, xb, None, torch.empty(1, 16, dtype=torch.float32, device=DEV)))
 
@@ -76,3 +76,45 @@ def test_noalloc_refuses_m_outside_one_to_eight():
     with pytest.raises(ValueError, match="outside 1"):
         _call("dm_gemv_noalloc", rt, torch.zeros(9, 4096, dtype=torch.bfloat16, device=DEV), None,
               torch.empty(9, 64, dtype=torch.bfloat16, device=DEV))
+
+
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float32])
+def test_noalloc_misaligned_activations_match_dm_gemv(xdt):
+    """Activations one element past a 16-byte boundary are staged into the
+    static array (copied, or split for fp32) and give dm_gemv's bits."""
+    rt, bits = _tensor(4096, 12288, "sip", seed=31)
+    g = torch.Generator().manual_seed(8)
+    for M in (1, 3, 8):
+        buf = torch.empty(M * 12288 + 1, dtype=xdt, device=DEV)
+        buf[1:] = torch.randn(M * 12288, generator=g).to(xdt).to(DEV)
+        x = buf[1:].view(M, 12288)
+        assert x.data_ptr() % 16 != 0
+        ref = _call("dm_gemv", rt, x, None, torch.empty(M, 4096, dtype=torch.float32, device=DEV))
+        for _ in range(2):
+            got = _call("dm_gemv_noalloc", rt, x, None, torch.full((M, 4096), float("nan"), device=DEV))
+            assert torch.equal(got, ref)
+        y64, bound = oracle.gemv_bound(x.float().cpu().numpy(), bits)
+        assert np.all(np.abs(ref.cpu().numpy() - y64) <= bound)
+    assert rt["rx_handle"].device_error() == 0
+
+
+def test_noalloc_calls_allocate_no_device_memory():
+    """After a first call (which looks the array's address up), further calls
+    of every kind leave the device's free memory unchanged."""
+    rt, _ = _tensor(4096, 12288, "sip", seed=32)
+    g = torch.Generator().manual_seed(9)
+    xs = [torch.randn(2, 12288, generator=g).to(torch.bfloat16).to(DEV),
+          torch.randn(3, 12288, generator=g).to(DEV)]
+    buf = torch.empty(2 * 12288 + 1, dtype=torch.bfloat16, device=DEV)
+    xs.append(buf[1:].view(2, 12288))
+    outs = [torch.empty(x.shape[0], 4096, dtype=torch.float32, device=DEV) for x in xs]
+    for x, o in zip(xs, outs):
+        _call("dm_gemv_noalloc", rt, x, None, o)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for x, o in zip(xs, outs):
+            _call("dm_gemv_noalloc", rt, x, None, o)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
