@@ -532,9 +532,10 @@ def config5_prefill(device):
                      "prefill kernel (decoded tiles in shared memory, TMEM accumulators)", "per_linear": out}
 
 
-def cublas_arm(shapes, device, reps=20):
+def cublas_arm(shapes, device, reps=10):
     """cuBLAS dense bf16 (F.linear, M = 1) on uncompressed weights of the same
-    shapes, rotating over copies larger than L2: µs per call and GB/s."""
+    shapes, rotating over copies larger than 3x L2 inside one CUDA graph (as
+    this package's launches are timed): µs per call and GB/s."""
     import torch
 
     res = {}
@@ -542,20 +543,7 @@ def cublas_arm(shapes, device, reps=20):
         copies = max(2, int(3 * 126e6 // (R * C * 2)) + 1)
         ws = [(torch.randn((R, C), device=device) * 0.02).to(torch.bfloat16) for _ in range(copies)]
         x = torch.randn((1, C), device=device).to(torch.bfloat16)
-        for w in ws:
-            torch.nn.functional.linear(x, w)
-        torch.cuda.synchronize(device)
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        n = 0
-        for _ in range(reps):
-            for w in ws:
-                torch.nn.functional.linear(x, w)
-                n += 1
-        b.record()
-        torch.cuda.synchronize(device)
-        us = a.elapsed_time(b) / n * 1e3
+        us = _graph_us(lambda: [torch.nn.functional.linear(x, w) for w in ws], device, reps) / copies
         res[name] = {"shape": [R, C], "us": round(us, 2), "gbs": round(R * C * 2 / us * 1e-3, 1)}
         del ws
         torch.cuda.empty_cache()

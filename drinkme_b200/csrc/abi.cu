@@ -50,6 +50,7 @@ void free_tensor(dm_tensor *t) {
     DeviceGuard g(t->device);
     if (t->d_data) cudaFree(t->d_data);
     if (t->d_unit16) cudaFree(t->d_unit16);
+    if (t->d_rowdir) cudaFree(t->d_rowdir);
     if (t->S.partials) cudaFree(t->S.partials);
     if (t->S.counters) cudaFree(t->S.counters);
     if (t->S.xsplit) cudaFree(t->S.xsplit);
@@ -108,7 +109,7 @@ int create_from_parts(const dm::PackPart *given, int nparts, int32_t device, dm_
     std::string msg;
     dm_tensor *t = new dm_tensor();
     t->device = device;
-    std::string bytes, unit16;
+    std::string bytes, unit16, rowdir;
     // the source packs' own read bytes and payload words (the reference's count)
     int64_t src_read = 0, src_words = 0;
     for (int i = 0; i < nparts; ++i) {
@@ -127,7 +128,7 @@ int create_from_parts(const dm::PackPart *given, int nparts, int32_t device, dm_
                 transcoded = false;
                 break;
             }
-    if (dm::build_layout(parts.data(), nparts, t->L, bytes, unit16, msg)) {
+    if (dm::build_layout(parts.data(), nparts, t->L, bytes, unit16, msg, &rowdir)) {
         delete t;
         return fail(err, err_len, DM_EINVAL, msg);
     }
@@ -158,6 +159,15 @@ int create_from_parts(const dm::PackPart *given, int nparts, int32_t device, dm_
         return cuda_fail(err, err_len, e, "cudaMemcpy(layout)");
     }
     t->resident_bytes = bytes.size() + unit16.size();
+    if (!rowdir.empty()) {
+        if ((e = cudaMalloc(&t->d_rowdir, rowdir.size())) != cudaSuccess ||
+            (e = cudaMemcpy(t->d_rowdir, rowdir.data(), rowdir.size(), cudaMemcpyHostToDevice)) != cudaSuccess) {
+            free_tensor(t);
+            return cuda_fail(err, err_len, e, "cudaMalloc(row directory)");
+        }
+        t->rowdir_bytes = rowdir.size();
+        t->resident_bytes += rowdir.size();
+    }
     if ((e = cudaMalloc(&t->S.err, sizeof(int))) != cudaSuccess || (e = cudaMemset(t->S.err, 0, sizeof(int))) != cudaSuccess) {
         free_tensor(t);
         return cuda_fail(err, err_len, e, "cudaMalloc(error word)");
@@ -249,6 +259,15 @@ extern "C" int dm_tensor_clone(const dm_tensor *src, dm_tensor **out, char *err,
         return cuda_fail(err, err_len, e, "dm_tensor_clone");
     }
     t->resident_bytes = src->data_bytes + ubytes;
+    if (src->d_rowdir) {
+        if ((e = cudaMalloc(&t->d_rowdir, src->rowdir_bytes)) != cudaSuccess ||
+            (e = cudaMemcpy(t->d_rowdir, src->d_rowdir, src->rowdir_bytes, cudaMemcpyDeviceToDevice)) != cudaSuccess) {
+            free_tensor(t);
+            return cuda_fail(err, err_len, e, "dm_tensor_clone(row directory)");
+        }
+        t->rowdir_bytes = src->rowdir_bytes;
+        t->resident_bytes += src->rowdir_bytes;
+    }
     if (src->L.fast_sip) {
         const size_t pbytes = (size_t)t->S.max_workers * 2 * 128 * sizeof(float);
         const size_t cbytes = (size_t)t->L.tiles * sizeof(int);

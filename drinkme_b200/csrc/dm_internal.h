@@ -67,6 +67,8 @@ struct TensorLayout {
     int32_t npal_words = 0;
     // per-tier word offset of each tier's table inside pal_words
     int32_t tier_table[8] = {0};
+    // sip: the first eight parts' exponent tables (th0, th1, tl0, tl1), as the unit headers hold them
+    uint32_t part_tabs[8][4] = {{0}};
 };
 
 // Launch knobs of the sip kernels (dm_tensor_set_launch): negative or zero
@@ -96,6 +98,8 @@ struct dm_tensor {
     uint8_t *d_data = nullptr;     // unit-major layout + tail pad
     size_t data_bytes = 0;
     uint32_t *d_unit16 = nullptr;  // [units + 1] unit starts in 16-byte units
+    uint32_t *d_rowdir = nullptr;  // sip: [16-row padded rows][NB][2] stream offset (16-byte units), nesc | part << 16
+    size_t rowdir_bytes = 0;
     dm::Scratch S;
     dm::LaunchKnobs K;
     int32_t sms = 148;
@@ -110,7 +114,7 @@ void set_error(char *err, size_t len, const std::string &msg);
 int validate_pack(const uint8_t *palette, size_t npal, const uint32_t *offsets, size_t noff, size_t nwords,
                   int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, std::string &msg);
 int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string &bytes, std::string &unit16,
-                 std::string &msg);
+                 std::string &msg, std::string *rowdir = nullptr);
 int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
 void decode_rows(const PackPart &P, uint16_t *out);
 int64_t prefill_workspace_bytes(const dm_tensor *t, int64_t M);

@@ -267,7 +267,7 @@ static void sip_tables(const uint8_t *palette, uint32_t tab[4]) {
 }
 
 int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string &bytes, std::string &unit16,
-                 std::string &msg) {
+                 std::string &msg, std::string *rowdir) {
     if (nparts < 1) { msg = "no tensor parts"; return 1; }
     const PackPart &P0 = parts[0];
     const int64_t C = P0.C;
@@ -338,7 +338,10 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
     }
     std::vector<uint32_t> tabs((size_t)nparts * 4, 0);
     if (L.fast_sip)
-        for (int p = 0; p < nparts; ++p) sip_tables(parts[p].palette, &tabs[(size_t)p * 4]);
+        for (int p = 0; p < nparts; ++p) {
+            sip_tables(parts[p].palette, &tabs[(size_t)p * 4]);
+            if (p < 8) std::memcpy(L.part_tabs[p], &tabs[(size_t)p * 4], 16);
+        }
     auto block_of = [&](int64_t i, const PackPart *&P, int64_t &gb) {
         const int64_t r = i / NB, b = i % NB;
         P = &parts[rpart[r]];
@@ -449,6 +452,24 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
             }
         }
     });
+    if (fast && rowdir) {
+        // per row block (16-row padded rows x block columns): the absolute
+        // offset of its streams in 16-byte units, and its escape count with
+        // its part index (the prefill kernel's one-load directory)
+        const int64_t rows16 = L.tiles * kUnitRows;
+        rowdir->assign((size_t)(rows16 * NB) * 8, '\0');
+        uint32_t *rd = reinterpret_cast<uint32_t *>(&(*rowdir)[0]);
+        parallel_for(L.units, [&](int64_t u) {
+            const int64_t tile = u / NB, b = u % NB;
+            const RowEntry *hdr = reinterpret_cast<const RowEntry *>(out + ustart[u]);
+            for (int s = 0; s < kUnitRows; ++s) {
+                const int64_t r = tile * kUnitRows + s;
+                const uint32_t part = r < rows ? (uint32_t)rpart[r] : 0u;
+                rd[(r * NB + b) * 2] = (uint32_t)(ustart[u] / 16) + hdr[s].off16;
+                rd[(r * NB + b) * 2 + 1] = (uint32_t)hdr[s].nesc | (part << 16);
+            }
+        });
+    }
     return 0;
 }
 

@@ -1,7 +1,7 @@
-// The prefill path on sm_100a: Y[M, rows] = X[M, C] @ W^T for M >= 9
-// activation rows (a prefill chunk) with W a sip tensor, the weights decoded
-// into shared memory and contracted on the 5th-generation tensor cores
-// (tcgen05.mma, fp32 accumulators in tensor memory).
+// The prefill path on sm_100a: Y[M, rows] = X[M, C] @ W^T for a prefill
+// chunk (the module routes M >= 9 here) with W a sip tensor, the weights
+// decoded into shared memory and contracted on the 5th-generation tensor
+// cores (tcgen05.mma, fp32 accumulators in tensor memory).
 //
 // Reference: the dense arm (radix_kernel_gpu.py:615-636 `_dense`, swap.py:
 // 361-378) decodes the whole weight to HBM, then runs one bf16 GEMM. The
@@ -9,35 +9,43 @@
 // rounding; here the decoded weight never leaves the SM.
 //
 // Design:
-//   * One CTA per 128 weight rows (the MMA's N), covering up to 512
-//     activation rows in up to four 128-row token tiles (the MMA's M), one
-//     fp32 accumulator per token tile in tensor memory (128 lanes x 128
-//     columns each). The K loop runs over 64-wide windows.
-//   * Decode warps 0-7: threads i and 128 + i own weight row i of the CTA,
-//     taking alternate windows. Per window a thread reads the row's 64
-//     literal bytes and 64 tier-0 codes (six words) straight from HBM (its
-//     next window's prefetched into registers while it decodes), decodes
-//     them with the GEMV's byte-parallel table lookups into bf16, and writes
-//     the 128-byte K-major row of the B tile in the 128-byte swizzled layout
-//     the tensor core reads (16-byte chunk c at c XOR (row mod 8)); escaped
-//     weights take their terminal exponent from the escape index and are
-//     patched in place. A fence makes the generic writes visible to the
-//     tensor core's (async) reads; the warps then arrive on the stage's
-//     barrier.
-//   * Warp 8 stages the activation window of every token tile with one bulk
-//     copy: a pre-pass (x_swizzle_kernel) wrote X window-major in the same
-//     swizzled layout, so each window is one contiguous block.
-//   * Warp 9 allocates the tensor memory; one of its threads issues the MMAs
-//     (kind::f16, bf16 x bf16 -> fp32, M = 128, N = 128, K = 16) and commits
-//     each window's MMAs to the barriers that free its stages.
-//   * Epilogue: warps 0-3 read the accumulators (tcgen05.ld, thread = token
-//     row, 32 weight rows per load), add the bias in fp32, round once, store.
+//   * A TILE is 128 weight rows (the MMA's M: the decoded weights are the A
+//     operand) by up to 256 activation rows (the MMA's N: the activations are
+//     the B operand), over the whole K; its fp32 accumulator takes 256 of the
+//     CTA's 512 tensor-memory columns, so two accumulators alternate and one
+//     tile's epilogue runs under the next tile's MMAs.
+//   * Persistent stream-K over K windows of 64: one CTA per SM; the windows of
+//     every tile, tile after tile (a weight row tile's activation tiles next to
+//     each other, so its compressed bytes come from L2 the second time), are
+//     split evenly over the CTAs. A CTA's first and last tiles may be shared
+//     with its neighbours (PIECES); it runs those first. A piece's fp32
+//     partial goes to the workspace, and for each quarter of the tile's rows
+//     the last piece to arrive (an acquire-release counter) adds every
+//     piece's partial in CTA order and writes the outputs.
+//   * Warps 0-7 decode: a lane pair per weight row, each lane 32 weights of a
+//     window, from the loader's code planes with the GEMV's byte-parallel
+//     table lookups (escaped weights come out as sign | 0 | mantissa), into
+//     the 128-byte-swizzled K-major tile the tensor core reads. An escaped
+//     weight's terminal exponent is its rank among the row block's escapes:
+//     the lane pair counts code-7 nibbles as it goes and ORs the exponent in
+//     from the row's terminal stream, staged per block column in shared
+//     memory by cp.async. Data for window j + 2 is loaded while window j is
+//     decoded; the row-block directory entry of the next block column one
+//     block column ahead.
+//   * Warp 12 loads each activation window with one TMA tensor copy (no
+//     multicast) in the same swizzled layout; warp 13 owns the tensor memory
+//     and one of its lanes issues the MMAs (kind::f16, M = 128, N = tokens,
+//     K = 16) and commits each window to the barriers that free its stages.
+//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
+//     add the bias in fp32, round once and store; or write a piece's partial.
 //   * Every wait is bounded (the device error word records a wait that gave
 //     up); the tensor memory is freed on every path.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 #include <string>
 
 #include "dm_device.cuh"
@@ -47,18 +55,30 @@ namespace dm {
 
 namespace {
 
-constexpr int kPfRows = 128;         // weight rows per CTA (MMA N)
-constexpr int kPfTok = 128;          // activation rows per token tile (MMA M)
-constexpr int kPfMaxTiles = 4;       // token tiles per pass (512 tensor-memory columns)
-constexpr int kPfBStages = 4;        // decoded weight windows in flight
-constexpr int kPfAStages = 2;        // activation windows in flight
-constexpr int kPfWin = 64;           // K per window (one 128-byte swizzle row of bf16)
-constexpr int kPfDecWarps = 8;       // two threads per weight row, alternate windows
-constexpr int kPfActWarp = kPfDecWarps, kPfMmaWarp = kPfDecWarps + 1;
-constexpr int kPfThreads = (kPfDecWarps + 2) * 32;
-constexpr int kBTile = kPfRows * 128;          // 16 KB
-constexpr int kPfEsc = 64;                     // escapes per row block staged in shared memory
-constexpr int kATile = kPfTok * 128;           // 16 KB per token tile
+constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
+constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
+constexpr int kPfStages = 4;      // windows in flight (both operands)
+constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
+constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kPfProd = 12;       // warp 12: activation TMA
+constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
+constexpr int kPfThreads = 14 * 32;
+constexpr int kWStage = kPfRows * 128;    // 16 KB: 128 rows x 64 bf16
+constexpr int kXStage = kPfTokMax * 128;  // 32 KB: 256 rows x 64 bf16
+constexpr int kTermRing = 4;              // block columns of staged terminal bytes
+constexpr int kTermRow = 64;              // terminal bytes staged per row (the rest read from HBM)
+constexpr int kTermStage = kPfRows * kTermRow;
+constexpr int kAccCols = 256;             // tensor-memory columns per accumulator
+constexpr int kMaxParts = 8;
+
+constexpr int kOffX = 0;
+constexpr int kOffW = kOffX + kPfStages * kXStage;
+constexpr int kOffTerm = kOffW + kPfStages * kWStage;
+constexpr int kOffBar = kOffTerm + kTermRing * kTermStage;
+constexpr int kNumBars = 4 * kPfStages + 5;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kOffTabs = kOffTmem + 16;
+constexpr int kSmemBytes = kOffTabs + kMaxParts * 16 + 1024;  // + alignment slack
 
 // Shared-memory matrix descriptor of a 128-byte-swizzled K-major tile whose
 // 8-row groups are 1024 bytes apart (rows 128 bytes): start address,
@@ -72,15 +92,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
 // Instruction descriptor of kind::f16: fp32 accumulate (bits 4-5 = 1), A and
 // B bf16 (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at
 // bits 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPfRows >> 3) << 17) |
-                            ((uint32_t)(kPfTok >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         :
-        : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+        : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -104,11 +126,37 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// The selectors of 16 codes (quarter t of a quad) from the unit's code
-// planes (the GEMV's code_selectors): v = plane word 4q + t, P = bit-2 word
-// 64 + 2q + t / 2.
-__device__ __forceinline__ void selectors16(uint32_t v, uint32_t P, int t, uint32_t &s0, uint32_t &s1) {
-    const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
+// One 2-D TMA tile load global -> shared (no multicast), completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 16 bytes global -> shared, asynchronously (the LDGSTS path, L2 only).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most `n` (0..3) of this thread's newest groups are pending.
+__device__ __forceinline__ void cp_async_wait(int n) {
+    if (n <= 0)
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else if (n == 1)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else if (n == 2)
+        asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else
+        asm volatile("cp.async.wait_group 3;" ::: "memory");
+}
+
+// The selectors of 16 codes (quarter t of a 64-weight window) from a row
+// block's code planes: v = its low-two-bit word, P = its bit-2 word (the
+// GEMV's code_selectors).
+__device__ __forceinline__ void selectors16(uint32_t v, uint32_t P, uint32_t rl, uint32_t rh, uint32_t &s0,
+                                            uint32_t &s1) {
     s0 = (v & 0x33333333u) | (__funnelshift_l(P, P, rl) & 0x44444444u);
     s1 = ((v >> 2) & 0x33333333u) | (__funnelshift_l(P, P, rh) & 0x44444444u);
 }
@@ -124,52 +172,175 @@ __device__ __forceinline__ void dec4(uint32_t L, uint32_t S, uint32_t th0, uint3
     p23 = __byte_perm(lo, hi, 0x7362);
 }
 
+// Bit 4i set where nibble i of a selector word holds code 7 (an escape).
+__device__ __forceinline__ uint32_t escape_nibbles(uint32_t s) { return s & (s >> 1) & (s >> 2) & 0x11111111u; }
+
 struct PfArgs {
     const uint8_t *data;
-    const uint32_t *unit16;
+    const uint2 *rowdir;     // [16-row padded rows][NB]: stream offset (16-byte units), nesc | part << 16
     int64_t rows, NB;
-    const uint8_t *xs;  // swizzled activations: [windows][ntiles * 128 rows][128 bytes]
-    int32_t ntiles, m;   // token tiles of this pass, real activation rows of it
+    int32_t M, ntok, ntt;    // real activation rows, activation tiles, activation rows per tile (MMA N)
+    int32_t nparts;
+    int64_t ntiles, nwin, W; // tiles (row tiles x activation tiles), windows per tile, all windows
+    uint32_t idesc;
     const uint16_t *bias;
-    void *out;           // [m][rows] of this pass
+    void *out;               // [M][rows]
     int32_t out_f32;
+    float *part;             // [grid][2][128][ntt]: a CTA's partials of its first / last tile
+    int *counters;           // [ntiles][4], zero on entry
     int *err;
+    uint32_t tabs[kMaxParts][4];
 };
 
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
+// The CTA's windows [x0, x1) of the whole sequence (tile-major), as PIECES:
+// its first tile when partial, its last tile when partial, then its whole
+// tiles in order.
+struct Range {
+    int64_t x0, x1, tA, tB, nwin;
+    bool pA, pB;
+    int32_t n;
+    __device__ void init(int64_t c, int64_t G, int64_t W, int64_t nw) {
+        nwin = nw;
+        x0 = c * W / G;
+        x1 = (c + 1) * W / G;
+        n = 0;
+        pA = pB = false;
+        tA = tB = 0;
+        if (x1 <= x0) return;
+        tA = x0 / nwin;
+        tB = (x1 - 1) / nwin;
+        if (tA == tB) {
+            n = 1;
+            return;
+        }
+        pA = x0 % nwin != 0;
+        pB = x1 % nwin != 0;
+        n = (pA ? 1 : 0) + (pB ? 1 : 0) + (int32_t)((pB ? tB : tB + 1) - (pA ? tA + 1 : tA));
+    }
+    __device__ void piece(int32_t i, int64_t &t, int32_t &w0, int32_t &w1) const {
+        if (tA == tB) {
+            t = tA;
+            w0 = (int32_t)(x0 - tA * nwin);
+            w1 = (int32_t)(x1 - tA * nwin);
+            return;
+        }
+        if (pA) {
+            if (i == 0) {
+                t = tA;
+                w0 = (int32_t)(x0 - tA * nwin);
+                w1 = (int32_t)nwin;
+                return;
+            }
+            --i;
+        }
+        if (pB) {
+            if (i == 0) {
+                t = tB;
+                w0 = 0;
+                w1 = (int32_t)(x1 - tB * nwin);
+                return;
+            }
+            --i;
+        }
+        t = (pA ? tA + 1 : tA) + i;
+        w0 = 0;
+        w1 = (int32_t)nwin;
+    }
+};
+
+__device__ __forceinline__ int64_t cta_start(int64_t c, int64_t G, int64_t W) { return c * W / G; }
+
+// The CTA whose windows hold window x.
+__device__ __forceinline__ int64_t owner_of(int64_t x, int64_t G, int64_t W) {
+    int64_t c = x * G / W;
+    while (c + 1 < G && cta_start(c + 1, G, W) <= x) ++c;
+    while (c > 0 && cta_start(c, G, W) > x) --c;
+    return c;
+}
+
+// A position in the CTA's window sequence: piece pi, window w of tile t.
+struct Cursor {
+    int32_t pi, w, w1;
+    int64_t t, rt;  // tile, its weight row tile (t / ntok)
+    bool done;
+    __device__ void begin(const Range &R, int32_t ntok) {
+        pi = 0;
+        done = R.n == 0;
+        t = rt = 0;
+        w = w1 = 0;
+        if (!done) {
+            R.piece(0, t, w, w1);
+            rt = t / ntok;
+        }
+    }
+    __device__ void next(const Range &R, int32_t ntok) {
+        if (++w < w1) return;
+        if (++pi >= R.n) {
+            done = true;
+            return;
+        }
+        R.piece(pi, t, w, w1);
+        rt = t / ntok;
+    }
+    // the first window of the next block column (segment) after this one
+    __device__ bool next_segment(const Range &R, int64_t &t2, int32_t &w2) const {
+        const int32_t e = ((w >> 4) + 1) << 4;
+        if (e < w1) {
+            t2 = t;
+            w2 = e;
+            return true;
+        }
+        if (pi + 1 >= R.n) return false;
+        int32_t x;
+        R.piece(pi + 1, t2, w2, x);
+        return true;
+    }
+};
+
+// A window's loaded operands for one lane: 32 literal bytes, two code-plane
+// words and the bit-2 word, and where they came from.
+struct Win {
+    uint4 L0, L1;
+    uint32_t c0, c1, P;
+    uint2 dir;    // the row block's directory entry
+    bool real;
+};
+
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid_constant__ CUtensorMap xmap, PfArgs a) {
+    extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned tiles (the swizzle pattern follows address bits 7-9)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *btile = smem;                                    // [kPfBStages][128 rows][128 B]
-    uint8_t *atile = btile + kPfBStages * kBTile;             // [kPfAStages][ntiles][128 rows][128 B]
-    // per weight row, the escapes of its current block column: position | terminal << 16
-    uint32_t *esc = reinterpret_cast<uint32_t *>(atile + kPfAStages * kPfMaxTiles * kATile);  // [128][kPfEsc]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(esc + kPfRows * kPfEsc);
-    uint64_t *b_full = bar, *b_empty = bar + kPfBStages;
-    uint64_t *a_full = bar + 2 * kPfBStages, *a_empty = a_full + kPfAStages;
-    uint64_t *acc_done = a_empty + kPfAStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_done + 1);
+    uint8_t *xs = smem + kOffX;
+    uint8_t *ws = smem + kOffW;
+    uint8_t *term = smem + kOffTerm;  // [kTermRing][128 rows][64 bytes]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint64_t *x_full = bar, *x_empty = bar + kPfStages, *w_full = bar + 2 * kPfStages, *w_empty = bar + 3 * kPfStages;
+    uint64_t *acc_full = bar + 4 * kPfStages, *acc_empty = acc_full + 2, *drained = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffTmem);
+    uint32_t *tabs = reinterpret_cast<uint32_t *>(smem + kOffTabs);  // [kMaxParts][4]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t NB = a.NB;
-    const int32_t nwin = (int32_t)(NB * 16);
-    const int32_t ncols = a.ntiles <= 1 ? 128 : (a.ntiles == 2 ? 256 : 512);
-    pdl_launch_dependents();
+    const int64_t G = gridDim.x;
+    Range R;
+    R.init(blockIdx.x, G, a.W, a.nwin);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPfBStages; ++s) {
-            mbar_init(&b_full[s], 4);  // the four warps of the half that decodes the window
-            mbar_init(&b_empty[s], 1);
+        for (int s = 0; s < kPfStages; ++s) {
+            mbar_init(&x_full[s], 1);
+            mbar_init(&x_empty[s], 1);
+            mbar_init(&w_full[s], kPfDecWarps);
+            mbar_init(&w_empty[s], 1);
         }
-        for (int s = 0; s < kPfAStages; ++s) {
-            mbar_init(&a_full[s], 1);
-            mbar_init(&a_empty[s], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
         }
-        mbar_init(acc_done, 1);
+        mbar_init(drained, 1);
         mbar_fence_init();
     }
-    if (warp == kPfMmaWarp) {
+    if (warp == kPfProd && lane < kMaxParts * 4) tabs[lane] = (&a.tabs[0][0])[lane];
+    if (warp == kPfMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(ncols)
+                     "r"(2 * kAccCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -177,333 +348,463 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(PfArgs a) {
     __syncthreads();
     tmem_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int64_t NB = a.NB;
 
     if (warp < kPfDecWarps) {
         // ------------------------------------------------------ decode --
-        const int i = threadIdx.x & (kPfRows - 1);  // weight row of the CTA
-        const int half = threadIdx.x >> 7;          // windows w = half, half + 2, ...
-        const int64_t row = (int64_t)blockIdx.x * kPfRows + i;
-        const bool real = row < a.rows;
-        const int64_t tile16 = row / 16;
-        const uint32_t sw = (uint32_t)(i & 7);
+        const int r = warp * 16 + (lane >> 1);  // weight row of the tile
+        const int h = lane & 1;                 // weights [32h, 32h + 32) of each window
+        const uint32_t sw = (uint32_t)(r & 7);
+        const uint32_t rl0 = 2u, rh0 = 1u, rl1 = 0u, rh1 = 31u;  // quarters 2h (even) and 2h + 1 (odd)
         bool ok = true;
-        // the row's block of a block column: its literal plane, escape index,
-        // terminal stream, escape count and exponent tables
-        struct Hdr {
-            const uint8_t *lit;
-            const uint16_t *idx;
-            const uint8_t *term;
-            uint32_t th0, th1, tl0, tl1;
-            int nesc;
+        // the load cursor runs kAhead windows before the decode position
+        constexpr int kAhead = 2;
+        Cursor cl;
+        cl.begin(R, a.ntok);
+        int32_t seg_load = -1;     // segments the load cursor has entered
+        int64_t seg_t = -1;
+        int32_t seg_bc = -1;
+        uint2 dir_cur = make_uint2(0, 0), dir_next = make_uint2(0, 0);
+        bool has_next = false;
+        int64_t nxt_t = 0;
+        int32_t nxt_w = 0;
+        auto dir_load = [&](int64_t t, int32_t bc) -> uint2 {
+            const int64_t row = (t / a.ntok) * kPfRows + r;
+            if (row >= a.rows) return make_uint2(0, 0);
+            return __ldg(a.rowdir + row * NB + bc);
         };
-        auto load_hdr = [&](int64_t bc, Hdr &h) {
-            const uint8_t *base = a.data + (size_t)a.unit16[tile16 * NB + bc] * 16;
-            const RowEntry e = reinterpret_cast<const RowEntry *>(base)[row & 15];
-            const uint4 tab = *reinterpret_cast<const uint4 *>(base + kUnitRows * sizeof(RowEntry));
-            h.th0 = tab.x;
-            h.th1 = tab.y;
-            h.tl0 = tab.z;
-            h.tl1 = tab.w;
-            h.lit = base + (size_t)e.off16 * 16;
-            h.idx = reinterpret_cast<const uint16_t *>(h.lit + (((uint32_t)e.words * 4u + 15u) & ~15u));
-            h.term = h.lit + 1408;
-            h.nesc = e.nesc;
-        };
-        auto load_win = [&](const Hdr &h, int qb, uint4 (&L)[4], uint32_t (&c)[6]) {
-            const uint4 *lp = reinterpret_cast<const uint4 *>(h.lit + 64 * qb);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) L[j] = lp[j];
-            const uint32_t *cp = reinterpret_cast<const uint32_t *>(h.lit + 1024);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) c[j] = cp[4 * qb + j];
-            c[4] = cp[64 + 2 * qb];
-            c[5] = cp[64 + 2 * qb + 1];
-        };
-        // this thread's windows w = half, half + 2, ...: block column w / 16,
-        // quad w % 16
-        Hdr hc{}, hn{};
-        uint4 Ln[4] = {};
-        uint32_t cn[6] = {0, 0, 0, 0, 0, 0};
-        int cur = 0;
-        const int32_t wk0 = half;
-        // this thread's share of its row's staged escapes: entries
-        // [32 half, 32 half + 32) of a block column's list, prefetched a
-        // block column ahead and written at each block column's start
-        uint4 sh_idx[4] = {};
-        uint4 sh_term[2] = {};
-        auto load_share = [&](const Hdr &h) {
-            const uint4 *ip = reinterpret_cast<const uint4 *>(h.idx + 32 * half);
-            const uint4 *tp = reinterpret_cast<const uint4 *>(h.term + 32 * half);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) sh_idx[j] = ip[j];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) sh_term[j] = tp[j];
-        };
-        auto store_share = [&]() {
-            uint32_t *d = esc + i * kPfEsc + 32 * half;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const uint32_t iw = (&sh_idx[j >> 3].x)[(j >> 1) & 3];
-                const uint32_t tw = (&sh_term[j >> 4].x)[(j >> 2) & 3];
-                d[j] = ((iw >> (16 * (j & 1))) & 0xFFFFu) | (((tw >> (8 * (j & 3))) & 0xFFu) << 16);
+        // enter the load cursor's window: a new segment takes the prefetched
+        // directory entry, prefetches the next one and stages its terminals
+        auto load_window = [&](Win &wv) {
+            const int32_t bc = cl.w >> 4;
+            if (cl.t != seg_t || bc != seg_bc) {
+                if (has_next && nxt_t == cl.t && (nxt_w >> 4) == bc)
+                    dir_cur = dir_next;
+                else
+                    dir_cur = dir_load(cl.t, bc);
+                has_next = cl.next_segment(R, nxt_t, nxt_w);
+                if (has_next) dir_next = dir_load(nxt_t, nxt_w >> 4);
+                ++seg_load;
+                seg_t = cl.t;
+                seg_bc = bc;
+                const int64_t row = cl.rt * kPfRows + r;
+                uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
+                if (row < a.rows) {
+                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
+                    cp_async16(dst, src);
+                    cp_async16(dst + 16, src + 16);
+                }
+                cp_async_commit();
+            }
+            wv.real = cl.rt * kPfRows + r < a.rows;
+            wv.dir = dir_cur;
+            if (wv.real) {
+                const int q = cl.w & 15;
+                const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
+                const uint4 *lp = reinterpret_cast<const uint4 *>(lit + 64 * q + 32 * h);
+                wv.L0 = __ldg(lp);
+                wv.L1 = __ldg(lp + 1);
+                const uint32_t *cp = reinterpret_cast<const uint32_t *>(lit + 1024);
+                wv.c0 = __ldg(cp + 4 * q + 2 * h);
+                wv.c1 = __ldg(cp + 4 * q + 2 * h + 1);
+                wv.P = __ldg(cp + 64 + 2 * q + h);
             }
         };
-        auto decoders_sync = [&]() {
-            asm volatile("bar.sync 1, %0;" ::"r"(kPfDecWarps * 32) : "memory");
-        };
-        if (real) {
-            load_hdr(wk0 >> 4, hc);
-            load_hdr(((wk0 >> 4) + 1) % NB, hn);
-            load_win(hc, wk0 & 15, Ln, cn);
-            load_share(hc);
+        Win pf[kAhead];
+#pragma unroll
+        for (int i = 0; i < kAhead; ++i) {
+            pf[i].real = false;
+            pf[i].dir = make_uint2(0, 0);
+            if (!cl.done) {
+                load_window(pf[i]);
+                cl.next(R, a.ntok);
+            }
         }
-        store_share();
-        decoders_sync();
-        bool need_share = true;  // the next block column's share still to fetch
-        for (int32_t w = half; w < nwin; w += 2) {
-            const int s = w % kPfBStages, use = w / kPfBStages;
-            const int32_t wk = w;
-            const int qb = wk & 15;
-            uint4 L[4];
-            uint32_t cw[6];
+        int32_t seg_dec = -1;  // segment of the decode position
+        uint32_t run = 0;      // escapes of this row block before the current window
+        int32_t j = 0;  // window sequence number (its stage)
+        Cursor cd;
+        cd.begin(R, a.ntok);
+        int64_t dseg_t = -1;
+        int32_t dseg_bc = -1;
+        for (; !cd.done; cd.next(R, a.ntok), ++j) {
+            const Win cur = pf[0];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) L[j] = Ln[j];
-#pragma unroll
-            for (int j = 0; j < 6; ++j) cw[j] = cn[j];
-            // the next window of this thread: its bytes fetched now (from the
-            // next block column's row block when it starts one)
-            const int32_t wk2 = w + 2;
-            const bool more = wk2 < nwin;
-            const bool newblk = more && (wk2 >> 4) != (wk >> 4);
-            if (real && more) load_win(newblk ? hn : hc, wk2 & 15, Ln, cn);
-            if (need_share && !newblk) {  // the next block column's escapes, a block column early
-                if (real) load_share(hn);
-                need_share = false;
+            for (int i = 0; i + 1 < kAhead; ++i) pf[i] = pf[i + 1];
+            if (!cl.done) {
+                load_window(pf[kAhead - 1]);
+                cl.next(R, a.ntok);
+            } else {
+                pf[kAhead - 1].real = false;
             }
-            if (use > 0 && ok && !mbar_wait(&b_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
-            uint8_t *rowp = btile + s * kBTile + i * 128;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {  // 16 weights: quarter j of the quad
-                uint32_t xa, xb;
-                selectors16(cw[j], cw[4 + (j >> 1)], j, xa, xb);
-                uint32_t p[8];
-                // code 7 decodes to sign | exponent 0 | mantissa: the escape
-                // patch below only ORs the terminal exponent in
-                const uint32_t th1 = hc.th1 & 0x00FFFFFFu, tl1 = hc.tl1 & 0x00FFFFFFu;
-                dec4(L[j].x, xa, hc.th0, th1, hc.tl0, tl1, p[0], p[1]);
-                dec4(L[j].y, xa >> 16, hc.th0, th1, hc.tl0, tl1, p[2], p[3]);
-                dec4(L[j].z, xb, hc.th0, th1, hc.tl0, tl1, p[4], p[5]);
-                dec4(L[j].w, xb >> 16, hc.th0, th1, hc.tl0, tl1, p[6], p[7]);
-                if (!real) {
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) p[k] = 0u;
-                }
-                *reinterpret_cast<uint4 *>(rowp + (((2u * j) ^ sw) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
-                *reinterpret_cast<uint4 *>(rowp + (((2u * j + 1u) ^ sw) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
+            // the decode position's segment: its directory entry and terminals
+            const int32_t bc = cd.w >> 4;
+            if (cd.t != dseg_t || bc != dseg_bc) {
+                ++seg_dec;
+                dseg_t = cd.t;
+                dseg_bc = bc;
+                run = 0;
+                cp_async_wait(seg_load - seg_dec);
+                __syncwarp();
             }
-            // escapes of this window: the terminal exponent ORed in (the other
-            // half's windows' escapes are passed over); the staged list, then
-            // global memory past its kPfEsc entries
-            if (real) {
-                const uint32_t start = 64u * (uint32_t)qb, end = start + 64u;
-                const uint32_t *el = esc + i * kPfEsc;
-                const int lim = hc.nesc < kPfEsc ? hc.nesc : kPfEsc;
-                while (cur < lim) {
-                    const uint32_t e = el[cur];
-                    const uint32_t pos = e & 1023u;
-                    if (pos >= end) break;
-                    if (pos >= start) {
-                        const uint32_t k = pos - start;
-                        *reinterpret_cast<uint16_t *>(rowp + ((((k >> 3) ^ sw) << 4) | ((k & 7u) << 1))) |=
-                            (uint16_t)(((e >> 16) & 0xFFu) << 7);
-                    }
-                    ++cur;
-                }
-                if (cur >= kPfEsc)
-                    while (cur < hc.nesc) {
-                        const uint32_t pos = hc.idx[cur] & 1023u;
-                        if (pos >= end) break;
-                        if (pos >= start) {
-                            const uint32_t k = pos - start;
-                            *reinterpret_cast<uint16_t *>(rowp + ((((k >> 3) ^ sw) << 4) | ((k & 7u) << 1))) |=
-                                (uint16_t)((uint32_t)hc.term[cur] << 7);
+            const int s = j % kPfStages, use = j / kPfStages;
+            if (use > 0 && ok && !mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
+            uint8_t *rowp = ws + s * kWStage + r * 128;
+            const uint32_t part = cur.dir.y >> 16;
+            const uint32_t nesc = cur.dir.y & 0xFFFFu;
+            const uint32_t *tb = tabs + 4 * (part < kMaxParts ? part : 0);
+            // code 7 decodes to sign | exponent 0 | mantissa; the terminal
+            // exponent is ORed in below
+            const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
+            uint32_t p[16];
+            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+            if (cur.real) {
+                uint32_t s0, s1, s2, s3;
+                selectors16(cur.c0, cur.P, rl0, rh0, s0, s1);
+                selectors16(cur.c1, cur.P, rl1, rh1, s2, s3);
+                dec4(cur.L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(cur.L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(cur.L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(cur.L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                dec4(cur.L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
+                dec4(cur.L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
+                dec4(cur.L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
+                dec4(cur.L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
+                e0 = escape_nibbles(s0);
+                e1 = escape_nibbles(s1);
+                e2 = escape_nibbles(s2);
+                e3 = escape_nibbles(s3);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) p[k] = 0u;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
+                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
+            // escapes: rank among the row block's escapes -> terminal exponent
+            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            uint32_t rank = run + (h ? other : 0u);
+            run += mine + other;
+            if (mine) {
+                const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
+                    while (m) {
+                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
+                        m &= m - 1;
+                        uint16_t *wp = reinterpret_cast<uint16_t *>(
+                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
+                        if (rank < nesc) {
+                            const uint32_t ex = rank < (uint32_t)kTermRow
+                                                    ? ts[rank]
+                                                    : a.data[(size_t)cur.dir.x * 16 + 1408 + rank];
+                            *wp |= (uint16_t)(ex << 7);
+                        } else {
+                            *wp = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
                         }
-                        ++cur;
+                        ++rank;
                     }
+                }
             }
             fence_proxy_async_smem();  // these generic writes, before the tensor core's async reads
             __syncwarp();
-            if ((threadIdx.x & 31) == 0) mbar_arrive(&b_full[s]);
-            if (newblk) {  // this thread's next window starts a block column
-                decoders_sync();  // every decoder done with the staged escapes
-                store_share();
-                decoders_sync();
-                hc = hn;
-                cur = 0;
-                if (real) load_hdr(((wk2 >> 4) + 1) % NB, hn);
-                need_share = true;
-            }
+            if (lane == 0) mbar_arrive(&w_full[s]);
         }
+        cp_async_wait(0);
+    } else if (warp >= kPfEpi0 && warp < kPfEpi0 + 4) {
         // ---------------------------------------------------- epilogue --
-        // warps 0-3 (warp w reads tensor-memory lanes 32w .. 32w + 31)
-        if (warp < 4) {
-        if (ok && !mbar_wait(acc_done, 0u, a.err, kErrWaitFull)) ok = false;
-        tmem_fence_after();
-        for (int tt = 0; tt < a.ntiles; ++tt) {
-            const int tok = tt * kPfTok + warp * 32 + lane;
-            for (int c0 = 0; c0 < kPfRows; c0 += 32) {
-                uint32_t r[32];
-                tmem_load32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(tt * kPfRows + c0), r);
-                if (!ok || tok >= a.m) continue;
+        const int qtr = warp - kPfEpi0;  // tensor-memory lanes 32 qtr .. 32 qtr + 31
+        bool ok = true;
+        for (int32_t pi = 0; pi < R.n; ++pi) {
+            int64_t t;
+            int32_t w0, w1;
+            R.piece(pi, t, w0, w1);
+            const int b = pi & 1;
+            if (ok && !mbar_wait(&acc_full[b], (uint32_t)((pi >> 1) & 1), a.err, kErrWaitFull)) ok = false;
+            tmem_fence_after();
+            const bool whole = w0 == 0 && w1 == a.nwin;
+            const int64_t row = (t / a.ntok) * kPfRows + qtr * 32 + lane;
+            const int32_t tok0 = (int32_t)(t % a.ntok) * a.ntt;
+            const float bv = (a.bias && row < a.rows) ? bf16_bits_to_f32(a.bias[row]) : 0.f;
+            const int slot = t == R.tA ? 0 : 1;
+            float *mine = a.part + (((int64_t)blockIdx.x * 2 + slot) * kPfRows + qtr * 32 + lane) * a.ntt;
+            for (int32_t c0 = 0; c0 < a.ntt; c0 += 32) {
+                uint32_t v[32];
+                tmem_load32(tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(b * kAccCols + c0), v);
+                if (!ok) continue;
+                if (whole) {
+                    if (row < a.rows)
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int64_t orow = (int64_t)blockIdx.x * kPfRows + c0 + j;
-                    if (orow >= a.rows) break;
-                    float y = __uint_as_float(r[j]);
-                    if (a.bias) y += bf16_bits_to_f32(a.bias[orow]);
-                    if (a.out_f32)
-                        reinterpret_cast<float *>(a.out)[(int64_t)tok * a.rows + orow] = y;
-                    else
-                        reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + orow] = f32_to_bf16_bits(y);
+                        for (int k = 0; k < 32; ++k) {
+                            const int32_t tok = tok0 + c0 + k;
+                            if (tok >= a.M) break;
+                            const float y = __uint_as_float(v[k]) + bv;
+                            if (a.out_f32)
+                                reinterpret_cast<float *>(a.out)[(int64_t)tok * a.rows + row] = y;
+                            else
+                                reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
+                        }
+                } else {
+                    float4 *d = reinterpret_cast<float4 *>(mine + c0);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        __stcg(d + k, make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                                  __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3])));
                 }
             }
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+            if (whole || !ok) continue;
+            // a shared tile: the last of its pieces to arrive (per row quarter)
+            // adds every piece's partial in CTA order
+            const int64_t cf = owner_of(t * a.nwin, G, a.W), cl = owner_of(t * a.nwin + a.nwin - 1, G, a.W);
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + t * 4 + qtr), 1u);
+                last = old == (uint32_t)(cl - cf);
+                if (last) a.counters[t * 4 + qtr] = 0;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            for (int32_t c0 = 0; c0 < a.ntt; c0 += 32) {
+                float acc[32];
+                for (int64_t c = cf; c <= cl; ++c) {
+                    const int sc = t == cta_start(c, G, a.W) / a.nwin ? 0 : 1;
+                    const float4 *pp = reinterpret_cast<const float4 *>(
+                        a.part + ((c * 2 + sc) * kPfRows + qtr * 32 + lane) * a.ntt + c0);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float4 x = __ldcg(pp + k);
+                        if (c == cf) {
+                            acc[4 * k] = x.x;
+                            acc[4 * k + 1] = x.y;
+                            acc[4 * k + 2] = x.z;
+                            acc[4 * k + 3] = x.w;
+                        } else {
+                            acc[4 * k] += x.x;
+                            acc[4 * k + 1] += x.y;
+                            acc[4 * k + 2] += x.z;
+                            acc[4 * k + 3] += x.w;
+                        }
+                    }
+                }
+                if (row < a.rows)
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        const int32_t tok = tok0 + c0 + k;
+                        if (tok >= a.M) break;
+                        const float y = acc[k] + bv;
+                        if (a.out_f32)
+                            reinterpret_cast<float *>(a.out)[(int64_t)tok * a.rows + row] = y;
+                        else
+                            reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
+                    }
+            }
         }
-        tmem_fence_before();
-        }
-    } else if (warp == kPfActWarp) {
+    } else if (warp == kPfProd) {
         // -------------------------------------------------- activations --
         if (lane == 0) {
-            pdl_wait();  // the swizzled activations come from the kernel before this one
-            const uint32_t bytes = (uint32_t)a.ntiles * kATile;
+            const uint32_t bytes = (uint32_t)a.ntt * 128u;
             bool ok = true;
-            for (int32_t w = 0; w < nwin && ok; ++w) {
-                const int s = w % kPfAStages, use = w / kPfAStages;
-                if (use > 0 && !mbar_wait(&a_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
+            int32_t j = 0;
+            Cursor cu;
+            for (cu.begin(R, a.ntok); !cu.done && ok; cu.next(R, a.ntok), ++j) {
+                const int s = j % kPfStages, use = j / kPfStages;
+                if (use > 0 && !mbar_wait(&x_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
                 if (!ok) break;
-                mbar_arrive_expect_tx(&a_full[s], bytes);
-                bulk_g2s(atile + s * kPfMaxTiles * kATile, a.xs + (size_t)w * bytes, bytes, &a_full[s]);
+                mbar_arrive_expect_tx(&x_full[s], bytes);
+                tma_load_2d(xs + s * kXStage, &xmap, cu.w * 64, (int32_t)(cu.t - cu.rt * a.ntok) * a.ntt, &x_full[s]);
             }
+            // every copy issued lands before the CTA exits (the last use of
+            // each stage: its phase has completed, or completes now)
+            for (int32_t i = std::max<int32_t>(0, j - kPfStages); i < j; ++i)
+                mbar_wait(&x_full[i % kPfStages], (uint32_t)((i / kPfStages) & 1), a.err, kErrWaitDrain);
         }
     } else {
         // ---------------------------------------------------------- MMA --
         bool ok = true;
-        for (int32_t w = 0; w < nwin; ++w) {
-            const int sb = w % kPfBStages, sa = w % kPfAStages;
-            if (ok && !mbar_wait(&a_full[sa], (uint32_t)((w / kPfAStages) & 1), a.err, kErrWaitFull)) ok = false;
-            if (ok && !mbar_wait(&b_full[sb], (uint32_t)((w / kPfBStages) & 1), a.err, kErrWaitFull)) ok = false;
+        int32_t j = 0;
+        for (int32_t pi = 0; pi < R.n; ++pi) {
+            int64_t t;
+            int32_t w0, w1;
+            R.piece(pi, t, w0, w1);
+            const int b = pi & 1;
+            if (pi >= 2 && ok && !mbar_wait(&acc_empty[b], (uint32_t)(((pi >> 1) - 1) & 1), a.err, kErrWaitEmpty))
+                ok = false;
             tmem_fence_after();
-            if (lane == 0) {
-                if (ok) {
-                    const uint32_t bb = smem_addr(btile + sb * kBTile);
-                    const uint32_t ab = smem_addr(atile + sa * kPfMaxTiles * kATile);
+            for (int32_t w = w0; w < w1; ++w, ++j) {
+                const int s = j % kPfStages;
+                const uint32_t par = (uint32_t)((j / kPfStages) & 1);
+                if (ok && !mbar_wait(&x_full[s], par, a.err, kErrWaitFull)) ok = false;
+                if (ok && !mbar_wait(&w_full[s], par, a.err, kErrWaitFull)) ok = false;
+                tmem_fence_after();
+                if (lane == 0) {
+                    if (ok) {
+                        const uint32_t wb = smem_addr(ws + s * kWStage), xb = smem_addr(xs + s * kXStage);
 #pragma unroll
-                    for (int k = 0; k < kPfWin / 16; ++k)
-                        for (int tt = 0; tt < a.ntiles; ++tt)
-                            umma_bf16(tmem + (uint32_t)(tt * kPfRows), sw128_desc(ab + tt * kATile + 32 * k),
-                                      sw128_desc(bb + 32 * k), (w > 0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < 4; ++k)
+                            umma_bf16(tmem + (uint32_t)(b * kAccCols), sw128_desc(wb + 32 * k), sw128_desc(xb + 32 * k),
+                                      a.idesc, (w > w0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&w_empty[s]);  // frees the stages once these MMAs have read them
+                    umma_commit(&x_empty[s]);
                 }
-                umma_commit(&b_empty[sb]);  // frees the stages once these MMAs have read them
-                umma_commit(&a_empty[sa]);
+                __syncwarp();
             }
+            if (lane == 0) umma_commit(&acc_full[b]);
             __syncwarp();
         }
-        if (lane == 0) umma_commit(acc_done);
+        // every MMA issued has completed before the tensor memory is freed
+        if (lane == 0) umma_commit(drained);
         __syncwarp();
+        mbar_wait(drained, 0u, a.err, kErrWaitDrain);
     }
     // every warp: the epilogue's tensor-memory reads done before the free
+    tmem_fence_before();
     __syncthreads();
-    if (warp == kPfMmaWarp) {
+    if (warp == kPfMma) {
         tmem_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAccCols) : "memory");
     }
 }
 
-// X [m][C] bf16 (row stride ldx) -> window-major 128-byte-swizzled tiles
-// [C / 64][ntiles * 128][128 bytes]; rows past m are zero.
-__global__ void x_swizzle_kernel(const uint16_t *__restrict__ x, int64_t ldx, int32_t m, int32_t ntiles, int64_t C,
-                                 uint8_t *__restrict__ xs) {
-    const int64_t rows = (int64_t)ntiles * kPfTok;
-    const int64_t chunks = (C / 8) * rows;  // 16-byte chunks
-    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < chunks; q += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = q % rows, kc = q / rows;  // token row, 8-weight chunk of K
-        const int64_t w = kc >> 3, c = kc & 7;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < m) v = *reinterpret_cast<const uint4 *>(x + r * ldx + kc * 8);
-        *reinterpret_cast<uint4 *>(xs + (w * rows + r) * 128 + ((c ^ (r & 7)) << 4)) = v;
-    }
+// cuTensorMapEncodeTiled, from the driver through the runtime (no link-time
+// dependency on libcuda).
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled(std::string &msg) {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    if (!fn) msg = "dm_prefill: cuTensorMapEncodeTiled is not available from the driver";
+    return fn;
+}
+
+// The launch geometry of a prefill over M activation rows.
+struct PfPlan {
+    int32_t ntt, ntok;
+    int64_t nrt, ntiles, nwin, W, grid;
+    int64_t counter_bytes, part_bytes;
+};
+
+PfPlan plan_prefill(const dm_tensor *t, int64_t M) {
+    PfPlan P{};
+    P.ntt = (int32_t)std::min<int64_t>(kPfTokMax, (M + 31) / 32 * 32);  // whole 32-column tensor-memory loads
+    P.ntok = (int32_t)((M + P.ntt - 1) / P.ntt);
+    P.nrt = (t->L.rows + kPfRows - 1) / kPfRows;
+    P.ntiles = P.nrt * P.ntok;
+    P.nwin = t->L.NB * 16;
+    P.W = P.ntiles * P.nwin;
+    P.grid = std::min<int64_t>(t->sms, P.W);
+    P.counter_bytes = (P.ntiles * 4 * (int64_t)sizeof(int) + 255) / 256 * 256;
+    P.part_bytes = P.grid * 2 * kPfRows * P.ntt * (int64_t)sizeof(float);
+    return P;
 }
 
 }  // namespace
 
 int64_t prefill_workspace_bytes(const dm_tensor *t, int64_t M) {
-    const int64_t m = std::min<int64_t>(M, (int64_t)kPfMaxTiles * kPfTok);
-    const int64_t ntiles = (m + kPfTok - 1) / kPfTok;
-    return t->L.C * ntiles * kPfTok * 2;
+    const PfPlan P = plan_prefill(t, M);
+    return P.counter_bytes + P.part_bytes;
 }
 
 int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const uint16_t *bias, void *out,
                        int out_f32, uint8_t *work, int64_t work_bytes, void *stream, std::string &msg) {
     const TensorLayout &L = t->L;
-    if (!L.fast_sip) {
+    if (!L.fast_sip || !t->d_rowdir) {
         msg = "dm_prefill: needs a sip tensor (the fast path)";
         return DM_EINVAL;
     }
-    if (work_bytes < prefill_workspace_bytes(t, M) || (reinterpret_cast<uintptr_t>(work) & 15) ||
-        (reinterpret_cast<uintptr_t>(x) & 15)) {
-        msg = "dm_prefill: workspace too small or activations / workspace not 16-byte aligned";
+    if (L.nparts > kMaxParts) {
+        msg = "dm_prefill: a fused tensor of more than " + std::to_string(kMaxParts) + " parts";
         return DM_EINVAL;
     }
-    const int smem = kPfBStages * kBTile + kPfAStages * kPfMaxTiles * kATile + kPfRows * kPfEsc * 4 + 1024 + 256;
+    if (M > (int64_t)INT32_MAX / 2) {
+        msg = "dm_prefill: too many activation rows";
+        return DM_EINVAL;
+    }
+    if (work_bytes < prefill_workspace_bytes(t, M) || (reinterpret_cast<uintptr_t>(work) & 255) ||
+        (reinterpret_cast<uintptr_t>(x) & 15)) {
+        msg = "dm_prefill: workspace too small or not 256-byte aligned, or activations not 16-byte aligned";
+        return DM_EINVAL;
+    }
+    if (L.units == 0) return DM_OK;
+    const PfPlan P = plan_prefill(t, M);
+    EncodeTiled enc = encode_tiled(msg);
+    if (!enc) return DM_ECUDA;
+    CUtensorMap xmap;
+    const cuuint64_t gdim[2] = {(cuuint64_t)L.C, (cuuint64_t)M};
+    const cuuint64_t gstride[1] = {(cuuint64_t)L.C * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)P.ntt};
+    const cuuint32_t estride[2] = {1u, 1u};
+    CUresult cr = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), gdim, gstride, box, estride,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) {
+        msg = "dm_prefill: cuTensorMapEncodeTiled failed (" + std::to_string((int)cr) + ")";
+        return DM_ECUDA;
+    }
     // a per-device attribute: one bit per device (64 and up: every launch)
     static std::atomic<uint64_t> attr{0};
     const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
     if (!dev_bit || !(attr.load() & dev_bit)) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_sip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(prefill_sip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
         attr.fetch_or(dev_bit);
     }
-    const int64_t grid = (L.rows + kPfRows - 1) / kPfRows;
-    for (int64_t m0 = 0; m0 < M; m0 += (int64_t)kPfMaxTiles * kPfTok) {
-        const int32_t m = (int32_t)std::min<int64_t>(M - m0, (int64_t)kPfMaxTiles * kPfTok);
-        const int32_t ntiles = (m + kPfTok - 1) / kPfTok;
-        const int64_t chunks = (L.C / 8) * ntiles * kPfTok;
-        const int blocks = (int)std::min<int64_t>((chunks + 255) / 256, (int64_t)t->sms * 16);
-        x_swizzle_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(x + m0 * L.C, L.C, m, ntiles, L.C, work);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) {
-            msg = std::string("x_swizzle_kernel: ") + cudaGetErrorString(e);
-            return DM_ECUDA;
-        }
-        PfArgs a{};
-        a.data = t->d_data;
-        a.unit16 = t->d_unit16;
-        a.rows = L.rows;
-        a.NB = L.NB;
-        a.xs = work;
-        a.ntiles = ntiles;
-        a.m = m;
-        a.bias = bias;
-        a.out = reinterpret_cast<uint8_t *>(out) + (size_t)m0 * L.rows * (out_f32 ? 4 : 2);
-        a.out_f32 = out_f32;
-        a.err = t->S.err;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)grid);
-        cfg.blockDim = dim3(kPfThreads);
-        cfg.dynamicSmemBytes = (size_t)smem;
-        cfg.stream = (cudaStream_t)stream;
-        cudaLaunchAttribute attr1[1];
-        attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr1[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr1;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, prefill_sip_kernel, a);
-        if (e != cudaSuccess) {
-            msg = std::string("prefill_sip_kernel: ") + cudaGetErrorString(e);
-            return DM_ECUDA;
-        }
+    int *counters = reinterpret_cast<int *>(work);
+    cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)P.counter_bytes, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        msg = std::string("dm_prefill: cudaMemsetAsync: ") + cudaGetErrorString(e);
+        return DM_ECUDA;
+    }
+    PfArgs a{};
+    a.data = t->d_data;
+    a.rowdir = reinterpret_cast<const uint2 *>(t->d_rowdir);
+    a.rows = L.rows;
+    a.NB = L.NB;
+    a.M = (int32_t)M;
+    a.ntok = P.ntok;
+    a.ntt = P.ntt;
+    a.nparts = L.nparts;
+    a.ntiles = P.ntiles;
+    a.nwin = P.nwin;
+    a.W = P.W;
+    a.idesc = idesc_f16(kPfRows, P.ntt);
+    a.bias = bias;
+    a.out = out;
+    a.out_f32 = out_f32;
+    a.counters = counters;
+    a.part = reinterpret_cast<float *>(work + P.counter_bytes);
+    a.err = t->S.err;
+    for (int p = 0; p < kMaxParts; ++p)
+        for (int k = 0; k < 4; ++k) a.tabs[p][k] = L.part_tabs[p][k];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)P.grid);
+    cfg.blockDim = dim3(kPfThreads);
+    cfg.dynamicSmemBytes = (size_t)kSmemBytes;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelEx(&cfg, prefill_sip_kernel, xmap, a);
+    if (e != cudaSuccess) {
+        msg = std::string("prefill_sip_kernel: ") + cudaGetErrorString(e);
+        return DM_ECUDA;
     }
     return DM_OK;
 }

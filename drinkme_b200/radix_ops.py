@@ -156,6 +156,8 @@ def prefill(p: dict, x: torch.Tensor, bias, out_dtype=torch.bfloat16) -> torch.T
     x = _check_x(x.reshape(-1, h.info.C), h.info.C, dev)
     if x.dtype != torch.bfloat16:
         x = x.to(torch.bfloat16)
+    if x.data_ptr() % 16:
+        x = x.clone()  # the kernel's TMA reads the activations from a 16-byte aligned base
     if out_dtype not in _DT:
         raise TypeError(f"radix_ops: output dtype must be bf16 or fp32, not {out_dtype}")
     M = x.shape[0]

@@ -67,3 +67,45 @@ def test_prefill_config5_shapes():
         ref = torch.nn.functional.linear(x.to(DEV).float(), W.to(DEV).float())
         assert (y - ref).abs().max() / ref.abs().max() <= 1e-3
         _check(y[:64], x[:64], W)
+
+
+def test_prefill_escape_heavy_rows_and_fused_parts():
+    """Exponents spread far past the sip palette: most weights escape, so
+    ranks run past the 64 terminal bytes staged per row (the rest come from
+    HBM); a fused q|k|v-like tensor (three parts, three palettes) and a row
+    shard; activations off a 16-byte boundary."""
+    g = torch.Generator().manual_seed(71)
+    base = torch.randn(200, 2048, generator=g) * 0.02
+    wild = torch.rand(200, 2048, generator=g) < 0.15  # about 150 escapes per block
+    scale = torch.pow(2.0, torch.randint(-60, 60, (200, 2048), generator=g).float())
+    W = torch.where(wild, base * scale, base).to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, "sip")
+    assert p["codec"] == "radix"
+    rt = swap.to_device_radix(p, DEV)
+    x = torch.randn(70, 2048, generator=g).to(torch.bfloat16)
+    buf = torch.empty(70 * 2048 + 1, dtype=torch.bfloat16, device=DEV)
+    buf[1:] = x.reshape(-1).to(DEV)
+    y = radix_ops.prefill(rt, buf[1:].view(70, 2048), None, torch.float32)
+    _check(y, x, W)
+    Ws = [(torch.randn(r, 4096, generator=g) * s).to(torch.bfloat16) for r, s in ((256, 0.02), (64, 0.05), (64, 1.0))]
+    packs = [codec.pack_weight_radix(w, "sip") for w in Ws]
+    fused = swap.to_device_radix_fused(packs, DEV)
+    xf = torch.randn(40, 4096, generator=g).to(torch.bfloat16)
+    yf = radix_ops.prefill(fused, xf.to(DEV), None, torch.float32)
+    _check(yf, xf, torch.cat(Ws))
+    shard = swap.to_device_radix(packs[0], DEV, 64, 192)
+    _check(radix_ops.prefill(shard, xf.to(DEV), None, torch.float32), xf, Ws[0][64:192])
+    assert rt["rx_handle"].device_error() == 0 and fused["rx_handle"].device_error() == 0
+
+
+@pytest.mark.parametrize("M", [9, 96, 257, 1100])
+def test_prefill_token_tiles_and_stream_k_pieces(M):
+    """Activation-row counts that leave partial token tiles, several token
+    tiles and (on the 8B down shape) tiles shared by several CTAs."""
+    W, x, rt = _case(4096, 12288, M, seed=M)
+    y = radix_ops.prefill(rt, x.to(DEV), None, torch.float32)
+    ref = torch.nn.functional.linear(x.to(DEV).float(), W.to(DEV).float())
+    assert (y - ref).abs().max() / ref.abs().max() <= 1e-3
+    _check(y[: min(M, 24)], x[: min(M, 24)], W)
+    assert torch.equal(y, radix_ops.prefill(rt, x.to(DEV), None, torch.float32))
+    assert rt["rx_handle"].device_error() == 0
