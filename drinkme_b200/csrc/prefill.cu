@@ -444,6 +444,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 dseg_t = cd.t;
                 dseg_bc = bc;
                 run = 0;
+                // a piece that starts inside a block column: the escapes of
+                // the block's earlier windows come before this window's ranks
+                const int q0 = cd.w & 15;
+                if (q0 > 0) {
+                    uint32_t pre = 0;
+                    if (cur.real) {
+                        const uint32_t *cp =
+                            reinterpret_cast<const uint32_t *>(a.data + (size_t)cur.dir.x * 16 + 1024);
+                        for (int qq = 0; qq < q0; ++qq) {
+                            uint32_t s0, s1, s2, s3;
+                            const uint32_t P = __ldg(cp + 64 + 2 * qq + h);
+                            selectors16(__ldg(cp + 4 * qq + 2 * h), P, rl0, rh0, s0, s1);
+                            selectors16(__ldg(cp + 4 * qq + 2 * h + 1), P, rl1, rh1, s2, s3);
+                            pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
+                                   __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
+                        }
+                    }
+                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
+                }
                 cp_async_wait(seg_load - seg_dec);
                 __syncwarp();
             }
