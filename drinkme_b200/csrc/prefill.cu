@@ -22,21 +22,22 @@
 //     partial goes to the workspace, and for each quarter of the tile's rows
 //     the last piece to arrive (an acquire-release counter) adds every
 //     piece's partial in CTA order and writes the outputs.
-//   * Warps 0-7 decode: a lane pair per weight row, each lane 32 weights of a
-//     window, from the loader's code planes with the GEMV's byte-parallel
-//     table lookups (escaped weights come out as sign | 0 | mantissa), into
-//     the 128-byte-swizzled K-major tile the tensor core reads. An escaped
-//     weight's terminal exponent is its rank among the row block's escapes:
-//     the lane pair counts code-7 nibbles as it goes and ORs the exponent in
-//     from the row's terminal stream, staged per block column in shared
-//     memory by cp.async. Data for window j + 2 is loaded while window j is
-//     decoded; the row-block directory entry of the next block column one
-//     block column ahead.
-//   * Warp 12 loads each activation window with one TMA tensor copy (no
-//     multicast) in the same swizzled layout; warp 13 owns the tensor memory
+//   * Warps 0-15 decode: four lanes per weight row, lane t taking weights
+//     [16t, 16t + 16) of each window, from the loader's code planes with the
+//     GEMV's byte-parallel table lookups (escaped weights come out as sign |
+//     0 | mantissa), into the 128-byte-swizzled K-major tile the tensor core
+//     reads. An escaped weight's terminal exponent is its rank among the row
+//     block's escapes: the row's lanes count code-7 nibbles as they go (a
+//     4-lane prefix sum) and OR the exponent in from the row's terminal
+//     stream, staged per block column in shared memory by cp.async. Each
+//     lane keeps the operands of the next four windows in flight, in
+//     register sets of an unrolled loop, and the row-block directory entry
+//     of the next block column.
+//   * Warp 20 loads each activation window with one TMA tensor copy (no
+//     multicast) in the same swizzled layout; warp 21 owns the tensor memory
 //     and one of its lanes issues the MMAs (kind::f16, M = 128, N = tokens,
 //     K = 16) and commits each window to the barriers that free its stages.
-//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
+//   * Warps 16-19 read the accumulators (tcgen05.ld, a lane per weight row),
 //     add the bias in fp32, round once and store; or write a piece's partial.
 //   * Every wait is bounded (the device error word records a wait that gave
 //     up); the tensor memory is freed on every path.
@@ -58,11 +59,12 @@ namespace {
 constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
 constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
 constexpr int kPfStages = 4;      // windows in flight (both operands)
-constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
-constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
-constexpr int kPfProd = 12;       // warp 12: activation TMA
-constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
-constexpr int kPfThreads = 14 * 32;
+constexpr int kPfDecWarps = 16;   // four lanes per weight row, 8 rows per warp
+constexpr int kPfEpi0 = 16;       // warps 16-19: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kPfProd = 20;       // warp 20: activation TMA
+constexpr int kPfMma = 21;        // warp 21: tensor memory and MMA issue
+constexpr int kPfThreads = 22 * 32;
+constexpr int kAhead = 4;         // windows of weight operands in flight per decoding lane
 constexpr int kWStage = kPfRows * 128;    // 16 KB: 128 rows x 64 bf16
 constexpr int kXStage = kPfTokMax * 128;  // 32 KB: 256 rows x 64 bf16
 constexpr int kTermRing = 4;              // block columns of staged terminal bytes
@@ -181,7 +183,8 @@ struct PfArgs {
     int64_t rows, NB;
     int32_t M, ntok, ntt;    // real activation rows, activation tiles, activation rows per tile (MMA N)
     int32_t nparts;
-    int64_t ntiles, nwin, W; // tiles (row tiles x activation tiles), windows per tile, all windows
+    int64_t ntiles, W;       // tiles (row tiles x activation tiles), all windows
+    int32_t nwin;            // windows per tile
     uint32_t idesc;
     const uint16_t *bias;
     void *out;               // [M][rows]
@@ -196,10 +199,11 @@ struct PfArgs {
 // its first tile when partial, its last tile when partial, then its whole
 // tiles in order.
 struct Range {
-    int64_t x0, x1, tA, tB, nwin;
+    int64_t x0, x1;
+    int32_t tA, tB, nwin;
     bool pA, pB;
     int32_t n;
-    __device__ void init(int64_t c, int64_t G, int64_t W, int64_t nw) {
+    __device__ void init(int64_t c, int64_t G, int64_t W, int32_t nw) {
         nwin = nw;
         x0 = c * W / G;
         x1 = (c + 1) * W / G;
@@ -207,28 +211,28 @@ struct Range {
         pA = pB = false;
         tA = tB = 0;
         if (x1 <= x0) return;
-        tA = x0 / nwin;
-        tB = (x1 - 1) / nwin;
+        tA = (int32_t)(x0 / nwin);
+        tB = (int32_t)((x1 - 1) / nwin);
         if (tA == tB) {
             n = 1;
             return;
         }
         pA = x0 % nwin != 0;
         pB = x1 % nwin != 0;
-        n = (pA ? 1 : 0) + (pB ? 1 : 0) + (int32_t)((pB ? tB : tB + 1) - (pA ? tA + 1 : tA));
+        n = (pA ? 1 : 0) + (pB ? 1 : 0) + ((pB ? tB : tB + 1) - (pA ? tA + 1 : tA));
     }
-    __device__ void piece(int32_t i, int64_t &t, int32_t &w0, int32_t &w1) const {
+    __device__ void piece(int32_t i, int32_t &t, int32_t &w0, int32_t &w1) const {
         if (tA == tB) {
             t = tA;
-            w0 = (int32_t)(x0 - tA * nwin);
-            w1 = (int32_t)(x1 - tA * nwin);
+            w0 = (int32_t)(x0 - (int64_t)tA * nwin);
+            w1 = (int32_t)(x1 - (int64_t)tA * nwin);
             return;
         }
         if (pA) {
             if (i == 0) {
                 t = tA;
-                w0 = (int32_t)(x0 - tA * nwin);
-                w1 = (int32_t)nwin;
+                w0 = (int32_t)(x0 - (int64_t)tA * nwin);
+                w1 = nwin;
                 return;
             }
             --i;
@@ -237,14 +241,14 @@ struct Range {
             if (i == 0) {
                 t = tB;
                 w0 = 0;
-                w1 = (int32_t)(x1 - tB * nwin);
+                w1 = (int32_t)(x1 - (int64_t)tB * nwin);
                 return;
             }
             --i;
         }
         t = (pA ? tA + 1 : tA) + i;
         w0 = 0;
-        w1 = (int32_t)nwin;
+        w1 = nwin;
     }
 };
 
@@ -258,20 +262,20 @@ __device__ __forceinline__ int64_t owner_of(int64_t x, int64_t G, int64_t W) {
     return c;
 }
 
-// A position in the CTA's window sequence: piece pi, window w of tile t.
+// A position in the CTA's window sequence: piece pi, window w of tile t
+// (weight row tile rt).
 struct Cursor {
-    int32_t pi, w, w1;
-    int64_t t, rt;  // tile, its weight row tile (t / ntok)
+    int32_t pi, w, w1, t, rt;
     bool done;
+    __device__ void at_piece(const Range &R, int32_t ntok) {
+        R.piece(pi, t, w, w1);
+        rt = t / ntok;
+    }
     __device__ void begin(const Range &R, int32_t ntok) {
         pi = 0;
         done = R.n == 0;
-        t = rt = 0;
-        w = w1 = 0;
-        if (!done) {
-            R.piece(0, t, w, w1);
-            rt = t / ntok;
-        }
+        t = rt = w = w1 = 0;
+        if (!done) at_piece(R, ntok);
     }
     __device__ void next(const Range &R, int32_t ntok) {
         if (++w < w1) return;
@@ -279,31 +283,30 @@ struct Cursor {
             done = true;
             return;
         }
-        R.piece(pi, t, w, w1);
-        rt = t / ntok;
+        at_piece(R, ntok);
     }
-    // the first window of the next block column (segment) after this one
-    __device__ bool next_segment(const Range &R, int64_t &t2, int32_t &w2) const {
+    // the first window (and its weight row tile) of the next block column
+    // (segment) after this one
+    __device__ bool next_segment(const Range &R, int32_t ntok, int32_t &rt2, int32_t &w2) const {
         const int32_t e = ((w >> 4) + 1) << 4;
         if (e < w1) {
-            t2 = t;
+            rt2 = rt;
             w2 = e;
             return true;
         }
         if (pi + 1 >= R.n) return false;
-        int32_t x;
+        int32_t t2, x;
         R.piece(pi + 1, t2, w2, x);
+        rt2 = t2 / ntok;
         return true;
     }
 };
 
-// A window's loaded operands for one lane: 32 literal bytes, two code-plane
-// words and the bit-2 word, and where they came from.
+// A window's loaded operands for one lane: 16 literal bytes, the code-plane
+// word and the bit-2 word.
 struct Win {
-    uint4 L0, L1;
-    uint32_t c0, c1, P;
-    uint2 dir;    // the row block's directory entry
-    bool real;
+    uint4 L;         // 16 literal bytes
+    uint32_t c, P;   // the low-two-bit code word and the bit-2 word
 };
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid_constant__ CUtensorMap xmap, PfArgs a) {
@@ -352,69 +355,66 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
 
     if (warp < kPfDecWarps) {
         // ------------------------------------------------------ decode --
-        const int r = warp * 16 + (lane >> 1);  // weight row of the tile
-        const int h = lane & 1;                 // weights [32h, 32h + 32) of each window
+        // four lanes per weight row; lane t decodes weights [16t, 16t + 16)
+        // of every window (the GEMV's quarter t of a quad)
+        const int r = warp * 8 + (lane >> 2);
+        const int t = lane & 3;
         const uint32_t sw = (uint32_t)(r & 7);
-        const uint32_t rl0 = 2u, rh0 = 1u, rl1 = 0u, rh1 = 31u;  // quarters 2h (even) and 2h + 1 (odd)
+        const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         bool ok = true;
-        // the load cursor runs kAhead windows before the decode position
-        constexpr int kAhead = 2;
+        // the load cursor runs kAhead windows before the decode position;
+        // window i's operands live in register set i mod kAhead (the loop
+        // is unrolled by kAhead, so no register is moved while its load is
+        // in flight)
         Cursor cl;
         cl.begin(R, a.ntok);
-        int32_t seg_load = -1;     // segments the load cursor has entered
-        int64_t seg_t = -1;
-        int32_t seg_bc = -1;
+        // segments the load cursor has entered; the ring of staged terminal
+        // bytes has kTermRing slots, and the load cursor is at most three
+        // segment starts ahead of the decode position (within kAhead = 4
+        // windows: a piece start, the next piece's start, one block column
+        // boundary), so no slot is overwritten while in use
+        int32_t seg_load = -1;
+        int32_t seg_t = -1, seg_bc = -1;
         uint2 dir_cur = make_uint2(0, 0), dir_next = make_uint2(0, 0);
         bool has_next = false;
-        int64_t nxt_t = 0;
-        int32_t nxt_w = 0;
-        auto dir_load = [&](int64_t t, int32_t bc) -> uint2 {
-            const int64_t row = (t / a.ntok) * kPfRows + r;
+        int32_t nxt_rt = 0, nxt_w = 0;
+        auto dir_load = [&](int32_t rt, int32_t bc) -> uint2 {
+            const int64_t row = (int64_t)rt * kPfRows + r;
             if (row >= a.rows) return make_uint2(0, 0);
             return __ldg(a.rowdir + row * NB + bc);
         };
-        // enter the load cursor's window: a new segment takes the prefetched
-        // directory entry, prefetches the next one and stages its terminals
+        // the load cursor's window into `wv`: a new segment takes the
+        // prefetched directory entry, prefetches the next one and stages its
+        // terminal bytes (lane t: bytes [16t, 16t + 16))
         auto load_window = [&](Win &wv) {
             const int32_t bc = cl.w >> 4;
             if (cl.t != seg_t || bc != seg_bc) {
-                if (has_next && nxt_t == cl.t && (nxt_w >> 4) == bc)
+                if (has_next && nxt_rt == cl.rt && (nxt_w >> 4) == bc)
                     dir_cur = dir_next;
                 else
-                    dir_cur = dir_load(cl.t, bc);
-                has_next = cl.next_segment(R, nxt_t, nxt_w);
-                if (has_next) dir_next = dir_load(nxt_t, nxt_w >> 4);
+                    dir_cur = dir_load(cl.rt, bc);
+                has_next = cl.next_segment(R, a.ntok, nxt_rt, nxt_w);
+                if (has_next) dir_next = dir_load(nxt_rt, nxt_w >> 4);
                 ++seg_load;
                 seg_t = cl.t;
                 seg_bc = bc;
-                const int64_t row = cl.rt * kPfRows + r;
-                uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
-                if (row < a.rows) {
-                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
-                    cp_async16(dst, src);
-                    cp_async16(dst + 16, src + 16);
-                }
+                if (cl.rt * kPfRows + r < a.rows)
+                    cp_async16(term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 16 * t,
+                               a.data + (size_t)dir_cur.x * 16 + 1408 + 16 * t);
                 cp_async_commit();
             }
-            wv.real = cl.rt * kPfRows + r < a.rows;
-            wv.dir = dir_cur;
-            if (wv.real) {
+            if (cl.rt * kPfRows + r < a.rows) {
                 const int q = cl.w & 15;
                 const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
-                const uint4 *lp = reinterpret_cast<const uint4 *>(lit + 64 * q + 32 * h);
-                wv.L0 = __ldg(lp);
-                wv.L1 = __ldg(lp + 1);
+                wv.L = __ldg(reinterpret_cast<const uint4 *>(lit + 64 * q + 16 * t));
                 const uint32_t *cp = reinterpret_cast<const uint32_t *>(lit + 1024);
-                wv.c0 = __ldg(cp + 4 * q + 2 * h);
-                wv.c1 = __ldg(cp + 4 * q + 2 * h + 1);
-                wv.P = __ldg(cp + 64 + 2 * q + h);
+                wv.c = __ldg(cp + 4 * q + t);
+                wv.P = __ldg(cp + 64 + 2 * q + (t >> 1));
             }
         };
         Win pf[kAhead];
 #pragma unroll
         for (int i = 0; i < kAhead; ++i) {
-            pf[i].real = false;
-            pf[i].dir = make_uint2(0, 0);
             if (!cl.done) {
                 load_window(pf[i]);
                 cl.next(R, a.ntok);
@@ -422,46 +422,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         }
         int32_t seg_dec = -1;  // segment of the decode position
         uint32_t run = 0;      // escapes of this row block before the current window
-        int32_t j = 0;  // window sequence number (its stage)
+        int32_t j = 0;         // window sequence number (its stage)
         Cursor cd;
         cd.begin(R, a.ntok);
-        int64_t dseg_t = -1;
-        int32_t dseg_bc = -1;
-        for (; !cd.done; cd.next(R, a.ntok), ++j) {
-            const Win cur = pf[0];
-#pragma unroll
-            for (int i = 0; i + 1 < kAhead; ++i) pf[i] = pf[i + 1];
-            if (!cl.done) {
-                load_window(pf[kAhead - 1]);
-                cl.next(R, a.ntok);
-            } else {
-                pf[kAhead - 1].real = false;
-            }
-            // the decode position's segment: its directory entry and terminals
+        int32_t dseg_t = -1, dseg_bc = -1;
+        uint2 dir = make_uint2(0, 0);  // the decode position's row block: stream offset, nesc | part << 16
+        bool real = false;             // its row exists
+        // decode the window in `cur`, then load the window kAhead ahead into it
+        auto step = [&](Win &cur) {
             const int32_t bc = cd.w >> 4;
             if (cd.t != dseg_t || bc != dseg_bc) {
                 ++seg_dec;
                 dseg_t = cd.t;
                 dseg_bc = bc;
                 run = 0;
+                real = (int64_t)cd.rt * kPfRows + r < a.rows;
+                dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
                 // a piece that starts inside a block column: the escapes of
                 // the block's earlier windows come before this window's ranks
                 const int q0 = cd.w & 15;
                 if (q0 > 0) {
                     uint32_t pre = 0;
-                    if (cur.real) {
-                        const uint32_t *cp =
-                            reinterpret_cast<const uint32_t *>(a.data + (size_t)cur.dir.x * 16 + 1024);
+                    if (real) {
+                        const uint32_t *cp = reinterpret_cast<const uint32_t *>(a.data + (size_t)dir.x * 16 + 1024);
                         for (int qq = 0; qq < q0; ++qq) {
-                            uint32_t s0, s1, s2, s3;
-                            const uint32_t P = __ldg(cp + 64 + 2 * qq + h);
-                            selectors16(__ldg(cp + 4 * qq + 2 * h), P, rl0, rh0, s0, s1);
-                            selectors16(__ldg(cp + 4 * qq + 2 * h + 1), P, rl1, rh1, s2, s3);
-                            pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
-                                   __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
+                            uint32_t s0, s1;
+                            selectors16(__ldg(cp + 4 * qq + t), __ldg(cp + 64 + 2 * qq + (t >> 1)), rl, rh, s0, s1);
+                            pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1));
                         }
                     }
-                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 1);
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 2);
+                    run = pre;
                 }
                 cp_async_wait(seg_load - seg_dec);
                 __syncwarp();
@@ -469,57 +461,53 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             const int s = j % kPfStages, use = j / kPfStages;
             if (use > 0 && ok && !mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
             uint8_t *rowp = ws + s * kWStage + r * 128;
-            const uint32_t part = cur.dir.y >> 16;
-            const uint32_t nesc = cur.dir.y & 0xFFFFu;
+            const uint32_t part = dir.y >> 16;
+            const uint32_t nesc = dir.y & 0xFFFFu;
             const uint32_t *tb = tabs + 4 * (part < kMaxParts ? part : 0);
             // code 7 decodes to sign | exponent 0 | mantissa; the terminal
             // exponent is ORed in below
             const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
-            uint32_t p[16];
-            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
-            if (cur.real) {
-                uint32_t s0, s1, s2, s3;
-                selectors16(cur.c0, cur.P, rl0, rh0, s0, s1);
-                selectors16(cur.c1, cur.P, rl1, rh1, s2, s3);
-                dec4(cur.L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(cur.L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(cur.L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(cur.L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
-                dec4(cur.L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
-                dec4(cur.L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
-                dec4(cur.L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
-                dec4(cur.L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
+            uint32_t p[8];
+            uint32_t e0 = 0, e1 = 0;
+            if (real) {
+                uint32_t s0, s1;
+                selectors16(cur.c, cur.P, rl, rh, s0, s1);
+                dec4(cur.L.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(cur.L.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(cur.L.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(cur.L.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
                 e0 = escape_nibbles(s0);
                 e1 = escape_nibbles(s1);
-                e2 = escape_nibbles(s2);
-                e3 = escape_nibbles(s3);
             } else {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) p[k] = 0u;
+                for (int k = 0; k < 8; ++k) p[k] = 0u;
             }
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
-                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
+            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t)) ^ sw) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t + 1)) ^ sw) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
             // escapes: rank among the row block's escapes -> terminal exponent
-            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-            uint32_t rank = run + (h ? other : 0u);
-            run += mine + other;
+            const uint32_t mine = __popc(e0) + __popc(e1);
+            uint32_t incl = mine;
+            uint32_t v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
+            if (t >= 1) incl += v;
+            v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
+            if (t >= 2) incl += v;
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 3, 4);
+            uint32_t rank = run + incl - mine;
+            run += total;
             if (mine) {
                 const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
+                for (int g = 0; g < 2; ++g) {
+                    uint32_t m = g == 0 ? e0 : e1;
                     while (m) {
-                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
+                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 16
                         m &= m - 1;
                         uint16_t *wp = reinterpret_cast<uint16_t *>(
-                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
+                            rowp + (((((uint32_t)(2 * t) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
                         if (rank < nesc) {
                             const uint32_t ex = rank < (uint32_t)kTermRow
                                                     ? ts[rank]
-                                                    : a.data[(size_t)cur.dir.x * 16 + 1408 + rank];
+                                                    : a.data[(size_t)dir.x * 16 + 1408 + rank];
                             *wp |= (uint16_t)(ex << 7);
                         } else {
                             *wp = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
@@ -531,6 +519,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             fence_proxy_async_smem();  // these generic writes, before the tensor core's async reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_full[s]);
+            // this register set's next window
+            if (!cl.done) {
+                load_window(cur);
+                cl.next(R, a.ntok);
+            }
+            cd.next(R, a.ntok);
+            ++j;
+        };
+        while (!cd.done) {
+#pragma unroll
+            for (int i = 0; i < kAhead; ++i)
+                if (!cd.done) step(pf[i]);
         }
         cp_async_wait(0);
     } else if (warp >= kPfEpi0 && warp < kPfEpi0 + 4) {
@@ -538,15 +538,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         const int qtr = warp - kPfEpi0;  // tensor-memory lanes 32 qtr .. 32 qtr + 31
         bool ok = true;
         for (int32_t pi = 0; pi < R.n; ++pi) {
-            int64_t t;
-            int32_t w0, w1;
+            int32_t t, w0, w1;
             R.piece(pi, t, w0, w1);
             const int b = pi & 1;
             if (ok && !mbar_wait(&acc_full[b], (uint32_t)((pi >> 1) & 1), a.err, kErrWaitFull)) ok = false;
             tmem_fence_after();
             const bool whole = w0 == 0 && w1 == a.nwin;
-            const int64_t row = (t / a.ntok) * kPfRows + qtr * 32 + lane;
-            const int32_t tok0 = (int32_t)(t % a.ntok) * a.ntt;
+            const int64_t row = (int64_t)(t / a.ntok) * kPfRows + qtr * 32 + lane;
+            const int32_t tok0 = (t % a.ntok) * a.ntt;
             const float bv = (a.bias && row < a.rows) ? bf16_bits_to_f32(a.bias[row]) : 0.f;
             const int slot = t == R.tA ? 0 : 1;
             float *mine = a.part + (((int64_t)blockIdx.x * 2 + slot) * kPfRows + qtr * 32 + lane) * a.ntt;
@@ -580,7 +579,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             if (whole || !ok) continue;
             // a shared tile: the last of its pieces to arrive (per row quarter)
             // adds every piece's partial in CTA order
-            const int64_t cf = owner_of(t * a.nwin, G, a.W), cl = owner_of(t * a.nwin + a.nwin - 1, G, a.W);
+            const int64_t tw = (int64_t)t * a.nwin;
+            const int64_t cf = owner_of(tw, G, a.W), cl = owner_of(tw + a.nwin - 1, G, a.W);
             __syncwarp();
             int last = 0;
             if (lane == 0) {
@@ -590,14 +590,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             }
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
-            for (int32_t c0 = 0; c0 < a.ntt; c0 += 32) {
-                float acc[32];
+            for (int32_t c0 = 0; c0 < a.ntt; c0 += 16) {
+                float acc[16];
                 for (int64_t c = cf; c <= cl; ++c) {
                     const int sc = t == cta_start(c, G, a.W) / a.nwin ? 0 : 1;
                     const float4 *pp = reinterpret_cast<const float4 *>(
                         a.part + ((c * 2 + sc) * kPfRows + qtr * 32 + lane) * a.ntt + c0);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
+                    for (int k = 0; k < 4; ++k) {
                         const float4 x = __ldcg(pp + k);
                         if (c == cf) {
                             acc[4 * k] = x.x;
@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 }
                 if (row < a.rows)
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) {
+                    for (int k = 0; k < 16; ++k) {
                         const int32_t tok = tok0 + c0 + k;
                         if (tok >= a.M) break;
                         const float y = acc[k] + bv;
@@ -637,7 +637,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 if (use > 0 && !mbar_wait(&x_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
                 if (!ok) break;
                 mbar_arrive_expect_tx(&x_full[s], bytes);
-                tma_load_2d(xs + s * kXStage, &xmap, cu.w * 64, (int32_t)(cu.t - cu.rt * a.ntok) * a.ntt, &x_full[s]);
+                tma_load_2d(xs + s * kXStage, &xmap, cu.w * 64, (cu.t - cu.rt * a.ntok) * a.ntt, &x_full[s]);
             }
             // every copy issued lands before the CTA exits (the last use of
             // each stage: its phase has completed, or completes now)
@@ -649,8 +649,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         bool ok = true;
         int32_t j = 0;
         for (int32_t pi = 0; pi < R.n; ++pi) {
-            int64_t t;
-            int32_t w0, w1;
+            int32_t t, w0, w1;
             R.piece(pi, t, w0, w1);
             const int b = pi & 1;
             if (pi >= 2 && ok && !mbar_wait(&acc_empty[b], (uint32_t)(((pi >> 1) - 1) & 1), a.err, kErrWaitEmpty))
@@ -803,7 +802,7 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
     a.ntt = P.ntt;
     a.nparts = L.nparts;
     a.ntiles = P.ntiles;
-    a.nwin = P.nwin;
+    a.nwin = (int32_t)P.nwin;
     a.W = P.W;
     a.idesc = idesc_f16(kPfRows, P.ntt);
     a.bias = bias;
