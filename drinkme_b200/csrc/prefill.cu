@@ -22,23 +22,23 @@
 //     partial goes to the workspace, and for each quarter of the tile's rows
 //     the last piece to arrive (an acquire-release counter) adds every
 //     piece's partial in CTA order and writes the outputs.
-//   * Warps 0-15 decode: four lanes per weight row, lane t taking weights
-//     [16t, 16t + 16) of each window, from the loader's code planes with the
+//   * Warps 0-7 decode: a lane pair per weight row, lane h taking weights
+//     [32h, 32h + 32) of each window, from the loader's code planes with the
 //     GEMV's byte-parallel table lookups (escaped weights come out as sign |
 //     0 | mantissa), into the 128-byte-swizzled K-major tile the tensor core
 //     reads. An escaped weight's terminal exponent is its rank among the row
-//     block's escapes: the row's lanes count code-7 nibbles as they go (a
-//     4-lane prefix sum) and OR the exponent in from the row's terminal
-//     stream, staged per block column in shared memory by cp.async. Each
-//     lane keeps the operands of the next four windows in flight, in
-//     register sets of an unrolled loop, and the row-block directory entry
-//     of the next block column.
-//   * Warp 20 loads each activation window with one TMA tensor copy (no
-//     multicast) in the same swizzled layout; warp 21 owns the tensor memory
+//     block's escapes: the lane pair counts code-7 nibbles as it goes and ORs
+//     the exponent in from the row's terminal stream, staged per block
+//     column in shared memory by cp.async. Each lane keeps the operands of
+//     the next four windows in flight, in register sets of an unrolled loop,
+//     and the row-block directory entry of the next block column.
+//   * Warp 12 loads each activation window with one TMA tensor copy (no
+//     multicast) in the same swizzled layout; warp 13 owns the tensor memory
 //     and one of its lanes issues the MMAs (kind::f16, M = 128, N = tokens,
 //     K = 16) and commits each window to the barriers that free its stages.
-//   * Warps 16-19 read the accumulators (tcgen05.ld, a lane per weight row),
-//     add the bias in fp32, round once and store; or write a piece's partial.
+//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
+//     add the bias in fp32, round once and store; or write a piece's partial
+//     (activation-row major, so a warp's store is one 128-byte line).
 //   * Every wait is bounded (the device error word records a wait that gave
 //     up); the tensor memory is freed on every path.
 #include <cuda.h>
@@ -59,11 +59,11 @@ namespace {
 constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
 constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
 constexpr int kPfStages = 4;      // windows in flight (both operands)
-constexpr int kPfDecWarps = 16;   // four lanes per weight row, 8 rows per warp
-constexpr int kPfEpi0 = 16;       // warps 16-19: the epilogue (tensor-memory lane quarters 0-3)
-constexpr int kPfProd = 20;       // warp 20: activation TMA
-constexpr int kPfMma = 21;        // warp 21: tensor memory and MMA issue
-constexpr int kPfThreads = 22 * 32;
+constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
+constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kPfProd = 12;       // warp 12: activation TMA
+constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
+constexpr int kPfThreads = 14 * 32;
 constexpr int kAhead = 4;         // windows of weight operands in flight per decoding lane
 constexpr int kWStage = kPfRows * 128;    // 16 KB: 128 rows x 64 bf16
 constexpr int kXStage = kPfTokMax * 128;  // 32 KB: 256 rows x 64 bf16
@@ -302,11 +302,12 @@ struct Cursor {
     }
 };
 
-// A window's loaded operands for one lane: 16 literal bytes, the code-plane
-// word and the bit-2 word.
+// A window's loaded operands for one lane: 32 literal bytes, two code-plane
+// words and the bit-2 word.
 struct Win {
-    uint4 L;         // 16 literal bytes
-    uint32_t c, P;   // the low-two-bit code word and the bit-2 word
+    uint4 L0, L1;    // 32 literal bytes
+    uint2 c;         // the two low-two-bit code words
+    uint32_t P;      // the bit-2 word
 };
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid_constant__ CUtensorMap xmap, PfArgs a) {
@@ -355,17 +356,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
 
     if (warp < kPfDecWarps) {
         // ------------------------------------------------------ decode --
-        // four lanes per weight row; lane t decodes weights [16t, 16t + 16)
-        // of every window (the GEMV's quarter t of a quad)
-        const int r = warp * 8 + (lane >> 2);
-        const int t = lane & 3;
+        // a lane pair per weight row; lane h decodes weights [32h, 32h + 32)
+        // of every window (the GEMV's quarters 2h and 2h + 1 of a quad)
+        const int r = warp * 16 + (lane >> 1);
+        const int h = lane & 1;
         const uint32_t sw = (uint32_t)(r & 7);
-        const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         bool ok = true;
         // the load cursor runs kAhead windows before the decode position;
-        // window i's operands live in register set i mod kAhead (the loop
-        // is unrolled by kAhead, so no register is moved while its load is
-        // in flight)
+        // window i's operands live in register set i mod kAhead (the loop is
+        // unrolled by kAhead, so no register is moved while its load is in
+        // flight)
         Cursor cl;
         cl.begin(R, a.ntok);
         // segments the load cursor has entered; the ring of staged terminal
@@ -385,9 +385,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         };
         // the load cursor's window into `wv`: a new segment takes the
         // prefetched directory entry, prefetches the next one and stages its
-        // terminal bytes (lane t: bytes [16t, 16t + 16))
+        // terminal bytes (lane h: bytes [32h, 32h + 32))
         auto load_window = [&](Win &wv) {
             const int32_t bc = cl.w >> 4;
+            const bool exists = (int64_t)cl.rt * kPfRows + r < a.rows;
             if (cl.t != seg_t || bc != seg_bc) {
                 if (has_next && nxt_rt == cl.rt && (nxt_w >> 4) == bc)
                     dir_cur = dir_next;
@@ -398,18 +399,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 ++seg_load;
                 seg_t = cl.t;
                 seg_bc = bc;
-                if (cl.rt * kPfRows + r < a.rows)
-                    cp_async16(term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 16 * t,
-                               a.data + (size_t)dir_cur.x * 16 + 1408 + 16 * t);
+                if (exists) {
+                    uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
+                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
+                    cp_async16(dst, src);
+                    cp_async16(dst + 16, src + 16);
+                }
                 cp_async_commit();
             }
-            if (cl.rt * kPfRows + r < a.rows) {
+            if (exists) {
                 const int q = cl.w & 15;
                 const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
-                wv.L = __ldg(reinterpret_cast<const uint4 *>(lit + 64 * q + 16 * t));
-                const uint32_t *cp = reinterpret_cast<const uint32_t *>(lit + 1024);
-                wv.c = __ldg(cp + 4 * q + t);
-                wv.P = __ldg(cp + 64 + 2 * q + (t >> 1));
+                const uint4 *lp = reinterpret_cast<const uint4 *>(lit + 64 * q + 32 * h);
+                wv.L0 = __ldg(lp);
+                wv.L1 = __ldg(lp + 1);
+                wv.c = __ldg(reinterpret_cast<const uint2 *>(lit + 1024 + 16 * q + 8 * h));
+                wv.P = __ldg(reinterpret_cast<const uint32_t *>(lit + 1024 + 256 + 8 * q + 4 * h));
             }
         };
         Win pf[kAhead];
@@ -439,21 +444,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 real = (int64_t)cd.rt * kPfRows + r < a.rows;
                 dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
                 // a piece that starts inside a block column: the escapes of
-                // the block's earlier windows come before this window's ranks
+                // the block's earlier windows come before this window's ranks;
+                // lane h counts whole windows h, h + 2, ... below q0, four
+                // windows' loads at a time
                 const int q0 = cd.w & 15;
                 if (q0 > 0) {
                     uint32_t pre = 0;
                     if (real) {
-                        const uint32_t *cp = reinterpret_cast<const uint32_t *>(a.data + (size_t)dir.x * 16 + 1024);
-                        for (int qq = 0; qq < q0; ++qq) {
-                            uint32_t s0, s1;
-                            selectors16(__ldg(cp + 4 * qq + t), __ldg(cp + 64 + 2 * qq + (t >> 1)), rl, rh, s0, s1);
-                            pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1));
+                        const uint8_t *cb = a.data + (size_t)dir.x * 16 + 1024;
+                        for (int base = h; base < q0; base += 8) {
+                            uint4 cw[4];
+                            uint2 pw[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int qq = base + 2 * i;
+                                if (qq < q0) {
+                                    cw[i] = __ldg(reinterpret_cast<const uint4 *>(cb + 16 * qq));
+                                    pw[i] = __ldg(reinterpret_cast<const uint2 *>(cb + 256 + 8 * qq));
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                if (base + 2 * i < q0) {
+                                    uint32_t s0, s1, s2, s3;
+                                    selectors16(cw[i].x, pw[i].x, 2u, 1u, s0, s1);
+                                    selectors16(cw[i].y, pw[i].x, 0u, 31u, s2, s3);
+                                    pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
+                                           __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
+                                    selectors16(cw[i].z, pw[i].y, 2u, 1u, s0, s1);
+                                    selectors16(cw[i].w, pw[i].y, 0u, 31u, s2, s3);
+                                    pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
+                                           __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
+                                }
+                            }
                         }
                     }
-                    pre += __shfl_xor_sync(0xffffffffu, pre, 1);
-                    pre += __shfl_xor_sync(0xffffffffu, pre, 2);
-                    run = pre;
+                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
                 }
                 cp_async_wait(seg_load - seg_dec);
                 __syncwarp();
@@ -467,47 +493,50 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             // code 7 decodes to sign | exponent 0 | mantissa; the terminal
             // exponent is ORed in below
             const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
-            uint32_t p[8];
-            uint32_t e0 = 0, e1 = 0;
+            uint32_t p[16];
+            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
             if (real) {
-                uint32_t s0, s1;
-                selectors16(cur.c, cur.P, rl, rh, s0, s1);
-                dec4(cur.L.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(cur.L.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(cur.L.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(cur.L.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                uint32_t s0, s1, s2, s3;
+                selectors16(cur.c.x, cur.P, 2u, 1u, s0, s1);   // quarter 2h (even)
+                selectors16(cur.c.y, cur.P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
+                dec4(cur.L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(cur.L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(cur.L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(cur.L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                dec4(cur.L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
+                dec4(cur.L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
+                dec4(cur.L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
+                dec4(cur.L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
                 e0 = escape_nibbles(s0);
                 e1 = escape_nibbles(s1);
+                e2 = escape_nibbles(s2);
+                e3 = escape_nibbles(s3);
             } else {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) p[k] = 0u;
+                for (int k = 0; k < 16; ++k) p[k] = 0u;
             }
-            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t)) ^ sw) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
-            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t + 1)) ^ sw) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
+                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
             // escapes: rank among the row block's escapes -> terminal exponent
-            const uint32_t mine = __popc(e0) + __popc(e1);
-            uint32_t incl = mine;
-            uint32_t v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
-            if (t >= 1) incl += v;
-            v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
-            if (t >= 2) incl += v;
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 3, 4);
-            uint32_t rank = run + incl - mine;
-            run += total;
+            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            uint32_t rank = run + (h ? other : 0u);
+            run += mine + other;
             if (mine) {
                 const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    uint32_t m = g == 0 ? e0 : e1;
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
                     while (m) {
-                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 16
+                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
                         m &= m - 1;
                         uint16_t *wp = reinterpret_cast<uint16_t *>(
-                            rowp + (((((uint32_t)(2 * t) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
+                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
                         if (rank < nesc) {
-                            const uint32_t ex = rank < (uint32_t)kTermRow
-                                                    ? ts[rank]
-                                                    : a.data[(size_t)dir.x * 16 + 1408 + rank];
+                            const uint32_t ex = rank < (uint32_t)kTermRow ? ts[rank]
+                                                                          : a.data[(size_t)dir.x * 16 + 1408 + rank];
                             *wp |= (uint16_t)(ex << 7);
                         } else {
                             *wp = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
@@ -548,7 +577,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             const int32_t tok0 = (t % a.ntok) * a.ntt;
             const float bv = (a.bias && row < a.rows) ? bf16_bits_to_f32(a.bias[row]) : 0.f;
             const int slot = t == R.tA ? 0 : 1;
-            float *mine = a.part + (((int64_t)blockIdx.x * 2 + slot) * kPfRows + qtr * 32 + lane) * a.ntt;
+            // a piece's partial: [activation row][weight row], so each store of
+            // one activation row by the warp's 32 lanes (rows) is one 128-byte line
+            float *mine = a.part + ((int64_t)blockIdx.x * 2 + slot) * a.ntt * kPfRows + qtr * 32 + lane;
             for (int32_t c0 = 0; c0 < a.ntt; c0 += 32) {
                 uint32_t v[32];
                 tmem_load32(tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(b * kAccCols + c0), v);
@@ -566,11 +597,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                                 reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
                         }
                 } else {
-                    float4 *d = reinterpret_cast<float4 *>(mine + c0);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        __stcg(d + k, make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                                                  __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3])));
+                    for (int k = 0; k < 32; ++k) __stcg(mine + (int64_t)(c0 + k) * kPfRows, __uint_as_float(v[k]));
                 }
             }
             tmem_fence_before();
@@ -594,22 +622,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 float acc[16];
                 for (int64_t c = cf; c <= cl; ++c) {
                     const int sc = t == cta_start(c, G, a.W) / a.nwin ? 0 : 1;
-                    const float4 *pp = reinterpret_cast<const float4 *>(
-                        a.part + ((c * 2 + sc) * kPfRows + qtr * 32 + lane) * a.ntt + c0);
+                    const float *pp = a.part + (c * 2 + sc) * a.ntt * kPfRows + (int64_t)c0 * kPfRows + qtr * 32 + lane;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float4 x = __ldcg(pp + k);
-                        if (c == cf) {
-                            acc[4 * k] = x.x;
-                            acc[4 * k + 1] = x.y;
-                            acc[4 * k + 2] = x.z;
-                            acc[4 * k + 3] = x.w;
-                        } else {
-                            acc[4 * k] += x.x;
-                            acc[4 * k + 1] += x.y;
-                            acc[4 * k + 2] += x.z;
-                            acc[4 * k + 3] += x.w;
-                        }
+                    for (int k = 0; k < 16; ++k) {
+                        const float x = __ldcg(pp + k * kPfRows);
+                        acc[k] = c == cf ? x : acc[k] + x;
                     }
                 }
                 if (row < a.rows)
