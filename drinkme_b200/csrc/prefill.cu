@@ -58,13 +58,16 @@ namespace {
 
 constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
 constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
-constexpr int kPfStages = 4;      // windows in flight (both operands)
+constexpr int kXStages = 3;       // activation windows in flight
+constexpr int kWStages = 3;       // decoded weight windows in flight
 constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
 constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
 constexpr int kPfProd = 12;       // warp 12: activation TMA
 constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
 constexpr int kPfThreads = 14 * 32;
-constexpr int kAhead = 4;         // windows of weight operands in flight per decoding lane
+constexpr int kAhead = 4;         // windows of compressed operands in flight (a cp.async ring)
+constexpr int kOpRow = 96;        // per row and window: 64 literal bytes, 4 code words, 2 bit-2 words
+constexpr int kOpStage = kPfRows * kOpRow;
 constexpr int kWStage = kPfRows * 128;    // 16 KB: 128 rows x 64 bf16
 constexpr int kXStage = kPfTokMax * 128;  // 32 KB: 256 rows x 64 bf16
 constexpr int kTermRing = 4;              // block columns of staged terminal bytes
@@ -74,10 +77,11 @@ constexpr int kAccCols = 256;             // tensor-memory columns per accumulat
 constexpr int kMaxParts = 8;
 
 constexpr int kOffX = 0;
-constexpr int kOffW = kOffX + kPfStages * kXStage;
-constexpr int kOffTerm = kOffW + kPfStages * kWStage;
+constexpr int kOffW = kOffX + kXStages * kXStage;
+constexpr int kOffOp = kOffW + kWStages * kWStage;
+constexpr int kOffTerm = kOffOp + kAhead * kOpStage;
 constexpr int kOffBar = kOffTerm + kTermRing * kTermStage;
-constexpr int kNumBars = 4 * kPfStages + 5;
+constexpr int kNumBars = 2 * kXStages + 2 * kWStages + 5;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kOffTabs = kOffTmem + 16;
 constexpr int kSmemBytes = kOffTabs + kMaxParts * 16 + 1024;  // + alignment slack
@@ -140,6 +144,12 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 // 16 bytes global -> shared, asynchronously (the LDGSTS path, L2 only).
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Waits until at most `n` (0..3) of this thread's newest groups are pending.
@@ -302,24 +312,17 @@ struct Cursor {
     }
 };
 
-// A window's loaded operands for one lane: 32 literal bytes, two code-plane
-// words and the bit-2 word.
-struct Win {
-    uint4 L0, L1;    // 32 literal bytes
-    uint2 c;         // the two low-two-bit code words
-    uint32_t P;      // the bit-2 word
-};
-
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid_constant__ CUtensorMap xmap, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned tiles (the swizzle pattern follows address bits 7-9)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *xs = smem + kOffX;
     uint8_t *ws = smem + kOffW;
+    uint8_t *ops = smem + kOffOp;     // [kAhead][128 rows][kOpRow]: compressed operands in flight
     uint8_t *term = smem + kOffTerm;  // [kTermRing][128 rows][64 bytes]
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
-    uint64_t *x_full = bar, *x_empty = bar + kPfStages, *w_full = bar + 2 * kPfStages, *w_empty = bar + 3 * kPfStages;
-    uint64_t *acc_full = bar + 4 * kPfStages, *acc_empty = acc_full + 2, *drained = acc_empty + 2;
+    uint64_t *x_full = bar, *x_empty = bar + kXStages, *w_full = bar + 2 * kXStages, *w_empty = w_full + kWStages;
+    uint64_t *acc_full = w_empty + kWStages, *acc_empty = acc_full + 2, *drained = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffTmem);
     uint32_t *tabs = reinterpret_cast<uint32_t *>(smem + kOffTabs);  // [kMaxParts][4]
 
@@ -328,9 +331,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
     Range R;
     R.init(blockIdx.x, G, a.W, a.nwin);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPfStages; ++s) {
+        for (int s = 0; s < kXStages; ++s) {
             mbar_init(&x_full[s], 1);
             mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < kWStages; ++s) {
             mbar_init(&w_full[s], kPfDecWarps);
             mbar_init(&w_empty[s], 1);
         }
@@ -383,10 +388,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             if (row >= a.rows) return make_uint2(0, 0);
             return __ldg(a.rowdir + row * NB + bc);
         };
-        // the load cursor's window into `wv`: a new segment takes the
-        // prefetched directory entry, prefetches the next one and stages its
-        // terminal bytes (lane h: bytes [32h, 32h + 32))
-        auto load_window = [&](Win &wv) {
+        // the load cursor's window into ring slot `nload` mod kAhead: a new
+        // segment takes the prefetched directory entry, prefetches the next
+        // one and stages its terminal bytes (lane h: bytes [32h, 32h + 32));
+        // one cp.async group per window
+        int32_t nload = 0;  // windows the load cursor has issued
+        auto load_window = [&]() {
             const int32_t bc = cl.w >> 4;
             const bool exists = (int64_t)cl.rt * kPfRows + r < a.rows;
             if (cl.t != seg_t || bc != seg_bc) {
@@ -405,25 +412,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                     cp_async16(dst, src);
                     cp_async16(dst + 16, src + 16);
                 }
-                cp_async_commit();
             }
             if (exists) {
                 const int q = cl.w & 15;
                 const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
-                const uint4 *lp = reinterpret_cast<const uint4 *>(lit + 64 * q + 32 * h);
-                wv.L0 = __ldg(lp);
-                wv.L1 = __ldg(lp + 1);
-                wv.c = __ldg(reinterpret_cast<const uint2 *>(lit + 1024 + 16 * q + 8 * h));
-                wv.P = __ldg(reinterpret_cast<const uint32_t *>(lit + 1024 + 256 + 8 * q + 4 * h));
+                uint8_t *o = ops + (nload % kAhead) * kOpStage + r * kOpRow;
+                cp_async16(o + 32 * h, lit + 64 * q + 32 * h);
+                cp_async16(o + 32 * h + 16, lit + 64 * q + 32 * h + 16);
+                cp_async8(o + 64 + 8 * h, lit + 1024 + 16 * q + 8 * h);
+                cp_async4(o + 80 + 4 * h, lit + 1024 + 256 + 8 * q + 4 * h);
             }
+            cp_async_commit();
+            ++nload;
         };
-        Win pf[kAhead];
-#pragma unroll
-        for (int i = 0; i < kAhead; ++i) {
-            if (!cl.done) {
-                load_window(pf[i]);
-                cl.next(R, a.ntok);
-            }
+#pragma unroll 1
+        for (int i = 0; i < kAhead && !cl.done; ++i) {
+            load_window();
+            cl.next(R, a.ntok);
         }
         int32_t seg_dec = -1;  // segment of the decode position
         uint32_t run = 0;      // escapes of this row block before the current window
@@ -433,8 +438,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         int32_t dseg_t = -1, dseg_bc = -1;
         uint2 dir = make_uint2(0, 0);  // the decode position's row block: stream offset, nesc | part << 16
         bool real = false;             // its row exists
-        // decode the window in `cur`, then load the window kAhead ahead into it
-        auto step = [&](Win &cur) {
+        // decode window j (ring slot j mod kAhead), then load the window
+        // kAhead ahead into the slot it frees
+        while (!cd.done) {
             const int32_t bc = cd.w >> 4;
             if (cd.t != dseg_t || bc != dseg_bc) {
                 ++seg_dec;
@@ -481,10 +487,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                     }
                     run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
                 }
-                cp_async_wait(seg_load - seg_dec);
-                __syncwarp();
             }
-            const int s = j % kPfStages, use = j / kPfStages;
+            // this window's group (and, at a segment start, its terminals) landed
+            cp_async_wait(nload - j - 1);
+            __syncwarp();
+            const int s = j % kWStages, use = j / kWStages;
             if (use > 0 && ok && !mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
             uint8_t *rowp = ws + s * kWStage + r * 128;
             const uint32_t part = dir.y >> 16;
@@ -496,17 +503,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             uint32_t p[16];
             uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
             if (real) {
+                const uint8_t *o = ops + (j % kAhead) * kOpStage + r * kOpRow;
+                const uint4 L0 = *reinterpret_cast<const uint4 *>(o + 32 * h);
+                const uint4 L1 = *reinterpret_cast<const uint4 *>(o + 32 * h + 16);
+                const uint2 c = *reinterpret_cast<const uint2 *>(o + 64 + 8 * h);
+                const uint32_t P = *reinterpret_cast<const uint32_t *>(o + 80 + 4 * h);
                 uint32_t s0, s1, s2, s3;
-                selectors16(cur.c.x, cur.P, 2u, 1u, s0, s1);   // quarter 2h (even)
-                selectors16(cur.c.y, cur.P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
-                dec4(cur.L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(cur.L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(cur.L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(cur.L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
-                dec4(cur.L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
-                dec4(cur.L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
-                dec4(cur.L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
-                dec4(cur.L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
+                selectors16(c.x, P, 2u, 1u, s0, s1);   // quarter 2h (even)
+                selectors16(c.y, P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
+                dec4(L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                dec4(L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
+                dec4(L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
+                dec4(L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
+                dec4(L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
                 e0 = escape_nibbles(s0);
                 e1 = escape_nibbles(s1);
                 e2 = escape_nibbles(s2);
@@ -548,18 +560,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             fence_proxy_async_smem();  // these generic writes, before the tensor core's async reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_full[s]);
-            // this register set's next window
+            // every lane has read its slot: it takes the window kAhead ahead
+            __syncwarp();
             if (!cl.done) {
-                load_window(cur);
+                load_window();
                 cl.next(R, a.ntok);
             }
             cd.next(R, a.ntok);
             ++j;
-        };
-        while (!cd.done) {
-#pragma unroll
-            for (int i = 0; i < kAhead; ++i)
-                if (!cd.done) step(pf[i]);
         }
         cp_async_wait(0);
     } else if (warp >= kPfEpi0 && warp < kPfEpi0 + 4) {
@@ -650,7 +658,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             int32_t j = 0;
             Cursor cu;
             for (cu.begin(R, a.ntok); !cu.done && ok; cu.next(R, a.ntok), ++j) {
-                const int s = j % kPfStages, use = j / kPfStages;
+                const int s = j % kXStages, use = j / kXStages;
                 if (use > 0 && !mbar_wait(&x_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
                 if (!ok) break;
                 mbar_arrive_expect_tx(&x_full[s], bytes);
@@ -658,8 +666,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             }
             // every copy issued lands before the CTA exits (the last use of
             // each stage: its phase has completed, or completes now)
-            for (int32_t i = std::max<int32_t>(0, j - kPfStages); i < j; ++i)
-                mbar_wait(&x_full[i % kPfStages], (uint32_t)((i / kPfStages) & 1), a.err, kErrWaitDrain);
+            for (int32_t i = std::max<int32_t>(0, j - kXStages); i < j; ++i)
+                mbar_wait(&x_full[i % kXStages], (uint32_t)((i / kXStages) & 1), a.err, kErrWaitDrain);
         }
     } else {
         // ---------------------------------------------------------- MMA --
@@ -673,21 +681,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 ok = false;
             tmem_fence_after();
             for (int32_t w = w0; w < w1; ++w, ++j) {
-                const int s = j % kPfStages;
-                const uint32_t par = (uint32_t)((j / kPfStages) & 1);
-                if (ok && !mbar_wait(&x_full[s], par, a.err, kErrWaitFull)) ok = false;
-                if (ok && !mbar_wait(&w_full[s], par, a.err, kErrWaitFull)) ok = false;
+                const int sx = j % kXStages, sw = j % kWStages;
+                if (ok && !mbar_wait(&x_full[sx], (uint32_t)((j / kXStages) & 1), a.err, kErrWaitFull)) ok = false;
+                if (ok && !mbar_wait(&w_full[sw], (uint32_t)((j / kWStages) & 1), a.err, kErrWaitFull)) ok = false;
                 tmem_fence_after();
                 if (lane == 0) {
                     if (ok) {
-                        const uint32_t wb = smem_addr(ws + s * kWStage), xb = smem_addr(xs + s * kXStage);
+                        const uint32_t wb = smem_addr(ws + sw * kWStage), xb = smem_addr(xs + sx * kXStage);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             umma_bf16(tmem + (uint32_t)(b * kAccCols), sw128_desc(wb + 32 * k), sw128_desc(xb + 32 * k),
                                       a.idesc, (w > w0 || k > 0) ? 1u : 0u);
                     }
-                    umma_commit(&w_empty[s]);  // frees the stages once these MMAs have read them
-                    umma_commit(&x_empty[s]);
+                    umma_commit(&w_empty[sw]);  // frees the stages once these MMAs have read them
+                    umma_commit(&x_empty[sx]);
                 }
                 __syncwarp();
             }
