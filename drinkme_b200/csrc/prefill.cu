@@ -22,21 +22,24 @@
 //     partial goes to the workspace, and for each quarter of the tile's rows
 //     the last piece to arrive (an acquire-release counter) adds every
 //     piece's partial in CTA order and writes the outputs.
-//   * Warps 0-7 decode: a lane pair per weight row, lane h taking weights
-//     [32h, 32h + 32) of each window, from the loader's code planes with the
+//   * Warps 0-15 decode: four lanes per weight row, lane t taking weights
+//     [16t, 16t + 16) of each window, from the loader's code planes with the
 //     GEMV's byte-parallel table lookups (escaped weights come out as sign |
 //     0 | mantissa), into the 128-byte-swizzled K-major tile the tensor core
 //     reads. An escaped weight's terminal exponent is its rank among the row
-//     block's escapes: the lane pair counts code-7 nibbles as it goes and ORs
-//     the exponent in from the row's terminal stream, staged per block
-//     column in shared memory by cp.async. Each lane keeps the operands of
-//     the next four windows in flight, in register sets of an unrolled loop,
-//     and the row-block directory entry of the next block column.
-//   * Warp 12 loads each activation window with one TMA tensor copy (no
-//     multicast) in the same swizzled layout; warp 13 owns the tensor memory
+//     block's escapes: the row's lanes count code-7 nibbles as they go (a
+//     four-lane prefix sum) and rewrite each escaped weight whole from its
+//     literal byte and the row's terminal stream, staged per block column in
+//     shared memory. The compressed operands of the next four windows are
+//     staged by cp.async into a shared-memory ring (the lanes hold no loads
+//     in flight, so the per-window barrier release and proxy fence never wait
+//     for them); the row-block directory entry of the next block column is
+//     prefetched a block column ahead.
+//   * Warp 20 loads each activation window with one TMA tensor copy (no
+//     multicast) in the same swizzled layout; warp 21 owns the tensor memory
 //     and one of its lanes issues the MMAs (kind::f16, M = 128, N = tokens,
 //     K = 16) and commits each window to the barriers that free its stages.
-//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
+//   * Warps 16-19 read the accumulators (tcgen05.ld, a lane per weight row),
 //     add the bias in fp32, round once and store; or write a piece's partial
 //     (activation-row major, so a warp's store is one 128-byte line).
 //   * Every wait is bounded (the device error word records a wait that gave
@@ -60,11 +63,11 @@ constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
 constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
 constexpr int kXStages = 3;       // activation windows in flight
 constexpr int kWStages = 3;       // decoded weight windows in flight
-constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
-constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
-constexpr int kPfProd = 12;       // warp 12: activation TMA
-constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
-constexpr int kPfThreads = 14 * 32;
+constexpr int kPfDecWarps = 16;   // four lanes per weight row, 8 rows per warp
+constexpr int kPfEpi0 = 16;       // warps 16-19: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kPfProd = 20;       // warp 20: activation TMA
+constexpr int kPfMma = 21;        // warp 21: tensor memory and MMA issue
+constexpr int kPfThreads = 22 * 32;
 constexpr int kAhead = 4;         // windows of compressed operands in flight (a cp.async ring)
 constexpr int kOpRow = 96;        // per row and window: 64 literal bytes, 4 code words, 2 bit-2 words
 constexpr int kOpStage = kPfRows * kOpRow;
@@ -120,14 +123,12 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -144,9 +145,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 // 16 bytes global -> shared, asynchronously (the LDGSTS path, L2 only).
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
@@ -361,16 +359,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
 
     if (warp < kPfDecWarps) {
         // ------------------------------------------------------ decode --
-        // a lane pair per weight row; lane h decodes weights [32h, 32h + 32)
-        // of every window (the GEMV's quarters 2h and 2h + 1 of a quad)
-        const int r = warp * 16 + (lane >> 1);
-        const int h = lane & 1;
+        // four lanes per weight row; lane t decodes weights [16t, 16t + 16)
+        // of every window (the GEMV's quarter t of a quad)
+        const int r = warp * 8 + (lane >> 2);
+        const int t = lane & 3;
         const uint32_t sw = (uint32_t)(r & 7);
+        const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         bool ok = true;
-        // the load cursor runs kAhead windows before the decode position;
-        // window i's operands live in register set i mod kAhead (the loop is
-        // unrolled by kAhead, so no register is moved while its load is in
-        // flight)
+        // the load cursor runs kAhead windows before the decode position,
+        // staging each window's compressed operands by cp.async into ring
+        // slot (window mod kAhead) of this row: nothing the decoder waits on
+        // is a load in flight of its own (a release or a proxy fence would
+        // wait for those)
         Cursor cl;
         cl.begin(R, a.ntok);
         // segments the load cursor has entered; the ring of staged terminal
@@ -390,8 +390,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         };
         // the load cursor's window into ring slot `nload` mod kAhead: a new
         // segment takes the prefetched directory entry, prefetches the next
-        // one and stages its terminal bytes (lane h: bytes [32h, 32h + 32));
-        // one cp.async group per window
+        // one and stages its terminal bytes (lane t: bytes [16t, 16t + 16));
+        // one cp.async group per window. Per row and window the slot holds
+        // the 64 literal bytes, the four code-plane words and, per lane, the
+        // bit-2 word it needs.
         int32_t nload = 0;  // windows the load cursor has issued
         auto load_window = [&]() {
             const int32_t bc = cl.w >> 4;
@@ -406,21 +408,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 ++seg_load;
                 seg_t = cl.t;
                 seg_bc = bc;
-                if (exists) {
-                    uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
-                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
-                    cp_async16(dst, src);
-                    cp_async16(dst + 16, src + 16);
-                }
+                if (exists)
+                    cp_async16(term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 16 * t,
+                               a.data + (size_t)dir_cur.x * 16 + 1408 + 16 * t);
             }
             if (exists) {
                 const int q = cl.w & 15;
                 const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
                 uint8_t *o = ops + (nload % kAhead) * kOpStage + r * kOpRow;
-                cp_async16(o + 32 * h, lit + 64 * q + 32 * h);
-                cp_async16(o + 32 * h + 16, lit + 64 * q + 32 * h + 16);
-                cp_async8(o + 64 + 8 * h, lit + 1024 + 16 * q + 8 * h);
-                cp_async4(o + 80 + 4 * h, lit + 1024 + 256 + 8 * q + 4 * h);
+                cp_async16(o + 16 * t, lit + 64 * q + 16 * t);
+                cp_async4(o + 64 + 4 * t, lit + 1024 + 16 * q + 4 * t);
+                cp_async4(o + 80 + 4 * t, lit + 1024 + 256 + 8 * q + 4 * (t >> 1));
             }
             cp_async_commit();
             ++nload;
@@ -451,27 +449,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
                 // a piece that starts inside a block column: the escapes of
                 // the block's earlier windows come before this window's ranks;
-                // lane h counts whole windows h, h + 2, ... below q0, four
-                // windows' loads at a time
+                // lane t counts whole windows t, t + 4, t + 8, t + 12 below q0,
+                // two windows' loads at a time
                 const int q0 = cd.w & 15;
                 if (q0 > 0) {
                     uint32_t pre = 0;
                     if (real) {
                         const uint8_t *cb = a.data + (size_t)dir.x * 16 + 1024;
-                        for (int base = h; base < q0; base += 8) {
-                            uint4 cw[4];
-                            uint2 pw[4];
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const int qq = base + 2 * i;
+                        for (int i0 = 0; i0 < 4; i0 += 2) {
+                            uint4 cw[2];
+                            uint2 pw[2];
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                const int qq = t + 4 * (i0 + i);
                                 if (qq < q0) {
                                     cw[i] = __ldg(reinterpret_cast<const uint4 *>(cb + 16 * qq));
                                     pw[i] = __ldg(reinterpret_cast<const uint2 *>(cb + 256 + 8 * qq));
                                 }
                             }
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                if (base + 2 * i < q0) {
+                            for (int i = 0; i < 2; ++i) {
+                                if (t + 4 * (i0 + i) < q0) {
                                     uint32_t s0, s1, s2, s3;
                                     selectors16(cw[i].x, pw[i].x, 2u, 1u, s0, s1);
                                     selectors16(cw[i].y, pw[i].x, 0u, 31u, s2, s3);
@@ -485,7 +484,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                             }
                         }
                     }
-                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 1);
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 2);
+                    run = pre;
                 }
             }
             // this window's group (and, at a segment start, its terminals) landed
@@ -494,65 +495,62 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             const int s = j % kWStages, use = j / kWStages;
             if (use > 0 && ok && !mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
             uint8_t *rowp = ws + s * kWStage + r * 128;
+            const uint8_t *o = ops + (j % kAhead) * kOpStage + r * kOpRow;
             const uint32_t part = dir.y >> 16;
             const uint32_t nesc = dir.y & 0xFFFFu;
             const uint32_t *tb = tabs + 4 * (part < kMaxParts ? part : 0);
-            // code 7 decodes to sign | exponent 0 | mantissa; the terminal
-            // exponent is ORed in below
+            // code 7 decodes to sign | exponent 0 | mantissa; escaped weights
+            // are rewritten whole below
             const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
-            uint32_t p[16];
-            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+            uint32_t p[8];
+            uint32_t e0 = 0, e1 = 0;
             if (real) {
-                const uint8_t *o = ops + (j % kAhead) * kOpStage + r * kOpRow;
-                const uint4 L0 = *reinterpret_cast<const uint4 *>(o + 32 * h);
-                const uint4 L1 = *reinterpret_cast<const uint4 *>(o + 32 * h + 16);
-                const uint2 c = *reinterpret_cast<const uint2 *>(o + 64 + 8 * h);
-                const uint32_t P = *reinterpret_cast<const uint32_t *>(o + 80 + 4 * h);
-                uint32_t s0, s1, s2, s3;
-                selectors16(c.x, P, 2u, 1u, s0, s1);   // quarter 2h (even)
-                selectors16(c.y, P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
-                dec4(L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
-                dec4(L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
-                dec4(L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
-                dec4(L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
-                dec4(L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
+                const uint4 L = *reinterpret_cast<const uint4 *>(o + 16 * t);
+                uint32_t s0, s1;
+                selectors16(*reinterpret_cast<const uint32_t *>(o + 64 + 4 * t),
+                            *reinterpret_cast<const uint32_t *>(o + 80 + 4 * t), rl, rh, s0, s1);
+                dec4(L.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(L.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(L.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(L.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
                 e0 = escape_nibbles(s0);
                 e1 = escape_nibbles(s1);
-                e2 = escape_nibbles(s2);
-                e3 = escape_nibbles(s3);
             } else {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) p[k] = 0u;
+                for (int k = 0; k < 8; ++k) p[k] = 0u;
             }
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
-                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
-            // escapes: rank among the row block's escapes -> terminal exponent
-            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-            uint32_t rank = run + (h ? other : 0u);
-            run += mine + other;
+            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t)) ^ sw) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t + 1)) ^ sw) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
+            // escapes: rank among the row block's escapes -> terminal
+            // exponent; the weight is written whole from its literal byte
+            // (independent loads and one store each, no read-modify-write)
+            const uint32_t mine = __popc(e0) + __popc(e1);
+            uint32_t incl = mine;
+            uint32_t v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
+            if (t >= 1) incl += v;
+            v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
+            if (t >= 2) incl += v;
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 3, 4);
+            uint32_t rank = run + incl - mine;
+            run += total;
             if (mine) {
                 const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
+                const uint8_t *lb = o + 16 * t;
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
+                for (int g = 0; g < 2; ++g) {
+                    uint32_t m = g == 0 ? e0 : e1;
                     while (m) {
-                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
+                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 16
                         m &= m - 1;
-                        uint16_t *wp = reinterpret_cast<uint16_t *>(
-                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1)));
+                        uint16_t w16 = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
                         if (rank < nesc) {
                             const uint32_t ex = rank < (uint32_t)kTermRow ? ts[rank]
                                                                           : a.data[(size_t)dir.x * 16 + 1408 + rank];
-                            *wp |= (uint16_t)(ex << 7);
-                        } else {
-                            *wp = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
+                            const uint32_t lit = lb[k];
+                            w16 = (uint16_t)(((lit & 0x80u) << 8) | (ex << 7) | (lit & 0x7Fu));
                         }
+                        *reinterpret_cast<uint16_t *>(
+                            rowp + (((((uint32_t)(2 * t) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1))) = w16;
                         ++rank;
                     }
                 }
@@ -561,7 +559,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_full[s]);
             // every lane has read its slot: it takes the window kAhead ahead
-            __syncwarp();
             if (!cl.done) {
                 load_window();
                 cl.next(R, a.ntok);
@@ -588,14 +585,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             // a piece's partial: [activation row][weight row], so each store of
             // one activation row by the warp's 32 lanes (rows) is one 128-byte line
             float *mine = a.part + ((int64_t)blockIdx.x * 2 + slot) * a.ntt * kPfRows + qtr * 32 + lane;
-            for (int32_t c0 = 0; c0 < a.ntt; c0 += 32) {
-                uint32_t v[32];
-                tmem_load32(tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(b * kAccCols + c0), v);
+            for (int32_t c0 = 0; c0 < a.ntt; c0 += 16) {
+                uint32_t v[16];
+                tmem_load16(tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(b * kAccCols + c0), v);
                 if (!ok) continue;
                 if (whole) {
                     if (row < a.rows)
 #pragma unroll
-                        for (int k = 0; k < 32; ++k) {
+                        for (int k = 0; k < 16; ++k) {
                             const int32_t tok = tok0 + c0 + k;
                             if (tok >= a.M) break;
                             const float y = __uint_as_float(v[k]) + bv;
@@ -606,7 +603,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                         }
                 } else {
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) __stcg(mine + (int64_t)(c0 + k) * kPfRows, __uint_as_float(v[k]));
+                    for (int k = 0; k < 16; ++k) __stcg(mine + (int64_t)(c0 + k) * kPfRows, __uint_as_float(v[k]));
                 }
             }
             tmem_fence_before();
@@ -744,7 +741,7 @@ struct PfPlan {
 
 PfPlan plan_prefill(const dm_tensor *t, int64_t M) {
     PfPlan P{};
-    P.ntt = (int32_t)std::min<int64_t>(kPfTokMax, (M + 31) / 32 * 32);  // whole 32-column tensor-memory loads
+    P.ntt = (int32_t)std::min<int64_t>(kPfTokMax, (M + 15) / 16 * 16);  // whole 16-column tensor-memory loads
     P.ntok = (int32_t)((M + P.ntt - 1) / P.ntt);
     P.nrt = (t->L.rows + kPfRows - 1) / kPfRows;
     P.ntiles = P.nrt * P.ntok;
