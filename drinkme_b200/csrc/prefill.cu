@@ -22,26 +22,27 @@
 //     partial goes to the workspace, and for each quarter of the tile's rows
 //     the last piece to arrive (an acquire-release counter) adds every
 //     piece's partial in CTA order and writes the outputs.
-//   * Warps 0-15 decode: four lanes per weight row, lane t taking weights
-//     [16t, 16t + 16) of each window, from the loader's code planes with the
+//   * Warps 0-7 decode: a lane pair per weight row, lane h taking weights
+//     [32h, 32h + 32) of each window, from the loader's code planes with the
 //     GEMV's byte-parallel table lookups (escaped weights come out as sign |
 //     0 | mantissa), into the 128-byte-swizzled K-major tile the tensor core
 //     reads. An escaped weight's terminal exponent is its rank among the row
-//     block's escapes: the row's lanes count code-7 nibbles as they go (a
-//     four-lane prefix sum) and rewrite each escaped weight whole from its
-//     literal byte and the row's terminal stream, staged per block column in
-//     shared memory. The compressed operands of the next four windows are
-//     staged by cp.async into a shared-memory ring (the lanes hold no loads
-//     in flight, so the per-window barrier release and proxy fence never wait
-//     for them); the row-block directory entry of the next block column is
-//     prefetched a block column ahead.
-//   * Warp 20 loads each activation window with one TMA tensor copy (no
-//     multicast) in the same swizzled layout; warp 21 owns the tensor memory
-//     and one of its lanes issues the MMAs (kind::f16, M = 128, N = tokens,
-//     K = 16) and commits each window to the barriers that free its stages.
-//   * Warps 16-19 read the accumulators (tcgen05.ld, a lane per weight row),
+//     block's escapes: the lane pair counts code-7 nibbles as it goes and
+//     rewrites each escaped weight whole from its literal byte and the row's
+//     terminal stream, staged per block column in shared memory. The
+//     compressed operands of the next four windows are staged by cp.async
+//     into a shared-memory ring (the lanes hold no loads in flight, so the
+//     per-window barrier release and proxy fence never wait for them); the
+//     row-block directory entry of the next block column is prefetched a
+//     block column ahead.
+//   * Warp 12 loads each activation window with one TMA tensor copy (no
+//     multicast) in the same swizzled layout; lane 0 of warp 13 owns the MMA
+//     issue (kind::f16, M = 128, N = tokens, K = 16) and commits each window
+//     to the barriers that free its stages; warp 13 owns the tensor memory.
+//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
 //     add the bias in fp32, round once and store; or write a piece's partial
-//     (activation-row major, so a warp's store is one 128-byte line).
+//     (activation-row major, so a warp's store is one 128-byte line). Only one
+//     lane of a warp polls a barrier.
 //   * Every wait is bounded (the device error word records a wait that gave
 //     up); the tensor memory is freed on every path.
 #include <cuda.h>
@@ -63,11 +64,11 @@ constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
 constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
 constexpr int kXStages = 3;       // activation windows in flight
 constexpr int kWStages = 3;       // decoded weight windows in flight
-constexpr int kPfDecWarps = 16;   // four lanes per weight row, 8 rows per warp
-constexpr int kPfEpi0 = 16;       // warps 16-19: the epilogue (tensor-memory lane quarters 0-3)
-constexpr int kPfProd = 20;       // warp 20: activation TMA
-constexpr int kPfMma = 21;        // warp 21: tensor memory and MMA issue
-constexpr int kPfThreads = 22 * 32;
+constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
+constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kPfProd = 12;       // warp 12: activation TMA
+constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
+constexpr int kPfThreads = 14 * 32;
 constexpr int kAhead = 4;         // windows of compressed operands in flight (a cp.async ring)
 constexpr int kOpRow = 96;        // per row and window: 64 literal bytes, 4 code words, 2 bit-2 words
 constexpr int kOpStage = kPfRows * kOpRow;
@@ -133,6 +134,24 @@ __device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// mbar_wait for a wait expected to be long: a try without a time hint, then a
+// 256 ns sleep between tries (about 2^16 tries: tens of milliseconds), so the
+// waiting lane takes almost no issue slots or shared-memory bandwidth.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, int *err, int code) {
+    for (uint32_t i = 0; i < (1u << 18); ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        __nanosleep(256);
+    }
+    if (err) atomicExch(err, code);
+    return false;
+}
+
 // One 2-D TMA tile load global -> shared (no multicast), completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar) {
     asm volatile(
@@ -145,6 +164,9 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 // 16 bytes global -> shared, asynchronously (the LDGSTS path, L2 only).
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
@@ -359,12 +381,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
 
     if (warp < kPfDecWarps) {
         // ------------------------------------------------------ decode --
-        // four lanes per weight row; lane t decodes weights [16t, 16t + 16)
-        // of every window (the GEMV's quarter t of a quad)
-        const int r = warp * 8 + (lane >> 2);
-        const int t = lane & 3;
+        // a lane pair per weight row; lane h decodes weights [32h, 32h + 32)
+        // of every window (the GEMV's quarters 2h and 2h + 1 of a quad)
+        const int r = warp * 16 + (lane >> 1);
+        const int h = lane & 1;
         const uint32_t sw = (uint32_t)(r & 7);
-        const uint32_t rl = (t & 1) ? 0u : 2u, rh = (t & 1) ? 31u : 1u;
         bool ok = true;
         // the load cursor runs kAhead windows before the decode position,
         // staging each window's compressed operands by cp.async into ring
@@ -390,10 +411,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         };
         // the load cursor's window into ring slot `nload` mod kAhead: a new
         // segment takes the prefetched directory entry, prefetches the next
-        // one and stages its terminal bytes (lane t: bytes [16t, 16t + 16));
+        // one and stages its terminal bytes (lane h: bytes [32h, 32h + 32));
         // one cp.async group per window. Per row and window the slot holds
-        // the 64 literal bytes, the four code-plane words and, per lane, the
-        // bit-2 word it needs.
+        // the 64 literal bytes, the four code-plane words and the two bit-2
+        // words.
         int32_t nload = 0;  // windows the load cursor has issued
         auto load_window = [&]() {
             const int32_t bc = cl.w >> 4;
@@ -408,17 +429,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 ++seg_load;
                 seg_t = cl.t;
                 seg_bc = bc;
-                if (exists)
-                    cp_async16(term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 16 * t,
-                               a.data + (size_t)dir_cur.x * 16 + 1408 + 16 * t);
+                if (exists) {
+                    uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
+                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
+                    cp_async16(dst, src);
+                    cp_async16(dst + 16, src + 16);
+                }
             }
             if (exists) {
                 const int q = cl.w & 15;
                 const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
                 uint8_t *o = ops + (nload % kAhead) * kOpStage + r * kOpRow;
-                cp_async16(o + 16 * t, lit + 64 * q + 16 * t);
-                cp_async4(o + 64 + 4 * t, lit + 1024 + 16 * q + 4 * t);
-                cp_async4(o + 80 + 4 * t, lit + 1024 + 256 + 8 * q + 4 * (t >> 1));
+                cp_async16(o + 32 * h, lit + 64 * q + 32 * h);
+                cp_async16(o + 32 * h + 16, lit + 64 * q + 32 * h + 16);
+                cp_async8(o + 64 + 8 * h, lit + 1024 + 16 * q + 8 * h);
+                cp_async4(o + 80 + 4 * h, lit + 1024 + 256 + 8 * q + 4 * h);
             }
             cp_async_commit();
             ++nload;
@@ -449,20 +474,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
                 // a piece that starts inside a block column: the escapes of
                 // the block's earlier windows come before this window's ranks;
-                // lane t counts whole windows t, t + 4, t + 8, t + 12 below q0,
-                // two windows' loads at a time
+                // lane h counts whole windows h, h + 2, ... below q0, two
+                // windows' loads at a time
                 const int q0 = cd.w & 15;
                 if (q0 > 0) {
                     uint32_t pre = 0;
                     if (real) {
                         const uint8_t *cb = a.data + (size_t)dir.x * 16 + 1024;
-#pragma unroll
-                        for (int i0 = 0; i0 < 4; i0 += 2) {
+                        for (int base = h; base < q0; base += 4) {
                             uint4 cw[2];
                             uint2 pw[2];
 #pragma unroll
                             for (int i = 0; i < 2; ++i) {
-                                const int qq = t + 4 * (i0 + i);
+                                const int qq = base + 2 * i;
                                 if (qq < q0) {
                                     cw[i] = __ldg(reinterpret_cast<const uint4 *>(cb + 16 * qq));
                                     pw[i] = __ldg(reinterpret_cast<const uint2 *>(cb + 256 + 8 * qq));
@@ -470,7 +494,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                             }
 #pragma unroll
                             for (int i = 0; i < 2; ++i) {
-                                if (t + 4 * (i0 + i) < q0) {
+                                if (base + 2 * i < q0) {
                                     uint32_t s0, s1, s2, s3;
                                     selectors16(cw[i].x, pw[i].x, 2u, 1u, s0, s1);
                                     selectors16(cw[i].y, pw[i].x, 0u, 31u, s2, s3);
@@ -484,16 +508,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                             }
                         }
                     }
-                    pre += __shfl_xor_sync(0xffffffffu, pre, 1);
-                    pre += __shfl_xor_sync(0xffffffffu, pre, 2);
-                    run = pre;
+                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
                 }
             }
             // this window's group (and, at a segment start, its terminals) landed
             cp_async_wait(nload - j - 1);
             __syncwarp();
             const int s = j % kWStages, use = j / kWStages;
-            if (use > 0 && ok && !mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
+            if (use > 0 && ok) {  // lane 0 polls; the warp barrier orders the others after it
+                int got = 1;
+                if (lane == 0) got = mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty);
+                ok = __shfl_sync(0xffffffffu, got, 0) != 0;
+            }
             uint8_t *rowp = ws + s * kWStage + r * 128;
             const uint8_t *o = ops + (j % kAhead) * kOpStage + r * kOpRow;
             const uint32_t part = dir.y >> 16;
@@ -502,45 +528,51 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             // code 7 decodes to sign | exponent 0 | mantissa; escaped weights
             // are rewritten whole below
             const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
-            uint32_t p[8];
-            uint32_t e0 = 0, e1 = 0;
+            uint32_t p[16];
+            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
             if (real) {
-                const uint4 L = *reinterpret_cast<const uint4 *>(o + 16 * t);
-                uint32_t s0, s1;
-                selectors16(*reinterpret_cast<const uint32_t *>(o + 64 + 4 * t),
-                            *reinterpret_cast<const uint32_t *>(o + 80 + 4 * t), rl, rh, s0, s1);
-                dec4(L.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(L.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(L.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(L.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                const uint4 L0 = *reinterpret_cast<const uint4 *>(o + 32 * h);
+                const uint4 L1 = *reinterpret_cast<const uint4 *>(o + 32 * h + 16);
+                const uint2 c = *reinterpret_cast<const uint2 *>(o + 64 + 8 * h);
+                const uint32_t P = *reinterpret_cast<const uint32_t *>(o + 80 + 4 * h);
+                uint32_t s0, s1, s2, s3;
+                selectors16(c.x, P, 2u, 1u, s0, s1);   // quarter 2h (even)
+                selectors16(c.y, P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
+                dec4(L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
+                dec4(L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
+                dec4(L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
+                dec4(L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
+                dec4(L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
+                dec4(L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
+                dec4(L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
+                dec4(L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
                 e0 = escape_nibbles(s0);
                 e1 = escape_nibbles(s1);
+                e2 = escape_nibbles(s2);
+                e3 = escape_nibbles(s3);
             } else {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) p[k] = 0u;
+                for (int k = 0; k < 16; ++k) p[k] = 0u;
             }
-            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t)) ^ sw) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
-            *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(2 * t + 1)) ^ sw) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
+                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
             // escapes: rank among the row block's escapes -> terminal
             // exponent; the weight is written whole from its literal byte
             // (independent loads and one store each, no read-modify-write)
-            const uint32_t mine = __popc(e0) + __popc(e1);
-            uint32_t incl = mine;
-            uint32_t v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
-            if (t >= 1) incl += v;
-            v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
-            if (t >= 2) incl += v;
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 3, 4);
-            uint32_t rank = run + incl - mine;
-            run += total;
+            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            uint32_t rank = run + (h ? other : 0u);
+            run += mine + other;
             if (mine) {
                 const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
-                const uint8_t *lb = o + 16 * t;
+                const uint8_t *lb = o + 32 * h;
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    uint32_t m = g == 0 ? e0 : e1;
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
                     while (m) {
-                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 16
+                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
                         m &= m - 1;
                         uint16_t w16 = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
                         if (rank < nesc) {
@@ -550,7 +582,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                             w16 = (uint16_t)(((lit & 0x80u) << 8) | (ex << 7) | (lit & 0x7Fu));
                         }
                         *reinterpret_cast<uint16_t *>(
-                            rowp + (((((uint32_t)(2 * t) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1))) = w16;
+                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1))) = w16;
                         ++rank;
                     }
                 }
@@ -575,7 +607,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
             int32_t t, w0, w1;
             R.piece(pi, t, w0, w1);
             const int b = pi & 1;
-            if (ok && !mbar_wait(&acc_full[b], (uint32_t)((pi >> 1) & 1), a.err, kErrWaitFull)) ok = false;
+            if (ok) {  // a long wait: lane 0 polls with a backoff, the others idle at the warp barrier
+                int got = 1;
+                if (lane == 0) got = mbar_wait_backoff(&acc_full[b], (uint32_t)((pi >> 1) & 1), a.err, kErrWaitFull);
+                ok = __shfl_sync(0xffffffffu, got, 0) != 0;
+            }
             tmem_fence_after();
             const bool whole = w0 == 0 && w1 == a.nwin;
             const int64_t row = (int64_t)(t / a.ntok) * kPfRows + qtr * 32 + lane;
@@ -668,21 +704,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         }
     } else {
         // ---------------------------------------------------------- MMA --
-        bool ok = true;
-        int32_t j = 0;
-        for (int32_t pi = 0; pi < R.n; ++pi) {
-            int32_t t, w0, w1;
-            R.piece(pi, t, w0, w1);
-            const int b = pi & 1;
-            if (pi >= 2 && ok && !mbar_wait(&acc_empty[b], (uint32_t)(((pi >> 1) - 1) & 1), a.err, kErrWaitEmpty))
-                ok = false;
-            tmem_fence_after();
-            for (int32_t w = w0; w < w1; ++w, ++j) {
-                const int sx = j % kXStages, sw = j % kWStages;
-                if (ok && !mbar_wait(&x_full[sx], (uint32_t)((j / kXStages) & 1), a.err, kErrWaitFull)) ok = false;
-                if (ok && !mbar_wait(&w_full[sw], (uint32_t)((j / kWStages) & 1), a.err, kErrWaitFull)) ok = false;
+        // lane 0 alone waits and issues (the other lanes idle at the warp
+        // barrier instead of polling the barriers with it)
+        if (lane == 0) {
+            bool ok = true;
+            int32_t j = 0;
+            for (int32_t pi = 0; pi < R.n; ++pi) {
+                int32_t t, w0, w1;
+                R.piece(pi, t, w0, w1);
+                const int b = pi & 1;
+                if (pi >= 2 && ok && !mbar_wait(&acc_empty[b], (uint32_t)(((pi >> 1) - 1) & 1), a.err, kErrWaitEmpty))
+                    ok = false;
                 tmem_fence_after();
-                if (lane == 0) {
+                for (int32_t w = w0; w < w1; ++w, ++j) {
+                    const int sx = j % kXStages, sw = j % kWStages;
+                    if (ok && !mbar_wait(&x_full[sx], (uint32_t)((j / kXStages) & 1), a.err, kErrWaitFull)) ok = false;
+                    if (ok && !mbar_wait(&w_full[sw], (uint32_t)((j / kWStages) & 1), a.err, kErrWaitFull)) ok = false;
+                    tmem_fence_after();
                     if (ok) {
                         const uint32_t wb = smem_addr(ws + sw * kWStage), xb = smem_addr(xs + sx * kXStage);
 #pragma unroll
@@ -693,15 +731,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                     umma_commit(&w_empty[sw]);  // frees the stages once these MMAs have read them
                     umma_commit(&x_empty[sx]);
                 }
-                __syncwarp();
+                umma_commit(&acc_full[b]);
             }
-            if (lane == 0) umma_commit(&acc_full[b]);
-            __syncwarp();
+            // every MMA issued has completed before the tensor memory is freed
+            umma_commit(drained);
+            mbar_wait(drained, 0u, a.err, kErrWaitDrain);
         }
-        // every MMA issued has completed before the tensor memory is freed
-        if (lane == 0) umma_commit(drained);
         __syncwarp();
-        mbar_wait(drained, 0u, a.err, kErrWaitDrain);
     }
     // every warp: the epilogue's tensor-memory reads done before the free
     tmem_fence_before();
