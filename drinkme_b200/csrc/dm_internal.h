@@ -98,7 +98,8 @@ struct dm_tensor {
     uint8_t *d_data = nullptr;     // unit-major layout + tail pad
     size_t data_bytes = 0;
     uint32_t *d_unit16 = nullptr;  // [units + 1] unit starts in 16-byte units
-    uint32_t *d_rowdir = nullptr;  // sip: [16-row padded rows][NB][2] stream offset (16-byte units), nesc | part << 16
+    uint32_t *d_rowdir = nullptr;  // sip: [16-row padded rows][NB][2] stream offset (16-byte units),
+                                   // nesc | part << 11 | escape-index offset (16-byte units) << 16
     size_t rowdir_bytes = 0;
     dm::Scratch S;
     dm::LaunchKnobs K;

@@ -454,8 +454,10 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
     });
     if (fast && rowdir) {
         // per row block (16-row padded rows x block columns): the absolute
-        // offset of its streams in 16-byte units, and its escape count with
-        // its part index (the prefill kernel's one-load directory)
+        // offset of its streams in 16-byte units; its escape count (bits
+        // 0-10), part index (bits 11-15) and the offset of its escape index
+        // from the stream start in 16-byte units (bits 16-31) — the prefill
+        // kernel's one-load directory
         const int64_t rows16 = L.tiles * kUnitRows;
         rowdir->assign((size_t)(rows16 * NB) * 8, '\0');
         uint32_t *rd = reinterpret_cast<uint32_t *>(&(*rowdir)[0]);
@@ -466,7 +468,8 @@ int build_layout(const PackPart *parts, int nparts, TensorLayout &L, std::string
                 const int64_t r = tile * kUnitRows + s;
                 const uint32_t part = r < rows ? (uint32_t)rpart[r] : 0u;
                 rd[(r * NB + b) * 2] = (uint32_t)(ustart[u] / 16) + hdr[s].off16;
-                rd[(r * NB + b) * 2 + 1] = (uint32_t)hdr[s].nesc | (part << 16);
+                const uint32_t idx16 = (uint32_t)(a16((int64_t)hdr[s].words * 4) / 16);
+                rd[(r * NB + b) * 2 + 1] = (uint32_t)hdr[s].nesc | ((part & 31u) << 11) | (idx16 << 16);
             }
         });
     }

@@ -10,39 +10,41 @@
 //
 // Design:
 //   * A TILE is 128 weight rows (the MMA's M: the decoded weights are the A
-//     operand) by up to 256 activation rows (the MMA's N: the activations are
-//     the B operand), over the whole K; its fp32 accumulator takes 256 of the
-//     CTA's 512 tensor-memory columns, so two accumulators alternate and one
-//     tile's epilogue runs under the next tile's MMAs.
+//     operand) by a GROUP of up to 512 activation rows (the B operand), over
+//     the whole K. A group is one or two HALVES of at most 256 activation rows
+//     (the MMA's N), each with its own 256-column fp32 accumulator in tensor
+//     memory, so every weight window is decoded ONCE for all the group's
+//     activation rows (at M = 512, half the decode work of 256-row tiles).
+//     With one half, the two accumulators alternate between tiles and a
+//     tile's epilogue runs under the next tile's MMAs; with two, the first
+//     half drains while the second half's last MMAs run.
 //   * Persistent stream-K over K windows of 64: one CTA per SM; the windows of
-//     every tile, tile after tile (a weight row tile's activation tiles next to
-//     each other, so its compressed bytes come from L2 the second time), are
-//     split evenly over the CTAs. A CTA's first and last tiles may be shared
-//     with its neighbours (PIECES); it runs those first. A piece's fp32
-//     partial goes to the workspace, and for each quarter of the tile's rows
-//     the last piece to arrive (an acquire-release counter) adds every
-//     piece's partial in CTA order and writes the outputs.
-//   * Warps 0-7 decode: a lane pair per weight row, lane h taking weights
-//     [32h, 32h + 32) of each window, from the loader's code planes with the
-//     GEMV's byte-parallel table lookups (escaped weights come out as sign |
-//     0 | mantissa), into the 128-byte-swizzled K-major tile the tensor core
-//     reads. An escaped weight's terminal exponent is its rank among the row
-//     block's escapes: the lane pair counts code-7 nibbles as it goes and
-//     rewrites each escaped weight whole from its literal byte and the row's
-//     terminal stream, staged per block column in shared memory. The
-//     compressed operands of the next four windows are staged by cp.async
-//     into a shared-memory ring (the lanes hold no loads in flight, so the
-//     per-window barrier release and proxy fence never wait for them); the
-//     row-block directory entry of the next block column is prefetched a
-//     block column ahead.
-//   * Warp 12 loads each activation window with one TMA tensor copy (no
-//     multicast) in the same swizzled layout; lane 0 of warp 13 owns the MMA
-//     issue (kind::f16, M = 128, N = tokens, K = 16) and commits each window
-//     to the barriers that free its stages; warp 13 owns the tensor memory.
-//   * Warps 8-11 read the accumulators (tcgen05.ld, a lane per weight row),
+//     every tile, tile after tile (a weight row tile's groups next to each
+//     other, so its compressed bytes come from L2 the second time), are split
+//     evenly over the CTAs. A CTA's first and last tiles may be shared with
+//     its neighbours (PIECES); it runs those first. Per quarter of a shared
+//     tile's rows, the pieces count their arrivals; every piece but the last
+//     writes its fp32 partial and marks it ready, and the last adds the
+//     others' partials and its own accumulator in CTA order (deterministic)
+//     straight from tensor memory to the outputs.
+//   * Warps 0-15 decode: four lanes per weight row (lane t takes weights
+//     [16t, 16t + 16) of every window), from the loader's code planes with
+//     the GEMV's byte-parallel table lookups (an escape, code 7, decodes to
+//     +0), into the 128-byte-swizzled K-major tile the tensor core reads. The
+//     escaped weights are then rewritten whole from the loader's escape
+//     index (their positions) and the row's terminal stream (their
+//     exponents, by rank): a row's four lanes share its window's escapes, no
+//     bit scans. The compressed operands of the next four windows are staged
+//     by cp.async into a shared-memory ring (literal plane, code words, bit-2
+//     words), so no lane waits on a load of its own in flight.
+//   * Warp 20 loads each activation window (one TMA tensor copy per half, no
+//     multicast) in the same swizzled layout; lane 0 of warp 21 owns the MMA
+//     issue (kind::f16, M = 128, N = half width, K = 16) and commits each
+//     window to the barriers that free its stages; warp 21 owns the tensor
+//     memory.
+//   * Warps 16-19 read the accumulators (tcgen05.ld, a lane per weight row),
 //     add the bias in fp32, round once and store; or write a piece's partial
-//     (activation-row major, so a warp's store is one 128-byte line). Only one
-//     lane of a warp polls a barrier.
+//     (activation-row major, so a warp's store is one 128-byte line).
 //   * Every wait is bounded (the device error word records a wait that gave
 //     up); the tensor memory is freed on every path.
 #include <cuda.h>
@@ -60,35 +62,28 @@ namespace dm {
 
 namespace {
 
-constexpr int kPfRows = 128;      // weight rows per tile (MMA M)
-constexpr int kPfTokMax = 256;    // activation rows per tile, at most (MMA N)
-constexpr int kXStages = 3;       // activation windows in flight
-constexpr int kWStages = 3;       // decoded weight windows in flight
-constexpr int kPfDecWarps = 8;    // a lane pair per weight row, 16 rows per warp
-constexpr int kPfEpi0 = 8;        // warps 8-11: the epilogue (tensor-memory lane quarters 0-3)
-constexpr int kPfProd = 12;       // warp 12: activation TMA
-constexpr int kPfMma = 13;        // warp 13: tensor memory and MMA issue
-constexpr int kPfThreads = 14 * 32;
-constexpr int kAhead = 4;         // windows of compressed operands in flight (a cp.async ring)
-constexpr int kOpRow = 96;        // per row and window: 64 literal bytes, 4 code words, 2 bit-2 words
-constexpr int kOpStage = kPfRows * kOpRow;
+constexpr int kPfRows = 128;       // weight rows per tile (MMA M)
+constexpr int kHalfMax = 256;      // activation rows per half, at most (MMA N)
+constexpr int kGroupMax = 512;     // activation rows per group (two halves)
+constexpr int kWStages = 3;        // decoded weight windows in flight
+constexpr int kMaxXStages = 6;     // activation half-windows in flight, at most
+constexpr int kDecWarps = 16;      // eight weight rows per warp, four lanes per row
+constexpr int kEpi0 = 16;          // warps 16-19: the epilogue (tensor-memory lane quarters 0-3)
+constexpr int kProd = 20;          // warp 20: activation TMA
+constexpr int kMma = 21;           // warp 21: tensor memory and MMA issue
+constexpr int kPfThreads = 22 * 32;
+constexpr int kAhead = 4;          // windows of compressed operands in flight (a cp.async ring)
+constexpr int kLitStage = kPfRows * 64;   // literal plane: 64 bytes per row and window
+constexpr int kCodeStage = kPfRows * 16;  // low-two-bit code words: four per row and window
+constexpr int kBitStage = kPfRows * 8;    // bit-2 words: two per row and window
+constexpr int kOpStage = kLitStage + kCodeStage + kBitStage;
 constexpr int kWStage = kPfRows * 128;    // 16 KB: 128 rows x 64 bf16
-constexpr int kXStage = kPfTokMax * 128;  // 32 KB: 256 rows x 64 bf16
-constexpr int kTermRing = 4;              // block columns of staged terminal bytes
-constexpr int kTermRow = 64;              // terminal bytes staged per row (the rest read from HBM)
-constexpr int kTermStage = kPfRows * kTermRow;
 constexpr int kAccCols = 256;             // tensor-memory columns per accumulator
 constexpr int kMaxParts = 8;
-
-constexpr int kOffX = 0;
-constexpr int kOffW = kOffX + kXStages * kXStage;
-constexpr int kOffOp = kOffW + kWStages * kWStage;
-constexpr int kOffTerm = kOffOp + kAhead * kOpStage;
-constexpr int kOffBar = kOffTerm + kTermRing * kTermStage;
-constexpr int kNumBars = 2 * kXStages + 2 * kWStages + 5;
-constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr int kOffTabs = kOffTmem + 16;
-constexpr int kSmemBytes = kOffTabs + kMaxParts * 16 + 1024;  // + alignment slack
+constexpr int kNumBars = 2 * kMaxXStages + 2 * kWStages + 5;
+constexpr int kFixedSmem = kWStages * kWStage + kAhead * kOpStage + kNumBars * 8 + 16 + kMaxParts * 16 + 80;
+constexpr int kSmemLimit = 232448;        // the per-block opt-in maximum of sm_100
+constexpr int kXBudget = kSmemLimit - 1024 - kFixedSmem;
 
 // Shared-memory matrix descriptor of a 128-byte-swizzled K-major tile whose
 // 8-row groups are 1024 bytes apart (rows 128 bytes): start address,
@@ -135,7 +130,7 @@ __device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 // mbar_wait for a wait expected to be long: a try without a time hint, then a
-// 256 ns sleep between tries (about 2^16 tries: tens of milliseconds), so the
+// 256 ns sleep between tries (about 2^18 tries: tens of milliseconds), so the
 // waiting lane takes almost no issue slots or shared-memory bandwidth.
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, int *err, int code) {
     for (uint32_t i = 0; i < (1u << 18); ++i) {
@@ -161,15 +156,12 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// 16 bytes global -> shared, asynchronously (the LDGSTS path, L2 only).
+// global -> shared, asynchronously (the LDGSTS path)
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async8(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Waits until at most `n` (0..3) of this thread's newest groups are pending.
@@ -184,16 +176,22 @@ __device__ __forceinline__ void cp_async_wait(int n) {
         asm volatile("cp.async.wait_group 3;" ::: "memory");
 }
 
-// The selectors of 16 codes (quarter t of a 64-weight window) from a row
-// block's code planes: v = its low-two-bit word, P = its bit-2 word (the
-// GEMV's code_selectors).
+// A release increment of a counter another CTA acquires.
+__device__ __forceinline__ void red_add_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The selectors of 16 codes (one quarter of a 64-weight window) from a row
+// block's code planes: v = the quarter's low-two-bit word, P = the bit-2 word
+// it shares with its neighbour, rotated by (rl, rh) = (2, 1) for an even
+// quarter and (0, 31) for an odd one (the GEMV's code_selectors).
 __device__ __forceinline__ void selectors16(uint32_t v, uint32_t P, uint32_t rl, uint32_t rh, uint32_t &s0,
                                             uint32_t &s1) {
     s0 = (v & 0x33333333u) | (__funnelshift_l(P, P, rl) & 0x44444444u);
     s1 = ((v >> 2) & 0x33333333u) | (__funnelshift_l(P, P, rh) & 0x44444444u);
 }
 
-// Four weights -> two bf16 pairs (the GEMV's decode4).
+// Four weights -> two bf16 pairs (the GEMV's decode4); code 7 gives +0.
 __device__ __forceinline__ void dec4(uint32_t L, uint32_t S, uint32_t th0, uint32_t th1, uint32_t tl0, uint32_t tl1,
                                      uint32_t &p01, uint32_t &p23) {
     const uint32_t eh = __byte_perm(th0, th1, S);
@@ -204,30 +202,37 @@ __device__ __forceinline__ void dec4(uint32_t L, uint32_t S, uint32_t th0, uint3
     p23 = __byte_perm(lo, hi, 0x7362);
 }
 
-// Bit 4i set where nibble i of a selector word holds code 7 (an escape).
-__device__ __forceinline__ uint32_t escape_nibbles(uint32_t s) { return s & (s >> 1) & (s >> 2) & 0x11111111u; }
+// Escapes (code 7) among the eight codes of a selector word: bit 4i is set
+// where nibble i holds 7; the multiply gathers the eight bits into the top
+// nibble (at most 8), which keeps the count off the XU pipe.
+__device__ __forceinline__ uint32_t escapes8(uint32_t s) {
+    return ((s & (s >> 1) & (s >> 2) & 0x11111111u) * 0x11111111u) >> 28;
+}
 
 struct PfArgs {
     const uint8_t *data;
-    const uint2 *rowdir;     // [16-row padded rows][NB]: stream offset (16-byte units), nesc | part << 16
+    const uint2 *rowdir;     // [16-row padded rows][NB]: stream offset (16-byte units),
+                             // nesc | part << 11 | escape-index offset (16-byte units) << 16
     int64_t rows, NB;
-    int32_t M, ntok, ntt;    // real activation rows, activation tiles, activation rows per tile (MMA N)
-    int32_t nparts;
-    int64_t ntiles, W;       // tiles (row tiles x activation tiles), all windows
+    int32_t M, ngrp, nt, nh; // real activation rows, groups, rows per half (MMA N), halves per group
+    int64_t ntiles, W;       // tiles (row tiles x groups), all windows
     int32_t nwin;            // windows per tile
+    int32_t nxs;             // activation stages
     uint32_t idesc;
     const uint16_t *bias;
     void *out;               // [M][rows]
     int32_t out_f32;
-    float *part;             // [grid][2][128][ntt]: a CTA's partials of its first / last tile
-    int *counters;           // [ntiles][4], zero on entry
+    float *part;             // [grid][2][nh * nt][128]: a CTA's partials of its first / last tile
+    uint32_t *counters;      // [ntiles][8]: per row quarter, arrivals then ready partials; zero on entry
     int *err;
     uint32_t tabs[kMaxParts][4];
 };
 
 // The CTA's windows [x0, x1) of the whole sequence (tile-major), as PIECES:
-// its first tile when partial, its last tile when partial, then its whole
-// tiles in order.
+// its first tile when partial, its whole tiles in order, then its last tile
+// when partial. The last piece is the CTA's last work, so when it is the
+// last of its tile's pieces to finish, its accumulator is still in tensor
+// memory for the tile's fixup at the CTA's end.
 struct Range {
     int64_t x0, x1;
     int32_t tA, tB, nwin;
@@ -267,18 +272,17 @@ struct Range {
             }
             --i;
         }
-        if (pB) {
-            if (i == 0) {
-                t = tB;
-                w0 = 0;
-                w1 = (int32_t)(x1 - (int64_t)tB * nwin);
-                return;
-            }
-            --i;
+        const int32_t first = pA ? tA + 1 : tA;
+        const int32_t nwhole = (pB ? tB : tB + 1) - first;
+        if (i < nwhole) {
+            t = first + i;
+            w0 = 0;
+            w1 = nwin;
+            return;
         }
-        t = (pA ? tA + 1 : tA) + i;
+        t = tB;
         w0 = 0;
-        w1 = nwin;
+        w1 = (int32_t)(x1 - (int64_t)tB * nwin);
     }
 };
 
@@ -297,38 +301,25 @@ __device__ __forceinline__ int64_t owner_of(int64_t x, int64_t G, int64_t W) {
 struct Cursor {
     int32_t pi, w, w1, t, rt;
     bool done;
-    __device__ void at_piece(const Range &R, int32_t ntok) {
-        R.piece(pi, t, w, w1);
-        rt = t / ntok;
+    __device__ void at_piece(const Range &R, int32_t ngrp) {
+        int32_t w0;
+        R.piece(pi, t, w0, w1);
+        w = w0;
+        rt = t / ngrp;
     }
-    __device__ void begin(const Range &R, int32_t ntok) {
+    __device__ void begin(const Range &R, int32_t ngrp) {
         pi = 0;
         done = R.n == 0;
         t = rt = w = w1 = 0;
-        if (!done) at_piece(R, ntok);
+        if (!done) at_piece(R, ngrp);
     }
-    __device__ void next(const Range &R, int32_t ntok) {
+    __device__ void next(const Range &R, int32_t ngrp) {
         if (++w < w1) return;
         if (++pi >= R.n) {
             done = true;
             return;
         }
-        at_piece(R, ntok);
-    }
-    // the first window (and its weight row tile) of the next block column
-    // (segment) after this one
-    __device__ bool next_segment(const Range &R, int32_t ntok, int32_t &rt2, int32_t &w2) const {
-        const int32_t e = ((w >> 4) + 1) << 4;
-        if (e < w1) {
-            rt2 = rt;
-            w2 = e;
-            return true;
-        }
-        if (pi + 1 >= R.n) return false;
-        int32_t t2, x;
-        R.piece(pi + 1, t2, w2, x);
-        rt2 = t2 / ntok;
-        return true;
+        at_piece(R, ngrp);
     }
 };
 
@@ -336,27 +327,32 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned tiles (the swizzle pattern follows address bits 7-9)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *xs = smem + kOffX;
-    uint8_t *ws = smem + kOffW;
-    uint8_t *ops = smem + kOffOp;     // [kAhead][128 rows][kOpRow]: compressed operands in flight
-    uint8_t *term = smem + kOffTerm;  // [kTermRing][128 rows][64 bytes]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
-    uint64_t *x_full = bar, *x_empty = bar + kXStages, *w_full = bar + 2 * kXStages, *w_empty = w_full + kWStages;
+    const uint32_t xstage = (uint32_t)a.nt * 128u;  // one half of an activation window
+    uint8_t *xs = smem;
+    uint8_t *ws = xs + (size_t)a.nxs * xstage;
+    uint8_t *ops = ws + kWStages * kWStage;  // [kAhead] x {literals [128][64], code words [128][16], bit-2 words [128][8]}
+    uint64_t *bar = reinterpret_cast<uint64_t *>(ops + kAhead * kOpStage);
+    uint64_t *x_full = bar, *x_empty = bar + kMaxXStages, *w_full = bar + 2 * kMaxXStages, *w_empty = w_full + kWStages;
     uint64_t *acc_full = w_empty + kWStages, *acc_empty = acc_full + 2, *drained = acc_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffTmem);
-    uint32_t *tabs = reinterpret_cast<uint32_t *>(smem + kOffTabs);  // [kMaxParts][4]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + kNumBars);
+    uint32_t *tabs = tmem_slot + 4;  // [kMaxParts][4]
+    // the shared tiles whose fixup this CTA runs at its end, per row quarter
+    // (at most two: its first and last tiles): tile, and whether its own sum
+    // is still in tensor memory
+    int32_t *fix_n = reinterpret_cast<int32_t *>(tabs + kMaxParts * 4);  // [4]
+    int32_t *fix_t = fix_n + 4, *fix_own = fix_t + 8;                       // [4][2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t G = gridDim.x;
     Range R;
     R.init(blockIdx.x, G, a.W, a.nwin);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kXStages; ++s) {
+        for (int s = 0; s < kMaxXStages; ++s) {
             mbar_init(&x_full[s], 1);
             mbar_init(&x_empty[s], 1);
         }
         for (int s = 0; s < kWStages; ++s) {
-            mbar_init(&w_full[s], kPfDecWarps);
+            mbar_init(&w_full[s], kDecWarps);
             mbar_init(&w_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -365,9 +361,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         }
         mbar_init(drained, 1);
         mbar_fence_init();
+        for (int q = 0; q < 4; ++q) fix_n[q] = 0;
     }
-    if (warp == kPfProd && lane < kMaxParts * 4) tabs[lane] = (&a.tabs[0][0])[lane];
-    if (warp == kPfMma) {
+    if (warp == kProd && lane < kMaxParts * 4) tabs[lane] = (&a.tabs[0][0])[lane];
+    if (warp == kMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(2 * kAccCols)
                      : "memory");
@@ -379,71 +376,50 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
     const uint32_t tmem = *tmem_slot;
     const int64_t NB = a.NB;
 
-    if (warp < kPfDecWarps) {
+    if (warp < kDecWarps) {
         // ------------------------------------------------------ decode --
-        // a lane pair per weight row; lane h decodes weights [32h, 32h + 32)
-        // of every window (the GEMV's quarters 2h and 2h + 1 of a quad)
-        const int r = warp * 16 + (lane >> 1);
-        const int h = lane & 1;
+        // row r of the tile; lane t of the row's four decodes weights
+        // [16t, 16t + 16) of every window
+        const int tq = lane & 3;
+        const int r = warp * 8 + (lane >> 2);
         const uint32_t sw = (uint32_t)(r & 7);
+        const uint32_t st0 = (uint32_t)r * 128u + (((uint32_t)(2 * tq) ^ sw) << 4);
+        const uint32_t st1 = (uint32_t)r * 128u + (((uint32_t)(2 * tq + 1) ^ sw) << 4);
+        const uint32_t rl = (tq & 1) ? 0u : 2u, rh = (tq & 1) ? 31u : 1u;
+        const uint32_t lit_at = (uint32_t)r * 64u + 16u * tq;
+        const uint32_t code_at = kLitStage + (uint32_t)r * 16u + 4u * tq;
+        const uint32_t bit_at = kLitStage + kCodeStage + (uint32_t)r * 8u + 4u * (tq >> 1);
         bool ok = true;
-        // the load cursor runs kAhead windows before the decode position,
-        // staging each window's compressed operands by cp.async into ring
-        // slot (window mod kAhead) of this row: nothing the decoder waits on
-        // is a load in flight of its own (a release or a proxy fence would
-        // wait for those)
+        // the load cursor runs kAhead windows before the decode position; a
+        // window's compressed operands go to ring slot (window mod kAhead):
+        // lane t its 16 literal bytes, lane 0 the row's four code words, lane
+        // 1 its two bit-2 words; one cp.async group per window
         Cursor cl;
-        cl.begin(R, a.ntok);
-        // segments the load cursor has entered; the ring of staged terminal
-        // bytes has kTermRing slots, and the load cursor is at most three
-        // segment starts ahead of the decode position (within kAhead = 4
-        // windows: a piece start, the next piece's start, one block column
-        // boundary), so no slot is overwritten while in use
-        int32_t seg_load = -1;
-        int32_t seg_t = -1, seg_bc = -1;
-        uint2 dir_cur = make_uint2(0, 0), dir_next = make_uint2(0, 0);
-        bool has_next = false;
-        int32_t nxt_rt = 0, nxt_w = 0;
+        cl.begin(R, a.ngrp);
+        int32_t lseg_t = -1, lseg_bc = -1;
+        uint32_t lbase16 = 0;
+        bool lreal = false;
+        int32_t nload = 0;
         auto dir_load = [&](int32_t rt, int32_t bc) -> uint2 {
             const int64_t row = (int64_t)rt * kPfRows + r;
             if (row >= a.rows) return make_uint2(0, 0);
             return __ldg(a.rowdir + row * NB + bc);
         };
-        // the load cursor's window into ring slot `nload` mod kAhead: a new
-        // segment takes the prefetched directory entry, prefetches the next
-        // one and stages its terminal bytes (lane h: bytes [32h, 32h + 32));
-        // one cp.async group per window. Per row and window the slot holds
-        // the 64 literal bytes, the four code-plane words and the two bit-2
-        // words.
-        int32_t nload = 0;  // windows the load cursor has issued
         auto load_window = [&]() {
             const int32_t bc = cl.w >> 4;
-            const bool exists = (int64_t)cl.rt * kPfRows + r < a.rows;
-            if (cl.t != seg_t || bc != seg_bc) {
-                if (has_next && nxt_rt == cl.rt && (nxt_w >> 4) == bc)
-                    dir_cur = dir_next;
-                else
-                    dir_cur = dir_load(cl.rt, bc);
-                has_next = cl.next_segment(R, a.ntok, nxt_rt, nxt_w);
-                if (has_next) dir_next = dir_load(nxt_rt, nxt_w >> 4);
-                ++seg_load;
-                seg_t = cl.t;
-                seg_bc = bc;
-                if (exists) {
-                    uint8_t *dst = term + (seg_load & (kTermRing - 1)) * kTermStage + r * kTermRow + 32 * h;
-                    const uint8_t *src = a.data + (size_t)dir_cur.x * 16 + 1408 + 32 * h;
-                    cp_async16(dst, src);
-                    cp_async16(dst + 16, src + 16);
-                }
+            if (cl.t != lseg_t || bc != lseg_bc) {
+                lseg_t = cl.t;
+                lseg_bc = bc;
+                lreal = (int64_t)cl.rt * kPfRows + r < a.rows;
+                lbase16 = dir_load(cl.rt, bc).x;
             }
-            if (exists) {
-                const int q = cl.w & 15;
-                const uint8_t *lit = a.data + (size_t)dir_cur.x * 16;
-                uint8_t *o = ops + (nload % kAhead) * kOpStage + r * kOpRow;
-                cp_async16(o + 32 * h, lit + 64 * q + 32 * h);
-                cp_async16(o + 32 * h + 16, lit + 64 * q + 32 * h + 16);
-                cp_async8(o + 64 + 8 * h, lit + 1024 + 16 * q + 8 * h);
-                cp_async4(o + 80 + 4 * h, lit + 1024 + 256 + 8 * q + 4 * h);
+            if (lreal) {
+                const uint32_t q = (uint32_t)(cl.w & 15);
+                const uint8_t *blk = a.data + (size_t)lbase16 * 16;
+                uint8_t *o = ops + (nload % kAhead) * kOpStage;
+                cp_async16(o + lit_at, blk + 64 * q + 16 * tq);
+                if (tq == 0) cp_async16(o + kLitStage + r * 16, blk + 1024 + 16 * q);
+                if (tq == 1) cp_async8(o + kLitStage + kCodeStage + r * 8, blk + 1280 + 8 * q);
             }
             cp_async_commit();
             ++nload;
@@ -451,67 +427,50 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
 #pragma unroll 1
         for (int i = 0; i < kAhead && !cl.done; ++i) {
             load_window();
-            cl.next(R, a.ntok);
+            cl.next(R, a.ngrp);
         }
-        int32_t seg_dec = -1;  // segment of the decode position
-        uint32_t run = 0;      // escapes of this row block before the current window
-        int32_t j = 0;         // window sequence number (its stage)
+        uint32_t run = 0;  // escapes of this row block before the current window
+        int32_t j = 0;     // window sequence number (its stage)
         Cursor cd;
-        cd.begin(R, a.ntok);
+        cd.begin(R, a.ngrp);
         int32_t dseg_t = -1, dseg_bc = -1;
-        uint2 dir = make_uint2(0, 0);  // the decode position's row block: stream offset, nesc | part << 16
-        bool real = false;             // its row exists
-        // decode window j (ring slot j mod kAhead), then load the window
-        // kAhead ahead into the slot it frees
+        const uint8_t *blk = a.data;  // the decode position's row block
+        const uint16_t *eidx = nullptr;
+        uint32_t nesc = 0;
+        bool real = false;
+        uint32_t th0 = 0, th1 = 0, tl0 = 0, tl1 = 0;
         while (!cd.done) {
             const int32_t bc = cd.w >> 4;
             if (cd.t != dseg_t || bc != dseg_bc) {
-                ++seg_dec;
                 dseg_t = cd.t;
                 dseg_bc = bc;
                 run = 0;
                 real = (int64_t)cd.rt * kPfRows + r < a.rows;
-                dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
-                // a piece that starts inside a block column: the escapes of
-                // the block's earlier windows come before this window's ranks;
-                // lane h counts whole windows h, h + 2, ... below q0, two
-                // windows' loads at a time
-                const int q0 = cd.w & 15;
+                const uint2 dir = dir_load(cd.rt, bc);  // an L1 hit: the load cursor read it a few windows ago
+                blk = a.data + (size_t)dir.x * 16;
+                nesc = dir.y & 0x7FFu;
+                eidx = reinterpret_cast<const uint16_t *>(blk + (size_t)(dir.y >> 16) * 16);
+                const uint32_t part = (dir.y >> 11) & 31u;
+                const uint32_t *tb = tabs + 4 * (part < kMaxParts ? part : 0);
+                th0 = tb[0];
+                th1 = tb[1] & 0x00FFFFFFu;
+                tl0 = tb[2];
+                tl1 = tb[3] & 0x00FFFFFFu;
+                // a piece that starts inside a block column: the block's
+                // escapes before this window come first in rank (the escape
+                // index is in block order)
+                const uint32_t q0 = (uint32_t)(cd.w & 15);
                 if (q0 > 0) {
                     uint32_t pre = 0;
-                    if (real) {
-                        const uint8_t *cb = a.data + (size_t)dir.x * 16 + 1024;
-                        for (int base = h; base < q0; base += 4) {
-                            uint4 cw[2];
-                            uint2 pw[2];
-#pragma unroll
-                            for (int i = 0; i < 2; ++i) {
-                                const int qq = base + 2 * i;
-                                if (qq < q0) {
-                                    cw[i] = __ldg(reinterpret_cast<const uint4 *>(cb + 16 * qq));
-                                    pw[i] = __ldg(reinterpret_cast<const uint2 *>(cb + 256 + 8 * qq));
-                                }
-                            }
-#pragma unroll
-                            for (int i = 0; i < 2; ++i) {
-                                if (base + 2 * i < q0) {
-                                    uint32_t s0, s1, s2, s3;
-                                    selectors16(cw[i].x, pw[i].x, 2u, 1u, s0, s1);
-                                    selectors16(cw[i].y, pw[i].x, 0u, 31u, s2, s3);
-                                    pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
-                                           __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
-                                    selectors16(cw[i].z, pw[i].y, 2u, 1u, s0, s1);
-                                    selectors16(cw[i].w, pw[i].y, 0u, 31u, s2, s3);
-                                    pre += __popc(escape_nibbles(s0)) + __popc(escape_nibbles(s1)) +
-                                           __popc(escape_nibbles(s2)) + __popc(escape_nibbles(s3));
-                                }
-                            }
-                        }
-                    }
-                    run = pre + __shfl_xor_sync(0xffffffffu, pre, 1);
+                    if (real)
+                        for (uint32_t i = tq; i < nesc; i += 4) pre += __ldg(eidx + i) < 64u * q0 ? 1u : 0u;
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 1);
+                    pre += __shfl_xor_sync(0xffffffffu, pre, 2);
+                    run = pre;
                 }
             }
-            // this window's group (and, at a segment start, its terminals) landed
+            // this window's group landed (every lane's: the escape rewrite
+            // reads literal bytes another lane staged)
             cp_async_wait(nload - j - 1);
             __syncwarp();
             const int s = j % kWStages, use = j / kWStages;
@@ -520,116 +479,120 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                 if (lane == 0) got = mbar_wait(&w_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty);
                 ok = __shfl_sync(0xffffffffu, got, 0) != 0;
             }
-            uint8_t *rowp = ws + s * kWStage + r * 128;
-            const uint8_t *o = ops + (j % kAhead) * kOpStage + r * kOpRow;
-            const uint32_t part = dir.y >> 16;
-            const uint32_t nesc = dir.y & 0xFFFFu;
-            const uint32_t *tb = tabs + 4 * (part < kMaxParts ? part : 0);
-            // code 7 decodes to sign | exponent 0 | mantissa; escaped weights
-            // are rewritten whole below
-            const uint32_t th0 = tb[0], th1 = tb[1] & 0x00FFFFFFu, tl0 = tb[2], tl1 = tb[3] & 0x00FFFFFFu;
-            uint32_t p[16];
-            uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+            uint8_t *wst = ws + s * kWStage;
+            const uint8_t *o = ops + (j % kAhead) * kOpStage;
+            uint32_t tot = 0;
             if (real) {
-                const uint4 L0 = *reinterpret_cast<const uint4 *>(o + 32 * h);
-                const uint4 L1 = *reinterpret_cast<const uint4 *>(o + 32 * h + 16);
-                const uint2 c = *reinterpret_cast<const uint2 *>(o + 64 + 8 * h);
-                const uint32_t P = *reinterpret_cast<const uint32_t *>(o + 80 + 4 * h);
-                uint32_t s0, s1, s2, s3;
-                selectors16(c.x, P, 2u, 1u, s0, s1);   // quarter 2h (even)
-                selectors16(c.y, P, 0u, 31u, s2, s3);  // quarter 2h + 1 (odd)
-                dec4(L0.x, s0, th0, th1, tl0, tl1, p[0], p[1]);
-                dec4(L0.y, s0 >> 16, th0, th1, tl0, tl1, p[2], p[3]);
-                dec4(L0.z, s1, th0, th1, tl0, tl1, p[4], p[5]);
-                dec4(L0.w, s1 >> 16, th0, th1, tl0, tl1, p[6], p[7]);
-                dec4(L1.x, s2, th0, th1, tl0, tl1, p[8], p[9]);
-                dec4(L1.y, s2 >> 16, th0, th1, tl0, tl1, p[10], p[11]);
-                dec4(L1.z, s3, th0, th1, tl0, tl1, p[12], p[13]);
-                dec4(L1.w, s3 >> 16, th0, th1, tl0, tl1, p[14], p[15]);
-                e0 = escape_nibbles(s0);
-                e1 = escape_nibbles(s1);
-                e2 = escape_nibbles(s2);
-                e3 = escape_nibbles(s3);
+                const uint4 L = *reinterpret_cast<const uint4 *>(o + lit_at);
+                const uint32_t v = *reinterpret_cast<const uint32_t *>(o + code_at);
+                const uint32_t P = *reinterpret_cast<const uint32_t *>(o + bit_at);
+                uint32_t s0, s1, p0, p1, p2, p3, p4, p5, p6, p7;
+                selectors16(v, P, rl, rh, s0, s1);
+                dec4(L.x, s0, th0, th1, tl0, tl1, p0, p1);
+                dec4(L.y, s0 >> 16, th0, th1, tl0, tl1, p2, p3);
+                dec4(L.z, s1, th0, th1, tl0, tl1, p4, p5);
+                dec4(L.w, s1 >> 16, th0, th1, tl0, tl1, p6, p7);
+                *reinterpret_cast<uint4 *>(wst + st0) = make_uint4(p0, p1, p2, p3);
+                *reinterpret_cast<uint4 *>(wst + st1) = make_uint4(p4, p5, p6, p7);
+                tot = escapes8(s0) + escapes8(s1);
             } else {
-#pragma unroll
-                for (int k = 0; k < 16; ++k) p[k] = 0u;
+                *reinterpret_cast<uint4 *>(wst + st0) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4 *>(wst + st1) = make_uint4(0u, 0u, 0u, 0u);
             }
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                *reinterpret_cast<uint4 *>(rowp + ((((uint32_t)(4 * h + k)) ^ sw) << 4)) =
-                    make_uint4(p[4 * k], p[4 * k + 1], p[4 * k + 2], p[4 * k + 3]);
-            // escapes: rank among the row block's escapes -> terminal
-            // exponent; the weight is written whole from its literal byte
-            // (independent loads and one store each, no read-modify-write)
-            const uint32_t mine = __popc(e0) + __popc(e1) + __popc(e2) + __popc(e3);
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-            uint32_t rank = run + (h ? other : 0u);
-            run += mine + other;
-            if (mine) {
-                const uint8_t *ts = term + (seg_dec & (kTermRing - 1)) * kTermStage + r * kTermRow;
-                const uint8_t *lb = o + 32 * h;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t m = g == 0 ? e0 : (g == 1 ? e1 : (g == 2 ? e2 : e3));
-                    while (m) {
-                        const uint32_t k = 8u * g + ((uint32_t)(__ffs(m) - 1) >> 2);  // weight of the 32
-                        m &= m - 1;
-                        uint16_t w16 = 0;  // past a truncated terminal stream: +0, as the GEMV decodes it
-                        if (rank < nesc) {
-                            const uint32_t ex = rank < (uint32_t)kTermRow ? ts[rank]
-                                                                          : a.data[(size_t)dir.x * 16 + 1408 + rank];
-                            const uint32_t lit = lb[k];
-                            w16 = (uint16_t)(((lit & 0x80u) << 8) | (ex << 7) | (lit & 0x7Fu));
-                        }
-                        *reinterpret_cast<uint16_t *>(
-                            rowp + (((((uint32_t)(4 * h) + (k >> 3)) ^ sw) << 4) | ((k & 7u) << 1))) = w16;
-                        ++rank;
-                    }
-                }
+            // the row's escapes in this window: ranks [run, run + tot) of the
+            // row block, their positions from the escape index, their
+            // exponents from the terminal stream; lane t takes every fourth.
+            // Ranks at or past nesc (a terminal stream cut short) stay +0.
+            tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+            tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+            __syncwarp();  // the quarters' stores before the rewrites of single weights
+            const uint32_t hi = min(run + tot, nesc);
+            for (uint32_t i = run + tq; i < hi; i += 4) {
+                const uint32_t pos = (uint32_t)__ldg(eidx + i) & 63u;
+                const uint32_t ex = __ldg(blk + 1408 + i);
+                const uint32_t lit = o[r * 64 + pos];
+                *reinterpret_cast<uint16_t *>(wst + (uint32_t)r * 128u + ((((pos >> 3) ^ sw) << 4) | ((pos & 7u) << 1))) =
+                    (uint16_t)(((lit & 0x80u) << 8) | (ex << 7) | (lit & 0x7Fu));
             }
+            run += tot;
             fence_proxy_async_smem();  // these generic writes, before the tensor core's async reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_full[s]);
-            // every lane has read its slot: it takes the window kAhead ahead
+            // every lane has read the ring slot: it takes the window kAhead ahead
             if (!cl.done) {
                 load_window();
-                cl.next(R, a.ntok);
+                cl.next(R, a.ngrp);
             }
-            cd.next(R, a.ntok);
+            cd.next(R, a.ngrp);
             ++j;
         }
         cp_async_wait(0);
-    } else if (warp >= kPfEpi0 && warp < kPfEpi0 + 4) {
+    } else if (warp >= kEpi0 && warp < kEpi0 + 4) {
         // ---------------------------------------------------- epilogue --
-        const int qtr = warp - kPfEpi0;  // tensor-memory lanes 32 qtr .. 32 qtr + 31
+        const int qtr = warp - kEpi0;  // tensor-memory lanes 32 qtr .. 32 qtr + 31
+        const int32_t GT = a.nh * a.nt;
         bool ok = true;
-        for (int32_t pi = 0; pi < R.n; ++pi) {
+        uint32_t uses[2] = {0u, 0u};
+        for (int32_t pi = 0; pi < R.n && ok; ++pi) {
             int32_t t, w0, w1;
             R.piece(pi, t, w0, w1);
-            const int b = pi & 1;
-            if (ok) {  // a long wait: lane 0 polls with a backoff, the others idle at the warp barrier
-                int got = 1;
-                if (lane == 0) got = mbar_wait_backoff(&acc_full[b], (uint32_t)((pi >> 1) & 1), a.err, kErrWaitFull);
-                ok = __shfl_sync(0xffffffffu, got, 0) != 0;
-            }
-            tmem_fence_after();
             const bool whole = w0 == 0 && w1 == a.nwin;
-            const int64_t row = (int64_t)(t / a.ntok) * kPfRows + qtr * 32 + lane;
-            const int32_t tok0 = (t % a.ntok) * a.ntt;
+            const bool final = pi == R.n - 1;
+            const int64_t row = (int64_t)(t / a.ngrp) * kPfRows + qtr * 32 + lane;
+            const int32_t tok0 = (t % a.ngrp) * GT;
             const float bv = (a.bias && row < a.rows) ? bf16_bits_to_f32(a.bias[row]) : 0.f;
-            const int slot = t == R.tA ? 0 : 1;
-            // a piece's partial: [activation row][weight row], so each store of
-            // one activation row by the warp's 32 lanes (rows) is one 128-byte line
-            float *mine = a.part + ((int64_t)blockIdx.x * 2 + slot) * a.ntt * kPfRows + qtr * 32 + lane;
-            for (int32_t c0 = 0; c0 < a.ntt; c0 += 16) {
-                uint32_t v[16];
-                tmem_load16(tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(b * kAccCols + c0), v);
-                if (!ok) continue;
-                if (whole) {
+            uint32_t *arrive = a.counters + t * 8 + qtr;
+            uint32_t np = 1;
+            if (!whole) {
+                const int64_t tw = (int64_t)t * a.nwin;
+                np = (uint32_t)(owner_of(tw + a.nwin - 1, G, a.W) - owner_of(tw, G, a.W) + 1);
+            }
+            // a piece's partial: [row quarter][activation row / 4][32 rows][4],
+            // so a warp's float4 store of four activation rows is 512
+            // consecutive bytes
+            float *mine = a.part + (((int64_t)blockIdx.x * 2 + (t == R.tA ? 0 : 1)) * 4 + qtr) * GT * 32 + lane * 4;
+            bool keep = false;
+            for (int h = 0; h < a.nh && ok; ++h) {
+                const int slot = a.nh == 2 ? h : (pi & 1);
+                int got = 1;  // a long wait: lane 0 polls with a backoff, the others idle at the warp barrier
+                if (lane == 0) got = mbar_wait_backoff(&acc_full[slot], uses[slot] & 1u, a.err, kErrWaitFull);
+                ok = __shfl_sync(0xffffffffu, got, 0) != 0;
+                ++uses[slot];
+                tmem_fence_after();
+                if (h == 0 && !whole && final) {
+                    // the CTA's last piece of a shared tile: if it is the last
+                    // of the tile's pieces to arrive, its sum stays in tensor
+                    // memory and the CTA adds the others' partials at its end
+                    uint32_t old = 0;
+                    if (lane == 0) old = atom_add_acq_rel_gpu(arrive, 1u);
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                    if (old == np - 1) {
+                        keep = true;
+                        if (lane == 0) {
+                            const int k = fix_n[qtr]++;
+                            fix_t[qtr * 2 + k] = t;
+                            fix_own[qtr * 2 + k] = 1;
+                        }
+                        break;
+                    }
+                }
+                const uint32_t tbase = tmem + ((uint32_t)(qtr * 32) << 16) + (uint32_t)(slot * kAccCols);
+                for (int32_t c0 = 0; ok && c0 < a.nt; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_load16(tbase + (uint32_t)c0, v);
+                    const int32_t tl = h * a.nt + c0;
+                    if (!whole) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            __stcg(reinterpret_cast<float4 *>(mine + (int64_t)(tl / 4 + i) * 128),
+                                   make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+                        continue;
+                    }
                     if (row < a.rows)
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
-                            const int32_t tok = tok0 + c0 + k;
+                            const int32_t tok = tok0 + tl + k;
                             if (tok >= a.M) break;
                             const float y = __uint_as_float(v[k]) + bv;
                             if (a.out_f32)
@@ -637,70 +600,51 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
                             else
                                 reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
                         }
-                } else {
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) __stcg(mine + (int64_t)(c0 + k) * kPfRows, __uint_as_float(v[k]));
                 }
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[slot]);
             }
-            tmem_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[b]);
-            if (whole || !ok) continue;
-            // a shared tile: the last of its pieces to arrive (per row quarter)
-            // adds every piece's partial in CTA order
-            const int64_t tw = (int64_t)t * a.nwin;
-            const int64_t cf = owner_of(tw, G, a.W), cl = owner_of(tw + a.nwin - 1, G, a.W);
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) {
-                const uint32_t old = atom_add_acq_rel_gpu(reinterpret_cast<uint32_t *>(a.counters + t * 4 + qtr), 1u);
-                last = old == (uint32_t)(cl - cf);
-                if (last) a.counters[t * 4 + qtr] = 0;
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) continue;
-            for (int32_t c0 = 0; c0 < a.ntt; c0 += 16) {
-                float acc[16];
-                for (int64_t c = cf; c <= cl; ++c) {
-                    const int sc = t == cta_start(c, G, a.W) / a.nwin ? 0 : 1;
-                    const float *pp = a.part + (c * 2 + sc) * a.ntt * kPfRows + (int64_t)c0 * kPfRows + qtr * 32 + lane;
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const float x = __ldcg(pp + k * kPfRows);
-                        acc[k] = c == cf ? x : acc[k] + x;
+            if (!whole && !keep && ok) {
+                // the partial is written: mark it ready; a piece that is not
+                // the CTA's last counts its arrival only now, and if it is
+                // the tile's last, the CTA runs the tile's fixup at its end
+                __syncwarp();
+                if (lane == 0) {
+                    red_add_release_gpu(arrive + 4, 1u);
+                    if (!final && atom_add_acq_rel_gpu(arrive, 1u) == np - 1) {
+                        const int k = fix_n[qtr]++;
+                        fix_t[qtr * 2 + k] = t;
+                        fix_own[qtr * 2 + k] = 0;
                     }
                 }
-                if (row < a.rows)
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const int32_t tok = tok0 + c0 + k;
-                        if (tok >= a.M) break;
-                        const float y = acc[k] + bv;
-                        if (a.out_f32)
-                            reinterpret_cast<float *>(a.out)[(int64_t)tok * a.rows + row] = y;
-                        else
-                            reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
-                    }
             }
         }
-    } else if (warp == kPfProd) {
+    } else if (warp == kProd) {
         // -------------------------------------------------- activations --
+        // one stage per half window: stage k holds half k mod nh of window
+        // k / nh of the CTA's sequence
         if (lane == 0) {
-            const uint32_t bytes = (uint32_t)a.ntt * 128u;
+            const int32_t GT = a.nh * a.nt;
             bool ok = true;
-            int32_t j = 0;
+            int32_t k = 0;
             Cursor cu;
-            for (cu.begin(R, a.ntok); !cu.done && ok; cu.next(R, a.ntok), ++j) {
-                const int s = j % kXStages, use = j / kXStages;
-                if (use > 0 && !mbar_wait(&x_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) ok = false;
-                if (!ok) break;
-                mbar_arrive_expect_tx(&x_full[s], bytes);
-                tma_load_2d(xs + s * kXStage, &xmap, cu.w * 64, (cu.t - cu.rt * a.ntok) * a.ntt, &x_full[s]);
+            for (cu.begin(R, a.ngrp); !cu.done && ok; cu.next(R, a.ngrp)) {
+                const int32_t y0 = (cu.t - cu.rt * a.ngrp) * GT;
+                for (int h = 0; h < a.nh && ok; ++h, ++k) {
+                    const int s = k % a.nxs, use = k / a.nxs;
+                    if (use > 0 && !mbar_wait(&x_empty[s], (uint32_t)((use - 1) & 1), a.err, kErrWaitEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&x_full[s], xstage);
+                    tma_load_2d(xs + (size_t)s * xstage, &xmap, cu.w * 64, y0 + h * a.nt, &x_full[s]);
+                }
             }
             // every copy issued lands before the CTA exits (the last use of
             // each stage: its phase has completed, or completes now)
-            for (int32_t i = std::max<int32_t>(0, j - kXStages); i < j; ++i)
-                mbar_wait(&x_full[i % kXStages], (uint32_t)((i / kXStages) & 1), a.err, kErrWaitDrain);
+            for (int32_t i = max(0, k - a.nxs); i < k; ++i)
+                mbar_wait(&x_full[i % a.nxs], (uint32_t)((i / a.nxs) & 1), a.err, kErrWaitDrain);
         }
     } else {
         // ---------------------------------------------------------- MMA --
@@ -708,30 +652,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         // barrier instead of polling the barriers with it)
         if (lane == 0) {
             bool ok = true;
-            int32_t j = 0;
+            int32_t j = 0, k = 0;
+            uint32_t uses[2] = {0u, 0u};
             for (int32_t pi = 0; pi < R.n; ++pi) {
                 int32_t t, w0, w1;
                 R.piece(pi, t, w0, w1);
-                const int b = pi & 1;
-                if (pi >= 2 && ok && !mbar_wait(&acc_empty[b], (uint32_t)(((pi >> 1) - 1) & 1), a.err, kErrWaitEmpty))
-                    ok = false;
-                tmem_fence_after();
                 for (int32_t w = w0; w < w1; ++w, ++j) {
-                    const int sx = j % kXStages, sw = j % kWStages;
-                    if (ok && !mbar_wait(&x_full[sx], (uint32_t)((j / kXStages) & 1), a.err, kErrWaitFull)) ok = false;
+                    const int sw = j % kWStages;
                     if (ok && !mbar_wait(&w_full[sw], (uint32_t)((j / kWStages) & 1), a.err, kErrWaitFull)) ok = false;
-                    tmem_fence_after();
-                    if (ok) {
-                        const uint32_t wb = smem_addr(ws + sw * kWStage), xb = smem_addr(xs + sx * kXStage);
+                    const uint32_t wb = smem_addr(ws + sw * kWStage);
+                    for (int h = 0; h < a.nh; ++h, ++k) {
+                        const int slot = a.nh == 2 ? h : (pi & 1);
+                        const int sx = k % a.nxs;
+                        if (ok && !mbar_wait(&x_full[sx], (uint32_t)((k / a.nxs) & 1), a.err, kErrWaitFull)) ok = false;
+                        if (w == w0 && uses[slot] > 0 && ok &&
+                            !mbar_wait(&acc_empty[slot], (uint32_t)((uses[slot] - 1) & 1), a.err, kErrWaitEmpty))
+                            ok = false;
+                        tmem_fence_after();
+                        if (ok) {
+                            const uint32_t xb = smem_addr(xs + (size_t)sx * xstage);
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            umma_bf16(tmem + (uint32_t)(b * kAccCols), sw128_desc(wb + 32 * k), sw128_desc(xb + 32 * k),
-                                      a.idesc, (w > w0 || k > 0) ? 1u : 0u);
+                            for (int kk = 0; kk < 4; ++kk)
+                                umma_bf16(tmem + (uint32_t)(slot * kAccCols), sw128_desc(wb + 32 * kk),
+                                          sw128_desc(xb + 32 * kk), a.idesc, (w > w0 || kk > 0) ? 1u : 0u);
+                        }
+                        umma_commit(&x_empty[sx]);  // frees the half's stage once its MMAs have read it
+                        if (w == w1 - 1) {
+                            umma_commit(&acc_full[slot]);  // this half's accumulator is complete
+                            ++uses[slot];
+                        }
                     }
-                    umma_commit(&w_empty[sw]);  // frees the stages once these MMAs have read them
-                    umma_commit(&x_empty[sx]);
+                    umma_commit(&w_empty[sw]);
                 }
-                umma_commit(&acc_full[b]);
             }
             // every MMA issued has completed before the tensor memory is freed
             umma_commit(drained);
@@ -739,10 +691,85 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_sip_kernel(const __grid
         }
         __syncwarp();
     }
-    // every warp: the epilogue's tensor-memory reads done before the free
+    // every warp: the main loops are done and every MMA has completed
     tmem_fence_before();
     __syncthreads();
-    if (warp == kPfMma) {
+    tmem_fence_after();
+    if (warp < kEpi0 + 4) {
+        // ------------------------------------------------------- fixup --
+        // the shared tiles this CTA arrived last at: the 16 decode warps and
+        // the 4 epilogue warps, five per row quarter (a warp reads only its
+        // own quarter of tensor memory), add every piece's sum in CTA order
+        const int q = warp & 3;
+        const int kq = warp < kEpi0 ? warp >> 2 : 4;
+        const int32_t GT = a.nh * a.nt;
+        for (int k = 0; k < fix_n[q]; ++k) {
+            const int32_t t = fix_t[q * 2 + k];
+            const bool own = fix_own[q * 2 + k] != 0;
+            const int64_t tw = (int64_t)t * a.nwin;
+            const int64_t cf = owner_of(tw, G, a.W), cl = owner_of(tw + a.nwin - 1, G, a.W);
+            const uint32_t need = (uint32_t)(cl - cf + 1) - (own ? 1u : 0u);
+            int got = 1;
+            if (lane == 0) {  // every other piece's partial is written
+                got = 0;
+                for (uint32_t i = 0; i < (1u << 22); ++i) {
+                    if (ld_acquire_gpu(a.counters + t * 8 + 4 + q) >= need) {
+                        got = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                if (!got) atomicExch(a.err, kErrWaitFull);
+            }
+            if (!__shfl_sync(0xffffffffu, got, 0)) continue;
+            const int64_t row = (int64_t)(t / a.ngrp) * kPfRows + q * 32 + lane;
+            const int32_t tok0 = (t % a.ngrp) * GT;
+            const float bv = (a.bias && row < a.rows) ? bf16_bits_to_f32(a.bias[row]) : 0.f;
+            for (int32_t tl = 16 * kq; tl < GT; tl += 80) {
+                const int h = tl / a.nt;
+                const uint32_t col = (uint32_t)((a.nh == 2 ? h : ((R.n - 1) & 1)) * kAccCols + tl % a.nt);
+                float acc[16];
+                for (int64_t c = cf; c <= cl; ++c) {
+                    float v[16];
+                    if (own && c == (int64_t)blockIdx.x) {
+                        uint32_t u[16];
+                        tmem_load16(tmem + ((uint32_t)(q * 32) << 16) + col, u);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(u[i]);
+                    } else {
+                        const int sc = t == cta_start(c, G, a.W) / a.nwin ? 0 : 1;
+                        const float4 *pp = reinterpret_cast<const float4 *>(
+                            a.part + ((c * 2 + sc) * 4 + q) * GT * 32 + (int64_t)(tl / 4) * 128 + lane * 4);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 f = __ldcg(pp + i * 32);
+                            v[4 * i] = f.x;
+                            v[4 * i + 1] = f.y;
+                            v[4 * i + 2] = f.z;
+                            v[4 * i + 3] = f.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) acc[i] = c == cf ? v[i] : acc[i] + v[i];
+                }
+                if (row < a.rows)
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int32_t tok = tok0 + tl + i;
+                        if (tok >= a.M) break;
+                        const float y = acc[i] + bv;
+                        if (a.out_f32)
+                            reinterpret_cast<float *>(a.out)[(int64_t)tok * a.rows + row] = y;
+                        else
+                            reinterpret_cast<uint16_t *>(a.out)[(int64_t)tok * a.rows + row] = f32_to_bf16_bits(y);
+                    }
+            }
+        }
+    }
+    // every warp: the tensor-memory reads done before the free
+    tmem_fence_before();
+    __syncthreads();
+    if (warp == kMma) {
         tmem_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAccCols) : "memory");
     }
@@ -768,24 +795,31 @@ EncodeTiled encode_tiled(std::string &msg) {
     return fn;
 }
 
-// The launch geometry of a prefill over M activation rows.
+// The launch geometry of a prefill over M activation rows: groups of at most
+// 512 activation rows of equal size, one or two halves each (a multiple of 16
+// rows, the tensor-memory loads' width).
 struct PfPlan {
-    int32_t ntt, ntok;
+    int32_t nt, nh, ngrp, nxs;
     int64_t nrt, ntiles, nwin, W, grid;
-    int64_t counter_bytes, part_bytes;
+    int64_t counter_bytes, part_bytes, smem;
 };
 
 PfPlan plan_prefill(const dm_tensor *t, int64_t M) {
     PfPlan P{};
-    P.ntt = (int32_t)std::min<int64_t>(kPfTokMax, (M + 15) / 16 * 16);  // whole 16-column tensor-memory loads
-    P.ntok = (int32_t)((M + P.ntt - 1) / P.ntt);
+    P.ngrp = (int32_t)((M + kGroupMax - 1) / kGroupMax);
+    const int64_t per = (M + P.ngrp - 1) / P.ngrp;
+    P.nh = per > kHalfMax ? 2 : 1;
+    P.nt = (int32_t)(((per + P.nh - 1) / P.nh + 15) / 16 * 16);
+    const int64_t xstage = (int64_t)P.nt * 128;  // one half window
+    P.nxs = (int32_t)std::min<int64_t>(kMaxXStages, kXBudget / xstage);
     P.nrt = (t->L.rows + kPfRows - 1) / kPfRows;
-    P.ntiles = P.nrt * P.ntok;
+    P.ntiles = P.nrt * P.ngrp;
     P.nwin = t->L.NB * 16;
     P.W = P.ntiles * P.nwin;
     P.grid = std::min<int64_t>(t->sms, P.W);
-    P.counter_bytes = (P.ntiles * 4 * (int64_t)sizeof(int) + 255) / 256 * 256;
-    P.part_bytes = P.grid * 2 * kPfRows * P.ntt * (int64_t)sizeof(float);
+    P.counter_bytes = (P.ntiles * 8 * (int64_t)sizeof(uint32_t) + 255) / 256 * 256;
+    P.part_bytes = P.grid * 2 * kPfRows * (int64_t)P.nh * P.nt * (int64_t)sizeof(float);
+    P.smem = 1024 + P.nxs * xstage + kFixedSmem;
     return P;
 }
 
@@ -818,12 +852,16 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
     }
     if (L.units == 0) return DM_OK;
     const PfPlan P = plan_prefill(t, M);
+    if (P.nxs < 2 || P.smem > kSmemLimit) {
+        msg = "dm_prefill: the shared-memory plan does not fit";
+        return DM_EINVAL;
+    }
     EncodeTiled enc = encode_tiled(msg);
     if (!enc) return DM_ECUDA;
     CUtensorMap xmap;
     const cuuint64_t gdim[2] = {(cuuint64_t)L.C, (cuuint64_t)M};
     const cuuint64_t gstride[1] = {(cuuint64_t)L.C * 2};
-    const cuuint32_t box[2] = {64u, (cuuint32_t)P.ntt};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)P.nt};
     const cuuint32_t estride[2] = {1u, 1u};
     CUresult cr = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), gdim, gstride, box, estride,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -836,14 +874,14 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
     static std::atomic<uint64_t> attr{0};
     const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
     if (!dev_bit || !(attr.load() & dev_bit)) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_sip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(prefill_sip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess) {
             msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
             return DM_ECUDA;
         }
         attr.fetch_or(dev_bit);
     }
-    int *counters = reinterpret_cast<int *>(work);
+    uint32_t *counters = reinterpret_cast<uint32_t *>(work);
     cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)P.counter_bytes, (cudaStream_t)stream);
     if (e != cudaSuccess) {
         msg = std::string("dm_prefill: cudaMemsetAsync: ") + cudaGetErrorString(e);
@@ -855,13 +893,14 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
     a.rows = L.rows;
     a.NB = L.NB;
     a.M = (int32_t)M;
-    a.ntok = P.ntok;
-    a.ntt = P.ntt;
-    a.nparts = L.nparts;
+    a.ngrp = P.ngrp;
+    a.nt = P.nt;
+    a.nh = P.nh;
     a.ntiles = P.ntiles;
     a.nwin = (int32_t)P.nwin;
     a.W = P.W;
-    a.idesc = idesc_f16(kPfRows, P.ntt);
+    a.nxs = P.nxs;
+    a.idesc = idesc_f16(kPfRows, P.nt);
     a.bias = bias;
     a.out = out;
     a.out_f32 = out_f32;
@@ -873,7 +912,7 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)P.grid);
     cfg.blockDim = dim3(kPfThreads);
-    cfg.dynamicSmemBytes = (size_t)kSmemBytes;
+    cfg.dynamicSmemBytes = (size_t)P.smem;
     cfg.stream = (cudaStream_t)stream;
     cfg.numAttrs = 0;
     e = cudaLaunchKernelEx(&cfg, prefill_sip_kernel, xmap, a);
