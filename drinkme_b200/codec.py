@@ -112,6 +112,50 @@ def encode_arrays(U: np.ndarray, widths, block_size: int = DEFAULT_BLOCK, thread
     return palette[:covered], offsets, data
 
 
+def encode_arrays_device(bits, widths, block_size: int = DEFAULT_BLOCK):
+    """encode_arrays on the GPU: `bits` is a CUDA tensor of uint16 (or int16)
+    bf16 patterns [R, C]; the exponent histogram, the per-block word counts
+    and the payload are computed on its device (dm_pack_plan_device /
+    dm_pack_encode_device). Returns the same (palette, offsets, data) numpy
+    arrays, byte for byte."""
+    import torch
+
+    if not isinstance(bits, torch.Tensor) or bits.device.type != "cuda":
+        raise TypeError("encode_arrays_device: expected a CUDA tensor of bf16 bit patterns")
+    if bits.dim() != 2 or min(bits.shape) < 1 or bits.element_size() != 2 or bits.is_floating_point():
+        raise ValueError("expected a nonempty 2D uint16 array of bf16 bit patterns")
+    bits = bits.contiguous()
+    R, C = bits.shape
+    w = np.ascontiguousarray([int(x) for x in widths], dtype=np.int32)
+    covered = sum((1 << int(x)) - 1 for x in widths[:-1])
+    nb = (C + block_size - 1) // block_size
+    palette = np.zeros(max(covered, 1), dtype=np.uint8)
+    offsets = np.zeros(R * nb + 1, dtype=np.uint32)
+    nwords = ct.c_uint64()
+    stream = ct.c_void_p(torch.cuda.current_stream(bits.device).cuda_stream)
+    _lib.call("dm_pack_plan_device", ct.c_void_p(bits.data_ptr()), R, C, _ptr(w), len(w), int(block_size),
+              _ptr(palette), _ptr(offsets), ct.byref(nwords), stream)
+    data = torch.empty(max(int(nwords.value), 1), dtype=torch.int32, device=bits.device)
+    _lib.call("dm_pack_encode_device", ct.c_void_p(bits.data_ptr()), R, C, _ptr(w), len(w), int(block_size),
+              _ptr(palette), _ptr(offsets), ct.c_void_p(data.data_ptr()), int(nwords.value), stream)
+    host = data[: int(nwords.value)].cpu().numpy().view(np.uint32)
+    return palette[:covered], offsets, host
+
+
+def pack_array_radix_device(bits, compression_profile: str, block_size: int = RADIX_BLOCK) -> dict | None:
+    """pack_array_radix for bits already on a GPU (encode_arrays_device): the
+    same dict, byte for byte, or None when radix would not compress."""
+    widths = widths_of(compression_profile)
+    palette, offsets, data = encode_arrays_device(bits, widths, block_size)
+    R, C = bits.shape
+    if _would_expand(palette, offsets, data, widths, R * C * 2):
+        return None
+    stored = palette.nbytes + offsets.nbytes + data.nbytes
+    return {"rx_palette": palette, "rx_offsets": offsets, "rx_data": data, "R": int(R), "C": int(C),
+            "bpw": 8.0 * stored / (R * C), "codec": RADIX, "profile": compression_profile,
+            "widths": list(widths), "block_size": int(block_size)}
+
+
 def _would_expand(palette, offsets, data, widths, nbytes: int) -> bool:
     """radix_pack._would_expand: stored OR device bytes reaching the raw
     plane's size means no compression."""

@@ -124,6 +124,13 @@ int launch_prefill_sip(const dm_tensor *t, const uint16_t *x, int64_t M, const u
 int64_t pack_read_bytes(const PackPart &P, int64_t *payload_words);
 int64_t block_words_most(int64_t n, const int32_t *widths, int32_t nw);
 
+// Pack encoder (encode.cpp): the parameter checks of radix.pack_array, and
+// the palette (exponents by frequency, ties to the lower exponent) with each
+// exponent's rank (covered when it is not in the palette).
+int check_pack_params(int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, int32_t *covered,
+                      std::string &msg);
+void palette_from_histogram(const uint64_t *hist, int32_t covered, uint8_t *palette_out, uint16_t *rank);
+
 // Kernel launchers (kernels.cu)
 int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
 int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,

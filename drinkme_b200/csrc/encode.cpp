@@ -57,26 +57,6 @@ struct Plan {
     std::array<uint16_t, 256> rank{};  // exponent -> palette rank (covered when absent)
 };
 
-int check_params(int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, int32_t *covered,
-                 std::string &msg) {
-    if (R <= 0 || C <= 0) { msg = "expected a nonempty 2D uint16 array of bf16 bit patterns"; return 1; }
-    if (B < 32 || B > 4096 || (B & (B - 1))) { msg = "block_size must be a power of two from 32 through 4096"; return 1; }
-    if (nw < 2 || nw > 8 || widths[nw - 1] != 8) {
-        msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
-        return 1;
-    }
-    int32_t c = 0;
-    for (int i = 0; i < nw; ++i)
-        if (widths[i] < 1 || widths[i] > 8) {
-            msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
-            return 1;
-        }
-    for (int i = 0; i < nw - 1; ++i) c += (1 << widths[i]) - 1;
-    if (c > 256) { msg = "radix tiers exceed the exponent alphabet"; return 1; }
-    *covered = c;
-    return 0;
-}
-
 inline int64_t cw(int64_t count, int64_t width) { return (count * width + 31) / 32; }
 
 // Appends `width`-bit little-endian fields into a zeroed word stream.
@@ -95,6 +75,41 @@ struct FieldWriter {
 
 }  // namespace
 
+namespace dm {
+
+int check_pack_params(int64_t R, int64_t C, const int32_t *widths, int32_t nw, int32_t B, int32_t *covered,
+                      std::string &msg) {
+    if (R <= 0 || C <= 0) { msg = "expected a nonempty 2D uint16 array of bf16 bit patterns"; return 1; }
+    if (B < 32 || B > 4096 || (B & (B - 1))) { msg = "block_size must be a power of two from 32 through 4096"; return 1; }
+    if (nw < 2 || nw > 8 || widths[nw - 1] != 8) {
+        msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
+        return 1;
+    }
+    int32_t c = 0;
+    for (int i = 0; i < nw; ++i)
+        if (widths[i] < 1 || widths[i] > 8) {
+            msg = "radix needs 2..8 widths in 1..8, ending with the exponent width";
+            return 1;
+        }
+    for (int i = 0; i < nw - 1; ++i) c += (1 << widths[i]) - 1;
+    if (c > 256) { msg = "radix tiers exceed the exponent alphabet"; return 1; }
+    *covered = c;
+    return 0;
+}
+
+void palette_from_histogram(const uint64_t *hist, int32_t covered, uint8_t *palette_out, uint16_t *rank) {
+    std::array<int, 256> order;
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return hist[a] > hist[b]; });
+    for (int e = 0; e < 256; ++e) rank[e] = (uint16_t)covered;
+    for (int k = 0; k < covered; ++k) {
+        palette_out[k] = (uint8_t)order[k];
+        rank[order[k]] = (uint16_t)k;
+    }
+}
+
+}  // namespace dm
+
 extern "C" int dm_pack_plan(const uint16_t *bits, int64_t R, int64_t C, const int32_t *widths, int32_t nw,
                             int32_t B, int32_t threads, uint8_t *palette_out, uint32_t *offsets_out,
                             uint64_t *nwords, char *err, size_t err_len) {
@@ -104,7 +119,7 @@ extern "C" int dm_pack_plan(const uint16_t *bits, int64_t R, int64_t C, const in
         dm::set_error(err, err_len, "dm_pack_plan: null pointer");
         return DM_EINVAL;
     }
-    if (check_params(R, C, widths, nw, B, &covered, msg)) { dm::set_error(err, err_len, msg); return DM_EINVAL; }
+    if (dm::check_pack_params(R, C, widths, nw, B, &covered, msg)) { dm::set_error(err, err_len, msg); return DM_EINVAL; }
     const int64_t NB = (C + B - 1) / B, nblk = R * NB;
     // histogram over the whole tensor, one partial per row range
     int nt = pool_size(threads, R * C / 4096 + 1);
@@ -123,15 +138,8 @@ extern "C" int dm_pack_plan(const uint16_t *bits, int64_t R, int64_t C, const in
     std::array<uint64_t, 256> hist{};
     for (auto &h : parts)
         for (int e = 0; e < 256; ++e) hist[e] += h[e];
-    std::array<int, 256> order;
-    std::iota(order.begin(), order.end(), 0);
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return hist[a] > hist[b]; });
     std::array<uint16_t, 256> rank;
-    rank.fill((uint16_t)covered);
-    for (int k = 0; k < covered; ++k) {
-        palette_out[k] = (uint8_t)order[k];
-        rank[order[k]] = (uint16_t)k;
-    }
+    dm::palette_from_histogram(hist.data(), covered, palette_out, rank.data());
     // per-block word counts, then the directory
     std::vector<uint32_t> words(nblk);
     run_blocks(nblk, threads, [&](int64_t blk) {
@@ -173,7 +181,7 @@ extern "C" int dm_pack_encode(const uint16_t *bits, int64_t R, int64_t C, const 
         dm::set_error(err, err_len, "dm_pack_encode: null pointer");
         return DM_EINVAL;
     }
-    if (check_params(R, C, widths, nw, B, &covered, msg)) { dm::set_error(err, err_len, msg); return DM_EINVAL; }
+    if (dm::check_pack_params(R, C, widths, nw, B, &covered, msg)) { dm::set_error(err, err_len, msg); return DM_EINVAL; }
     const int64_t NB = (C + B - 1) / B, nblk = R * NB;
     if (offsets[0] != 0 || offsets[nblk] != nwords) {
         dm::set_error(err, err_len, "directory endpoints");

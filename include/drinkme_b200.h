@@ -290,6 +290,23 @@ int dm_pack_encode(const uint16_t *host_bits, int64_t R, int64_t C, const int32_
                    int32_t nwidths, int32_t block_size, int32_t threads, const uint8_t *host_palette,
                    const uint32_t *host_offsets, uint32_t *host_data, uint64_t nwords, char *err, size_t err_len);
 
+/* The same encoder on the GPU (radix_native.cpp:57-166 `plan` / `encode`,
+ * the writers behind radix.py:77-136 `pack_array`), for bits already in
+ * device memory: dm_pack_plan_device histograms the exponents and counts
+ * every block's words on the device and fills host_palette, host_offsets
+ * (R*NB+1) and *nwords on the host (it synchronises `stream`);
+ * dm_pack_encode_device then writes the nwords payload words into d_data
+ * (device memory of the bits' GPU), byte-identical to dm_pack_encode, and
+ * synchronises `stream`. Temporary device memory comes from the stream-
+ * ordered allocator. */
+int dm_pack_plan_device(const uint16_t *d_bits, int64_t R, int64_t C, const int32_t *host_widths, int32_t nwidths,
+                        int32_t block_size, uint8_t *host_palette, uint32_t *host_offsets, uint64_t *nwords,
+                        void *stream, char *err, size_t err_len);
+int dm_pack_encode_device(const uint16_t *d_bits, int64_t R, int64_t C, const int32_t *host_widths,
+                          int32_t nwidths, int32_t block_size, const uint8_t *host_palette,
+                          const uint32_t *host_offsets, uint32_t *d_data, uint64_t nwords, void *stream, char *err,
+                          size_t err_len);
+
 /* Reads and clears the tensor's device error word (a kernel's bounded
  * wait that gave up writes it). Synchronises the tensor's device. */
 int dm_tensor_check(const dm_tensor *t, int32_t *device_error, char *err, size_t err_len);
