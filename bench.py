@@ -532,6 +532,53 @@ def config5_prefill(device):
                      "prefill kernel (decoded tiles in shared memory, TMEM accumulators)", "per_linear": out}
 
 
+def crossover_8b(device, Ms=(8, 9, 12, 16, 24, 32, 48, 64)):
+    """The row count at which the dense arm starts to beat the multi-column
+    GEMV on B200 (the measurement DRINKME_PREFILL_DENSE_MIN exists for,
+    swap.py:205-225): one Qwen3-8B layer's seven sip linears at M activation
+    rows through (a) the row loop in chunks of MC_MAX rows on the mc kernel,
+    (b) the reference's dense arm, decode to bf16 then cuBLAS, (c) the
+    tensor-core prefill kernel; µs per layer from one CUDA graph per arm."""
+    import torch
+
+    from drinkme_b200 import codec, radix_ops, swap
+    from drinkme_b200.ops import MC_MAX
+
+    lins = []
+    for j, (name, R, C) in enumerate(WORKLOADS["qwen3-8b"]["linears"]):
+        bits = make_bits(R, C, seed=3000 + j, device=device)
+        lins.append((name, swap.to_device_radix(codec.pack_array_radix(bits, "sip"), device), R, C))
+        del bits
+    rows = {}
+    for M in Ms:
+        xs = {C: (torch.randn((M, C), generator=torch.Generator(device=device).manual_seed(M), device=device)
+                  .to(torch.bfloat16)) for C in {c for _, _, _, c in lins}}
+        outs = [torch.empty((M, R), dtype=torch.bfloat16, device=device) for _, _, R, _ in lins]
+
+        def loop():
+            for (_, rt, R, C), o in zip(lins, outs):
+                for i in range(0, M, MC_MAX):
+                    radix_ops.gemv_into(rt, xs[C][i:i + MC_MAX], None, o[i:i + MC_MAX])
+
+        def dense():
+            for (_, rt, R, C), o in zip(lins, outs):
+                o.copy_(torch.nn.functional.linear(xs[C], radix_ops.decode_weight(rt)))
+
+        def tc():
+            for (_, rt, R, C), o in zip(lins, outs):
+                o.copy_(radix_ops.prefill(rt, xs[C], None, torch.bfloat16))
+
+        rows[M] = {"mc_loop_us": round(_graph_us(loop, device), 1), "dense_us": round(_graph_us(dense, device), 1),
+                   "tcgen05_us": round(_graph_us(tc, device), 1)}
+        del xs, outs
+    dense_min = next((M for M in Ms if rows[M]["dense_us"] < rows[M]["mc_loop_us"]), None)
+    del lins
+    torch.cuda.empty_cache()
+    return {"config": "Qwen3-8B layer (7 sip linears) at M activation rows: mc in chunks of MC_MAX vs decode + cuBLAS "
+                      "vs the tcgen05 prefill kernel, us per layer", "per_M": rows,
+            "dense_beats_mc_from_M": dense_min}
+
+
 def cublas_arm(shapes, device, reps=10):
     """cuBLAS dense bf16 (F.linear, M = 1) on uncompressed weights of the same
     shapes, rotating over copies larger than 3x L2 inside one CUDA graph (as
@@ -779,6 +826,7 @@ def main():
             result["vs_cublas_8b_m1"] = vs_cublas_8b(device, peak)
             result["config3_gulp_mc"] = config3_gulp_mc(device, peak)
             result["config5_prefill"] = config5_prefill(device)
+            result["crossover_8b"] = crossover_8b(device)
         if not a.no_cpu:
             tok_s, f = cpu_reference(a.workload, 3, 1, log)
             result["cpu_baseline"] = {"value": round(tok_s, 4), "unit": "tokens/s", "kind": "reference", **f}

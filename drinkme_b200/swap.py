@@ -18,9 +18,12 @@ drop-in for the reference's ``drinkme.codec.swap`` module classes and loader
   eligible                        swap.py:850-854  which Linears the codec takes
 
 Routing (swap.py:302-335): M == 1 -> "gemv"; 2 <= M <= MC_MAX -> "mc"
-unless DRINKME_PREFILL_DENSE_MIN says dense; M >= GEMM_MIN_ROWS (9) ->
-"dense" (decode the weight once, then one GEMM); "loop" when the dense arm
-is switched off. The epilogue rounds once: fp32 accumulate, plus the bias
+unless DRINKME_PREFILL_DENSE_MIN says dense; M >= the dense threshold ->
+"dense" (decode the weight once, then one GEMM); "loop" in between and when
+the dense arm is switched off, here through the multi-column kernel in
+chunks of MC_MAX rows (same bits as one row at a time). The threshold is
+DRINKME_PREFILL_DENSE_MIN when set, else the crossover measured on B200
+(DENSE_MIN_MEASURED = 17; the reference's box measured GEMM_MIN_ROWS = 9). The epilogue rounds once: fp32 accumulate, plus the bias
 in fp32, one cast (swap.py:284-300). There is no CPU route: a CPU input
 raises (the reference's CPU route is the oracle here, oracle/oracle.py).
 """
@@ -150,19 +153,27 @@ def resident_bytes(runtime: dict) -> int:
 
 _DENSE_MIN: int | None = None
 
+# The dense arm's row threshold measured on B200 (bench.crossover_8b, one
+# Qwen3-8B layer of sip linears): the row loop through the multi-column
+# kernel, MC_MAX rows per launch, takes 208-228 us per layer at 9-16 rows
+# (two launches per linear) against 275-277 us for decode + cuBLAS, and 336
+# us at 24 rows (three) — so the dense arm starts at 17 rows here, where the
+# reference box measured GEMM_MIN_ROWS = 9.
+DENSE_MIN_MEASURED = 2 * MC_MAX + 1
+
 
 def _dense_min() -> int:
-    """DRINKME_PREFILL_DENSE_MIN if set, else GEMM_MIN_ROWS; <= 0 disables the
-    dense arm. Read once (swap.py:205-225)."""
+    """DRINKME_PREFILL_DENSE_MIN if set, else the measured crossover; <= 0
+    disables the dense arm. Read once (swap.py:205-225)."""
     global _DENSE_MIN
     if _DENSE_MIN is None:
         raw = os.environ.get("DRINKME_PREFILL_DENSE_MIN", "").strip()
         try:
-            _DENSE_MIN = int(raw) if raw else CompressedLinear.GEMM_MIN_ROWS
+            _DENSE_MIN = int(raw) if raw else DENSE_MIN_MEASURED
         except ValueError:
             warnings.warn(f"DRINKME_PREFILL_DENSE_MIN={raw!r} is not an integer; using the measured default "
-                          f"{CompressedLinear.GEMM_MIN_ROWS}")
-            _DENSE_MIN = CompressedLinear.GEMM_MIN_ROWS
+                          f"{DENSE_MIN_MEASURED}")
+            _DENSE_MIN = DENSE_MIN_MEASURED
     return _DENSE_MIN
 
 
@@ -274,6 +285,8 @@ class RadixCompressedLinear(CompressedLinear):
             else:
                 out = radix_ops.gemv_mc_fused(self.p, xf, self.bias, x.dtype)
             return out.reshape(*shape[:-1], self.R)
+        if route == "loop" and x.dtype in (torch.bfloat16, torch.float32):
+            return self._loop_rows(x, x.shape)
         if route == "dense" and x.dtype == torch.bfloat16 and _prefill_kernel() and self.p["rx_handle"].info.fast_path:
             # the dense arm's arithmetic on the tensor cores, the weights
             # decoded into shared memory instead of HBM
@@ -281,6 +294,26 @@ class RadixCompressedLinear(CompressedLinear):
             out = radix_ops.prefill(self.p, x.reshape(-1, self.C), self.bias, x.dtype)
             return out.reshape(*shape[:-1], self.R)
         return super()._forward(x, route)
+
+
+    def _loop_rows(self, x, shape):
+        # the row loop in chunks of MC_MAX rows through the multi-column
+        # kernel: each row bitwise the M = 1 call (the reference loops one
+        # row at a time, swap.py:380-392), the weight read once per chunk
+        xf = x.reshape(-1, self.C)
+        out = torch.empty(xf.shape[0], self.R, device=x.device, dtype=x.dtype)
+        for i in range(0, xf.shape[0], MC_MAX):
+            radix_ops.gemv_into(self.p, xf[i:i + MC_MAX], self.bias, out[i:i + MC_MAX])
+        return out.reshape(*shape[:-1], self.R)
+
+
+def fused_m_max() -> int:
+    """The widest MTP verify batch whose compressed Linears stay on the serial
+    step's numerics (serving/mtp.py:228-240 FUSED_M_MAX): the multi-column
+    kernel serves 2..MC_MAX rows, each bitwise the M = 1 answer, up to the
+    row before the dense arm takes over."""
+    dense_min = _dense_min()
+    return MC_MAX if dense_min <= 0 else max(1, min(MC_MAX, dense_min - 1))
 
 
 class RawLinear(CompressedLinear):

@@ -191,13 +191,15 @@ def test_routing_thresholds(monkeypatch):
     monkeypatch.delenv("DRINKME_PREFILL_DENSE_MIN", raising=False)
     assert m._route_rows(1) == "gemv"
     assert [m._route_rows(k) for k in range(2, 9)] == ["mc"] * 7
-    assert m._route_rows(9) == "dense"
+    assert [m._route_rows(k) for k in range(9, 17)] == ["loop"] * 8  # the crossover measured on B200
+    assert m._route_rows(17) == "dense" and swap.fused_m_max() == 8
     swap._DENSE_MIN = None
     monkeypatch.setenv("DRINKME_PREFILL_DENSE_MIN", "0")
     assert m._route_rows(9) == "loop" and m._route_rows(5) == "mc"
     swap._DENSE_MIN = None
     monkeypatch.setenv("DRINKME_PREFILL_DENSE_MIN", "4")
     assert m._route_rows(4) == "dense" and m._route_rows(3) == "mc"
+    assert swap.fused_m_max() == 3  # an MTP verify batch stays below the dense arm
     swap._DENSE_MIN = None
 
 
