@@ -579,6 +579,38 @@ def crossover_8b(device, Ms=(8, 9, 12, 16, 24, 32, 48, 64)):
             "dense_beats_mc_from_M": dense_min}
 
 
+def decode_step_8b(device, steps=20, warmup=3):
+    """SURVEY (f) 3: a whole batch-1 Qwen3-8B decode step (36 layers: norms,
+    q|k|v, rotary, KV-cache attention, o, gate|up, SiLU, down, lm_head,
+    greedy sampling) replayed from one CUDA graph (decode_step.DecodeStack),
+    tokens/s from device-timed replays at positions 0..steps."""
+    import torch
+
+    from drinkme_b200 import decode_step
+
+    st = decode_step.DecodeStack(decode_step.QWEN3["qwen3-8b"], device, max_len=1024, seed=11)
+    st.reset(token=1)
+    st.capture()
+    for _ in range(warmup):
+        st.replay()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        st.replay()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b) / steps
+    out = {"config": "Qwen3-8B shapes, 36 layers, sip linears + raw bf16 lm_head, batch 1, KV cache of 1024 rows "
+                     "(attention over the allocation with a live-length mask), one CUDA graph per step",
+           "ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "steps": steps,
+           "graph_nodes_note": "norms, rotary, attention and sampling are torch operations; the linears are ours"}
+    del st
+    torch.cuda.empty_cache()
+    return out
+
+
 def cublas_arm(shapes, device, reps=10):
     """cuBLAS dense bf16 (F.linear, M = 1) on uncompressed weights of the same
     shapes, rotating over copies larger than 3x L2 inside one CUDA graph (as
@@ -827,6 +859,7 @@ def main():
             result["config3_gulp_mc"] = config3_gulp_mc(device, peak)
             result["config5_prefill"] = config5_prefill(device)
             result["crossover_8b"] = crossover_8b(device)
+            result["decode_step_8b"] = decode_step_8b(device)
         if not a.no_cpu:
             tok_s, f = cpu_reference(a.workload, 3, 1, log)
             result["cpu_baseline"] = {"value": round(tok_s, 4), "unit": "tokens/s", "kind": "reference", **f}

@@ -17,7 +17,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdrinkme_b200.so")
-SOURCES = ("abi.cu", "kernels.cu", "sip.cu", "prefill.cu", "noalloc.cu", "layout.cpp", "encode.cpp", "encode_gpu.cu")
+SOURCES = ("abi.cu", "kernels.cu", "sip.cu", "prefill.cu", "noalloc.cu", "layout.cpp", "encode.cpp", "encode_gpu.cu", "step_ops.cu")
 HEADERS = ("dm_internal.h", "dm_device.cuh")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

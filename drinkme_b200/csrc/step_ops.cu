@@ -1,0 +1,245 @@
+// The small fused operations of a batch-1 decode step around the packed
+// Linears (decode_step.DecodeStack; the reference runs transformers' own
+// modules there, src/drinkme/serving/cudagraph.py captures them): one
+// launch each for the residual add + RMSNorm, the per-head q/k RMSNorm +
+// rotary embedding + KV-cache write, grouped-query decode attention over
+// the cache (split over the sequence, then combined) and SiLU(gate) * up.
+// Every launch reads the position from device memory, so a captured graph
+// serves every step. bf16 storage, fp32 arithmetic. Each kernel lets the
+// launch after it start early (programmatic dependent launch): a sip GEMV
+// stages its first weights while these run and waits for them to finish
+// before it reads their output.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <string>
+
+#include "dm_device.cuh"
+#include "dm_internal.h"
+
+namespace dm {
+namespace {
+
+constexpr int kAttnChunk = 128;  // cache rows per attention CTA
+
+__device__ __forceinline__ float bf(uint16_t b) { return bf16_bits_to_f32(b); }
+__device__ __forceinline__ uint16_t to_bf(float f) { return f32_to_bf16_bits(f); }
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.f;
+    for (int i = 0; i < nw; ++i) s += red[i];
+    __syncthreads();
+    return s;
+}
+
+// h <- h + delta (rounded to bf16, as an in-place bf16 add), then
+// out = h * rsqrt(mean(h^2) + eps) * w; one CTA, one row.
+__global__ void add_rmsnorm_kernel(uint16_t *h, const uint16_t *delta, const uint16_t *w, uint16_t *out, int n,
+                                   float eps) {
+    pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float x = bf(h[i]);
+        if (delta) {
+            x = bf(to_bf(x + bf(delta[i])));
+            h[i] = to_bf(x);
+        }
+        ss += x * x;
+    }
+    const float r = rsqrtf(block_sum(ss, red) / (float)n + eps);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = to_bf(bf(to_bf(bf(h[i]) * r)) * bf(w[i]));
+}
+
+// A warp per head of the fused q|k|v row: q and k heads get RMSNorm over
+// the head (weights qn / kn) and the rotary embedding at *pos (pairs i,
+// i + hd/2); q goes to q_out, k and v to row *pos of the layer's caches
+// [max_len][nkv][hd].
+__global__ void qk_norm_rope_cache_kernel(const uint16_t *qkv, const uint16_t *qn, const uint16_t *kn,
+                                          const float *cosv, const float *sinv, const int64_t *pos, uint16_t *q_out,
+                                          uint16_t *kc, uint16_t *vc, int nh, int nkv, int hd, float eps) {
+    pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (head >= nh + 2 * nkv) return;
+    const int64_t p = *pos;
+    const uint16_t *src = qkv + (int64_t)head * hd;
+    if (head >= nh + nkv) {  // v: copied into the cache row
+        uint16_t *dst = vc + (p * nkv + (head - nh - nkv)) * hd;
+        for (int i = lane; i < hd; i += 32) dst[i] = src[i];
+        return;
+    }
+    const bool isq = head < nh;
+    const uint16_t *wn = isq ? qn : kn;
+    const int half = hd / 2;
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) {
+        const float x = bf(src[i]);
+        ss += x * x;
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)hd + eps);
+    uint16_t *dst = isq ? q_out + (int64_t)head * hd : kc + (p * nkv + (head - nh)) * hd;
+    for (int i = lane; i < half; i += 32) {
+        // the normed values rounded to bf16 first, as the module stores them
+        const float x1 = bf(to_bf(bf(to_bf(bf(src[i]) * r)) * bf(wn[i])));
+        const float x2 = bf(to_bf(bf(to_bf(bf(src[i + half]) * r)) * bf(wn[i + half])));
+        const float c = cosv[p * half + i], s = sinv[p * half + i];
+        dst[i] = to_bf(x1 * c - x2 * s);
+        dst[i + half] = to_bf(x2 * c + x1 * s);
+    }
+}
+
+// Split decode attention: CTA (kv head g, chunk j) covers cache rows
+// [128 j, 128 j + 128) below *pos + 1; a warp per query head of the group
+// keeps a running max, sum and weighted value sum, written to
+// part[head][j] = {m, l, acc[hd]}.
+__global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
+                                  float *part, int nh, int nkv, int hd, int nchunks, float scale) {
+    pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    const int g = blockIdx.x, j = blockIdx.y, lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
+    const int grp = nh / nkv;
+    if (wq >= grp) return;
+    const int head = g * grp + wq;
+    const int64_t live = *pos + 1;
+    const int64_t r0 = (int64_t)j * kAttnChunk, r1 = min(live, r0 + kAttnChunk);
+    float qv[4], acc[4];
+    const int per = hd / 32;  // 4 at hd = 128
+    for (int e = 0; e < per; ++e) {
+        qv[e] = bf(q[(int64_t)head * hd + lane * per + e]) * scale;
+        acc[e] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int64_t r = r0; r < r1; ++r) {
+        const uint16_t *kr = kc + (r * nkv + g) * hd + lane * per;
+        float s = 0.f;
+        for (int e = 0; e < per; ++e) s += qv[e] * bf(kr[e]);
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mn = fmaxf(m, s);
+        const float a = __expf(m - mn), b = __expf(s - mn);
+        const uint16_t *vr = vc + (r * nkv + g) * hd + lane * per;
+        for (int e = 0; e < per; ++e) acc[e] = acc[e] * a + b * bf(vr[e]);
+        l = l * a + b;
+        m = mn;
+    }
+    float *out = part + ((int64_t)head * nchunks + j) * (hd + 2);
+    if (lane == 0) {
+        out[0] = m;
+        out[1] = l;
+    }
+    for (int e = 0; e < per; ++e) out[2 + lane * per + e] = acc[e];
+}
+
+// A warp per query head: the chunks' partial softmaxes combined.
+__global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint16_t *out, int nh, int hd,
+                                    int nchunks) {
+    pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    const int head = blockIdx.x, lane = threadIdx.x;
+    const int used = (int)min((int64_t)nchunks, (*pos + kAttnChunk) / kAttnChunk);
+    const float *p = part + (int64_t)head * nchunks * (hd + 2);
+    float M = -INFINITY;
+    for (int j = 0; j < used; ++j) M = fmaxf(M, p[j * (hd + 2)]);
+    const int per = hd / 32;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+    for (int j = 0; j < used; ++j) {
+        const float *pj = p + j * (hd + 2);
+        if (pj[1] == 0.f) continue;
+        const float a = __expf(pj[0] - M);
+        L += a * pj[1];
+        for (int e = 0; e < per; ++e) acc[e] += a * pj[2 + lane * per + e];
+    }
+    for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(acc[e] / L);
+}
+
+__global__ void silu_mul_kernel(const uint16_t *gu, uint16_t *out, int n) {
+    pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float g = bf(gu[i]), u = bf(gu[n + i]);
+    out[i] = to_bf(g / (1.f + __expf(-g)) * u);
+}
+
+int launched(const char *what, std::string &msg) {
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return DM_OK;
+    msg = std::string(what) + ": " + cudaGetErrorString(e);
+    return DM_ECUDA;
+}
+
+}  // namespace
+}  // namespace dm
+
+extern "C" int dm_step_add_rmsnorm(void *h, const void *delta, const void *w, void *out, int64_t n, float eps,
+                                   void *stream, char *err, size_t err_len) {
+    if (!h || !w || !out || n < 1 || n > (1 << 20)) {
+        dm::set_error(err, err_len, "dm_step_add_rmsnorm: bad arguments");
+        return DM_EINVAL;
+    }
+    dm::add_rmsnorm_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(
+        (uint16_t *)h, (const uint16_t *)delta, (const uint16_t *)w, (uint16_t *)out, (int)n, eps);
+    std::string msg;
+    int rc = dm::launched("add_rmsnorm_kernel", msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_step_qk_rope_cache(const void *qkv, const void *qn, const void *kn, const float *cosv,
+                                     const float *sinv, const int64_t *pos, void *q_out, void *kcache, void *vcache,
+                                     int32_t nh, int32_t nkv, int32_t hd, float eps, void *stream, char *err,
+                                     size_t err_len) {
+    if (!qkv || !qn || !kn || !cosv || !sinv || !pos || !q_out || !kcache || !vcache || nh < 1 || nkv < 1 ||
+        nh % nkv || hd != 128) {
+        dm::set_error(err, err_len, "dm_step_qk_rope_cache: bad arguments (head_dim 128)");
+        return DM_EINVAL;
+    }
+    const int heads = nh + 2 * nkv, per = 4;
+    dm::qk_norm_rope_cache_kernel<<<(heads + per - 1) / per, 32 * per, 0, (cudaStream_t)stream>>>(
+        (const uint16_t *)qkv, (const uint16_t *)qn, (const uint16_t *)kn, cosv, sinv, pos, (uint16_t *)q_out,
+        (uint16_t *)kcache, (uint16_t *)vcache, nh, nkv, hd, eps);
+    std::string msg;
+    int rc = dm::launched("qk_norm_rope_cache_kernel", msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int64_t dm_step_attention_workspace_bytes(int32_t nh, int32_t hd, int64_t max_len) {
+    const int64_t nchunks = (max_len + dm::kAttnChunk - 1) / dm::kAttnChunk;
+    return (int64_t)nh * nchunks * (hd + 2) * 4;
+}
+
+extern "C" int dm_step_attention(const void *q, const void *kcache, const void *vcache, const int64_t *pos,
+                                 int64_t max_len, void *out, float *work, int32_t nh, int32_t nkv, int32_t hd,
+                                 void *stream, char *err, size_t err_len) {
+    if (!q || !kcache || !vcache || !pos || !out || !work || nh < 1 || nkv < 1 || nh % nkv || hd != 128 ||
+        nh / nkv > 32 || max_len < 1) {
+        dm::set_error(err, err_len, "dm_step_attention: bad arguments (head_dim 128, up to 32 heads per kv head)");
+        return DM_EINVAL;
+    }
+    const int nchunks = (int)((max_len + dm::kAttnChunk - 1) / dm::kAttnChunk);
+    cudaStream_t s = (cudaStream_t)stream;
+    dm::attn_split_kernel<<<dim3(nkv, nchunks), 32 * (nh / nkv), 0, s>>>(
+        (const uint16_t *)q, (const uint16_t *)kcache, (const uint16_t *)vcache, pos, work, nh, nkv, hd, nchunks,
+        1.0f / sqrtf((float)hd));
+    dm::attn_combine_kernel<<<nh, 32, 0, s>>>(work, pos, (uint16_t *)out, nh, hd, nchunks);
+    std::string msg;
+    int rc = dm::launched("attention kernels", msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int dm_step_silu_mul(const void *gu, void *out, int64_t n, void *stream, char *err, size_t err_len) {
+    if (!gu || !out || n < 1 || n > INT32_MAX) {
+        dm::set_error(err, err_len, "dm_step_silu_mul: bad arguments");
+        return DM_EINVAL;
+    }
+    dm::silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t *)gu,
+                                                                                       (uint16_t *)out, (int)n);
+    std::string msg;
+    int rc = dm::launched("silu_mul_kernel", msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}

@@ -307,6 +307,33 @@ int dm_pack_encode_device(const uint16_t *d_bits, int64_t R, int64_t C, const in
                           const uint32_t *host_offsets, uint32_t *d_data, uint64_t nwords, void *stream, char *err,
                           size_t err_len);
 
+/* The fused operations around the packed Linears in a batch-1 decode step
+ * (no counterpart in the reference's path: it runs transformers' own
+ * modules there, src/drinkme/serving/cudagraph.py). bf16 storage, fp32
+ * arithmetic; positions are read from device memory, so one captured graph
+ * serves every step.
+ *   dm_step_add_rmsnorm: h += delta (when delta is not null, rounded to
+ *     bf16), out = bf16(h * rsqrt(mean(h^2) + eps)) * w, over n values.
+ *   dm_step_qk_rope_cache: per head of the fused q|k|v row, RMSNorm of q and
+ *     k heads (weights qn, kn), the rotary embedding at *pos (cos/sin tables
+ *     [max_len][head_dim / 2] fp32), q into q_out, k and v into row *pos of
+ *     the layer's caches [max_len][nkv][head_dim]. head_dim 128.
+ *   dm_step_attention: grouped-query attention of q [nh][head_dim] over the
+ *     cache rows 0..*pos into out [nh][head_dim]; `work` holds
+ *     dm_step_attention_workspace_bytes(nh, head_dim, max_len) bytes.
+ *   dm_step_silu_mul: out[i] = silu(gu[i]) * gu[n + i]. */
+int dm_step_add_rmsnorm(void *h, const void *delta, const void *w, void *out, int64_t n, float eps, void *stream,
+                        char *err, size_t err_len);
+int dm_step_qk_rope_cache(const void *qkv, const void *qn, const void *kn, const float *cos_table,
+                          const float *sin_table, const int64_t *pos, void *q_out, void *kcache, void *vcache,
+                          int32_t nh, int32_t nkv, int32_t head_dim, float eps, void *stream, char *err,
+                          size_t err_len);
+int64_t dm_step_attention_workspace_bytes(int32_t nh, int32_t head_dim, int64_t max_len);
+int dm_step_attention(const void *q, const void *kcache, const void *vcache, const int64_t *pos, int64_t max_len,
+                      void *out, float *work, int32_t nh, int32_t nkv, int32_t head_dim, void *stream, char *err,
+                      size_t err_len);
+int dm_step_silu_mul(const void *gu, void *out, int64_t n, void *stream, char *err, size_t err_len);
+
 /* Reads and clears the tensor's device error word (a kernel's bounded
  * wait that gave up writes it). Synchronises the tensor's device. */
 int dm_tensor_check(const dm_tensor *t, int32_t *device_error, char *err, size_t err_len);
