@@ -135,11 +135,36 @@ def encode_arrays_device(bits, widths, block_size: int = DEFAULT_BLOCK):
     stream = ct.c_void_p(torch.cuda.current_stream(bits.device).cuda_stream)
     _lib.call("dm_pack_plan_device", ct.c_void_p(bits.data_ptr()), R, C, _ptr(w), len(w), int(block_size),
               _ptr(palette), _ptr(offsets), ct.byref(nwords), stream)
-    data = torch.empty(max(int(nwords.value), 1), dtype=torch.int32, device=bits.device)
+    n = int(nwords.value)
+    data = torch.empty(max(n, 1), dtype=torch.int32, device=bits.device)
     _lib.call("dm_pack_encode_device", ct.c_void_p(bits.data_ptr()), R, C, _ptr(w), len(w), int(block_size),
-              _ptr(palette), _ptr(offsets), ct.c_void_p(data.data_ptr()), int(nwords.value), stream)
-    host = data[: int(nwords.value)].cpu().numpy().view(np.uint32)
+              _ptr(palette), _ptr(offsets), ct.c_void_p(data.data_ptr()), n, stream)
+    # the payload comes back through a pinned buffer kept for the next call
+    # (a fresh pageable array would fault in every page during the copy)
+    host = np.empty(n, dtype=np.uint32)
+    pinned = _pinned_staging(n * 4)
+    done = 0
+    while done < n:
+        k = min(n - done, pinned.numel() // 4)
+        pinned[: k * 4].view(torch.int32).copy_(data[done: done + k], non_blocking=True)
+        torch.cuda.current_stream(bits.device).synchronize()
+        host[done: done + k] = pinned[: k * 4].numpy().view(np.uint32)
+        done += k
     return palette[:covered], offsets, host
+
+
+_PINNED = None
+
+
+def _pinned_staging(nbytes: int):
+    """A pinned host buffer of up to 64 MiB, reused across calls."""
+    import torch
+
+    global _PINNED
+    want = min(max(nbytes, 1 << 20), 64 << 20)
+    if _PINNED is None or _PINNED.numel() < want:
+        _PINNED = torch.empty(want, dtype=torch.uint8, pin_memory=True)
+    return _PINNED
 
 
 def pack_array_radix_device(bits, compression_profile: str, block_size: int = RADIX_BLOCK) -> dict | None:
