@@ -18,7 +18,7 @@ DM_MAX_RANKS = 8
 
 EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
-           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_pack_plan_device", "dm_pack_encode_device", "dm_step_add_rmsnorm", "dm_step_qk_rope_cache", "dm_step_attention_workspace_bytes", "dm_step_attention", "dm_step_silu_mul", "dm_tensor_check",
+           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_pack_plan_device", "dm_pack_encode_device", "dm_decode_pack", "dm_step_add_rmsnorm", "dm_step_qk_rope_cache", "dm_step_attention_workspace_bytes", "dm_step_attention", "dm_step_silu_mul", "dm_tensor_check",
            "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_tensor_set_launch", "dm_gemv_plan", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
 
 
@@ -91,6 +91,7 @@ def lib():
         L.dm_gemv_raw.argtypes = [p, i64, i64, p, i32, i64, p, p, i32, p, cp, sz]
         L.dm_pack_plan.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, ct.POINTER(ct.c_uint64), cp, sz]
         L.dm_pack_encode.argtypes = [p, i64, i64, p, i32, i32, i32, p, p, p, ct.c_uint64, cp, sz]
+        L.dm_decode_pack.argtypes = [p, sz, p, sz, sz, i64, i64, p, i32, i32, p, p, p, p, cp, sz]
         L.dm_pack_plan_device.argtypes = [p, i64, i64, p, i32, i32, p, p, ct.POINTER(ct.c_uint64), p, cp, sz]
         L.dm_pack_encode_device.argtypes = [p, i64, i64, p, i32, i32, p, p, p, ct.c_uint64, p, cp, sz]
         L.dm_step_add_rmsnorm.argtypes = [p, p, p, p, i64, ct.c_float, p, cp, sz]

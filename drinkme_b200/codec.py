@@ -112,6 +112,29 @@ def encode_arrays(U: np.ndarray, widths, block_size: int = DEFAULT_BLOCK, thread
     return palette[:covered], offsets, data
 
 
+def decode_pack_device(p: dict, device="cuda"):
+    """A radix pack decoded on a GPU straight from its own arrays (the word
+    stream and directory copied as they are; dm_decode_pack): uint16 bf16
+    bit patterns [R, C] as a CUDA tensor, bit-exact to the source."""
+    import torch
+
+    dev = torch.device(device)
+    palette = np.ascontiguousarray(p["rx_palette"], dtype=np.uint8)
+    offsets = np.ascontiguousarray(p["rx_offsets"], dtype=np.uint32)
+    data = np.ascontiguousarray(p["rx_data"], dtype=np.uint32)
+    R, C = int(p["R"]), int(p["C"])
+    w = np.ascontiguousarray([int(x) for x in p["widths"]], dtype=np.int32)
+    d_data = torch.zeros(data.size + 64, dtype=torch.int32, device=dev)  # a zero tail past the last block
+    d_data[: data.size].copy_(torch.from_numpy(data.view(np.int32)))
+    d_off = torch.from_numpy(offsets.view(np.int32)).to(dev)
+    out = torch.empty((R, C), dtype=torch.int16, device=dev)
+    stream = ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.call("dm_decode_pack", _ptr(palette), palette.size, _ptr(offsets), offsets.size, data.size, R, C, _ptr(w),
+              len(w), int(p.get("block_size", DEFAULT_BLOCK)), ct.c_void_p(d_data.data_ptr()),
+              ct.c_void_p(d_off.data_ptr()), ct.c_void_p(out.data_ptr()), stream)
+    return out
+
+
 def encode_arrays_device(bits, widths, block_size: int = DEFAULT_BLOCK):
     """encode_arrays on the GPU: `bits` is a CUDA tensor of uint16 (or int16)
     bf16 patterns [R, C]; the exponent histogram, the per-block word counts

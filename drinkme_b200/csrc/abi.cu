@@ -379,6 +379,22 @@ extern "C" int dm_decode(const dm_tensor *t, uint16_t *out, void *stream, char *
     return rc;
 }
 
+extern "C" int dm_decode_pack(const uint8_t *host_palette, size_t npalette, const uint32_t *host_offsets,
+                              size_t noffsets, size_t nwords, int64_t R, int64_t C, const int32_t *host_widths,
+                              int32_t nwidths, int32_t block_size, const uint32_t *d_data, const uint32_t *d_offsets,
+                              uint16_t *d_out, void *stream, char *err, size_t err_len) {
+    if (!host_palette || !host_offsets || !host_widths || !d_data || !d_offsets || !d_out)
+        return fail(err, err_len, DM_EINVAL, "dm_decode_pack: null pointer");
+    std::string msg;
+    if (dm::validate_pack(host_palette, npalette, host_offsets, noffsets, nwords, R, C, host_widths, nwidths,
+                          block_size, msg))
+        return fail(err, err_len, DM_EINVAL, msg);
+    int rc = dm::launch_decode_pack(host_palette, npalette, R, C, host_widths, nwidths, block_size, d_data, d_offsets,
+                                    d_out, stream, msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
 extern "C" int dm_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t *offsets, int64_t C,
                                    const int32_t *widths, int32_t nwidths, int32_t block_size, int64_t nblocks,
                                    uint16_t *out, void *stream, char *err, size_t err_len) {

@@ -133,6 +133,9 @@ void palette_from_histogram(const uint64_t *hist, int32_t covered, uint8_t *pale
 
 // Kernel launchers (kernels.cu)
 int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::string &msg);
+int launch_decode_pack(const uint8_t *palette, size_t npal, int64_t R, int64_t C, const int32_t *widths, int32_t nw,
+                       int32_t B, const uint32_t *words, const uint32_t *offsets, uint16_t *out, void *stream,
+                       std::string &msg);
 int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,
                         int out_f32, void *stream, std::string &msg);
 int launch_gemv_sip(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,

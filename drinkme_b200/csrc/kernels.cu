@@ -132,6 +132,26 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(GenericParams p, ui
     }
 }
 
+// The same walk over a pack as stored (pack format 1: the block directory and
+// the word stream, no device layout): a warp per block. For verification and
+// for callers that hold a pack in device memory as it is.
+__global__ void __launch_bounds__(128) decode_pack_kernel(GenericParams p, const uint32_t *words,
+                                                          const uint32_t *offsets, uint16_t *out) {
+    const int64_t warp = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (warp >= p.rows * p.NB) return;
+    const int64_t r = warp / p.NB, b = warp % p.NB;
+    const uint32_t *s = words + offsets[warp];
+    const int n = (int)((p.C - b * p.B) < p.B ? (p.C - b * p.B) : p.B);
+    BlockWalker w;
+    w.init(p, s, n);
+    uint16_t *dst = out + r * p.C + b * p.B;
+    for (int c0 = 0; c0 < n; c0 += 32) {
+        uint32_t bits = w.chunk(p, c0);
+        int i = c0 + (threadIdx.x & 31);
+        if (i < n) dst[i] = (uint16_t)bits;
+    }
+}
+
 // One warp per output row: every block of the row decoded and contracted with
 // up to 8 activation rows, fp32 accumulate per lane, a fixed butterfly
 // reduction, then bias in fp32 and one rounding. Column m's arithmetic does
@@ -380,6 +400,23 @@ int launch_decode_generic(const dm_tensor *t, uint16_t *out, void *stream, std::
     int64_t blocks = (warps + 3) / 4;
     decode_generic_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(p, out);
     return cuda_check(cudaGetLastError(), "decode_generic_kernel", msg);
+}
+
+int launch_decode_pack(const uint8_t *palette, size_t npal, int64_t R, int64_t C, const int32_t *widths, int32_t nw,
+                       int32_t B, const uint32_t *words, const uint32_t *offsets, uint16_t *out, void *stream,
+                       std::string &msg) {
+    GenericParams p{};
+    p.rows = R;
+    p.C = C;
+    p.B = B;
+    p.NB = (C + B - 1) / B;
+    p.nw = nw;
+    for (int i = 0; i < nw && i < 8; ++i) p.widths[i] = widths[i];
+    for (size_t i = 0; i < npal && i < 256; ++i) p.palette[i] = palette[i];
+    const int64_t warps = R * p.NB;
+    if (warps == 0) return DM_OK;
+    decode_pack_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, (cudaStream_t)stream>>>(p, words, offsets, out);
+    return cuda_check(cudaGetLastError(), "decode_pack_kernel", msg);
 }
 
 int launch_gemv_generic(const dm_tensor *t, const void *x, int x_f32, int64_t M, const uint16_t *bias, void *out,

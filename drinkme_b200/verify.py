@@ -6,9 +6,9 @@ packed tensors decoded to their BF16 bits — and streamed into SHA-256
 without being written out; the digest is compared with the one the
 checkpoint's publisher lists for the file.
 
-Here a producer thread lays each radix tensor out on the GPU (the loader),
-decodes it there (dm_decode) and copies the bits into one of a few pinned
-host buffers on a side stream, several parts ahead; the calling thread
+Here a producer thread copies each radix pack to the GPU as it is, decodes
+it there straight from its own arrays (dm_decode_pack) and copies the bits
+into one of a few pinned host buffers on a side stream, several parts ahead; the calling thread
 hashes the parts in file order as their copies land. SHA-256 of one file is
 sequential, so the hash sets the pace once the decode keeps ahead of it.
 Fetching digests and reading pack directories are the caller's (the
@@ -27,7 +27,7 @@ import time
 import numpy as np
 import torch
 
-from . import codec, radix_ops, swap
+from . import codec
 
 _AHEAD = 3  # pinned buffers: parts decoded and copied ahead of the hash
 
@@ -64,16 +64,15 @@ def rebuild_sha256(parts, device="cuda") -> dict:
             side = torch.cuda.Stream(dev)
             for part in parts:
                 if isinstance(part, dict) and part.get("codec") == codec.RADIX:
-                    rt = swap.to_device_radix(part, dev)
                     buf = free.get()
                     n = int(part["R"]) * int(part["C"])
                     with torch.cuda.stream(side):
-                        bits = radix_ops.decode_bits(rt)
-                        buf[:n].copy_(bits.view(torch.int16).reshape(-1), non_blocking=True)
+                        bits = codec.decode_pack_device(part, dev)
+                        buf[:n].copy_(bits.reshape(-1), non_blocking=True)
                         ev = torch.cuda.Event()
                         ev.record(side)
-                    ready.put(("radix", buf, n, ev, rt))
-                    del bits, rt
+                    ready.put(("radix", buf, n, ev, bits))
+                    del bits
                 else:
                     ready.put(("host", part))
         except BaseException as e:  # noqa: BLE001 - reported on the calling thread

@@ -290,6 +290,17 @@ int dm_pack_encode(const uint16_t *host_bits, int64_t R, int64_t C, const int32_
                    int32_t nwidths, int32_t block_size, int32_t threads, const uint8_t *host_palette,
                    const uint32_t *host_offsets, uint32_t *host_data, uint64_t nwords, char *err, size_t err_len);
 
+/* Decodes a pack as stored — its word stream and block directory copied to
+ * the device unchanged (d_data: nwords words, d_offsets: R*NB+1 entries),
+ * no device layout — to bf16 bit patterns d_out [R][C] (radix.py:241-278,
+ * radix_native.cpp:168-209). The host copies of the palette and directory
+ * are validated first (radix.py:174-238). A warp per block; for
+ * verification and for packs held in device memory as they are. */
+int dm_decode_pack(const uint8_t *host_palette, size_t npalette, const uint32_t *host_offsets, size_t noffsets,
+                   size_t nwords, int64_t R, int64_t C, const int32_t *host_widths, int32_t nwidths,
+                   int32_t block_size, const uint32_t *d_data, const uint32_t *d_offsets, uint16_t *d_out,
+                   void *stream, char *err, size_t err_len);
+
 /* The same encoder on the GPU (radix_native.cpp:57-166 `plan` / `encode`,
  * the writers behind radix.py:77-136 `pack_array`), for bits already in
  * device memory: dm_pack_plan_device histograms the exponents and counts

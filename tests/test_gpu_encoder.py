@@ -135,3 +135,21 @@ def test_verify_files_in_parallel():
     out = verify.verify_files(zip(files, wants[:2] + ["0" * 64]), DEV, workers=3)
     assert [o["verdict"] for o in out] == ["MATCH", "MATCH", "MISMATCH"]
     assert out[2]["sha256"] == wants[2]
+
+
+def test_decode_pack_as_stored(golden):
+    """dm_decode_pack: every golden pack (every profile, block size and ragged
+    shape) decoded on the GPU from its own arrays is its source bits; a
+    directory that does not fit the words is refused with validate's message."""
+    z, pins = golden
+    for name, m in pins["packs"].items():
+        if m.get("raw_fallback"):
+            continue
+        p = pack_of(z, pins, name)
+        got = codec.decode_pack_device(p, DEV).cpu().numpy().view(np.uint16)
+        assert np.array_equal(got, z[f"{name}/bits"]), name
+    p = dict(pack_of(z, pins, "sip_normal_16x4096"))
+    p["rx_offsets"] = p["rx_offsets"].copy()
+    p["rx_offsets"][-1] += 7
+    with pytest.raises(ValueError):
+        codec.decode_pack_device(p, DEV)

@@ -356,6 +356,17 @@ def test_config1_down_proj_full_size():
     assert np.abs(y - ref).max() / np.abs(ref).max() <= 5e-3
     with open(os.path.join(GOLDEN, "pins.json")) as f:
         assert radix_ops.read_bytes(rt) == json.load(f)["config1"]["sip"]["read_bytes"]
+    # the reference's own arithmetic at full size with fp32 outputs: its
+    # native decoder's weight (oracle/_ref, bit-exact to the source) and an
+    # fp32-accumulated product, the contract of its GEMV (radix_kernel_gpu.py:
+    # 683-718); north_star's bar is 1e-3 max relative error
+    if oracle.reference_native() is not None:
+        Wref = oracle.reference_decode(p)
+        assert np.array_equal(Wref, bits)
+        Wf = torch.from_numpy(Wref.view(np.int16).copy()).view(torch.bfloat16).to(DEV).float()
+        y32 = (xd.float() @ Wf.T)[0].cpu().numpy()
+        rel = np.abs(y - y32).max() / np.abs(y32).max()
+        assert rel <= 1e-3, rel
 
 
 @pytest.mark.parametrize("shape", [(48, 5120), (32, 4096), (256, 6656)])
@@ -466,3 +477,26 @@ def test_runtime_dict_carries_the_reference_device_arrays():
         assert formula == radix_ops.read_bytes(rt)
         assert rt["rx_data"].numel() * 4 == rt["rx_handle"].info.layout_bytes
         assert swap.resident_bytes(rt) >= rt["rx_handle"].info.resident_bytes
+
+
+def test_config3_gulp_full_size_rows():
+    """BASELINE configs[2] at full size: the Qwen3-8B gate shape (12288 x
+    4096) packed gulp, M = 2, 4 and 8 activation rows seeded per row: fp32
+    outputs within 1e-3 max relative error of an fp32-accumulated product
+    with the decoded (bit-exact) weight, and every row bitwise the M = 1
+    call's."""
+    g = torch.Generator().manual_seed(12)
+    W = (torch.randn(12288, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    p = codec.pack_weight_radix(W, "gulp")
+    assert p["codec"] == "radix" and p["profile"] == "gulp"
+    rt = swap.to_device_radix(p, DEV)
+    Wf = W.to(DEV).float()
+    x = torch.cat([torch.randn(1, 4096, generator=torch.Generator().manual_seed(100 + m)) for m in range(8)])
+    xd = x.to(torch.bfloat16).to(DEV)
+    ones = [radix_ops.gemv_mc(rt, xd[m:m + 1]) for m in range(8)]
+    for M in (2, 4, 8):
+        y = radix_ops.gemv_mc(rt, xd[:M])
+        ref = xd[:M].float() @ Wf.T
+        assert (y - ref).abs().max() / ref.abs().max() <= 1e-3, M
+        for m in range(M):
+            assert torch.equal(y[m:m + 1], ones[m]), (M, m)
