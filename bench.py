@@ -605,7 +605,10 @@ def decode_step_8b(device, steps=20, warmup=3):
     out = {"config": "Qwen3-8B shapes, 36 layers, sip linears + raw bf16 lm_head, batch 1, KV cache of 1024 rows "
                      "(attention over the allocation with a live-length mask), one CUDA graph per step",
            "ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "steps": steps,
-           "graph_nodes_note": "norms, rotary, attention and sampling are torch operations; the linears are ours"}
+           "graph_nodes_note": "per layer: the sip linears (q|k|v, o, gate|up, down), residual add + RMSNorm twice, the "
+                               "attention block (q/k norm, rotary, cache write, split attention and combine in one "
+                               "launch) and SiLU * up are this package's kernels; the embedding lookup, greedy argmax "
+                               "and position counter are torch operations"}
     del st
     torch.cuda.empty_cache()
     return out

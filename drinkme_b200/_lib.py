@@ -18,7 +18,7 @@ DM_MAX_RANKS = 8
 
 EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
-           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_pack_plan_device", "dm_pack_encode_device", "dm_decode_pack", "dm_step_add_rmsnorm", "dm_step_qk_rope_cache", "dm_step_attention_workspace_bytes", "dm_step_attention", "dm_step_silu_mul", "dm_tensor_check",
+           "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_pack_plan_device", "dm_pack_encode_device", "dm_decode_pack", "dm_step_add_rmsnorm", "dm_step_qk_rope_cache", "dm_step_attention_workspace_bytes", "dm_step_attention", "dm_step_silu_mul", "dm_step_attention_block_workspace_bytes", "dm_step_attention_block", "dm_tensor_check",
            "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_tensor_set_launch", "dm_gemv_plan", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
 
 
@@ -99,6 +99,8 @@ def lib():
         L.dm_step_attention_workspace_bytes.argtypes = [i32, i32, i64]
         L.dm_step_attention.argtypes = [p, p, p, p, i64, p, p, i32, i32, i32, p, cp, sz]
         L.dm_step_silu_mul.argtypes = [p, p, i64, p, cp, sz]
+        L.dm_step_attention_block_workspace_bytes.argtypes = [i32, i32, i32, i64]
+        L.dm_step_attention_block.argtypes = [p, p, p, p, p, p, p, p, i64, p, p, i32, i32, i32, ct.c_float, p, cp, sz]
         L.dm_tensor_check.argtypes = [p, ct.POINTER(ct.c_int32), cp, sz]
         L.dm_prefill.argtypes = [p, p, i64, p, p, i32, p, i64, p, cp, sz]
         L.dm_prefill_workspace_bytes.argtypes = [p, i64]
@@ -114,6 +116,7 @@ def lib():
             getattr(L, name).restype = ct.c_int
         L.dm_prefill_workspace_bytes.restype = ct.c_int64
         L.dm_step_attention_workspace_bytes.restype = ct.c_int64
+        L.dm_step_attention_block_workspace_bytes.restype = ct.c_int64
         _LIB = L
     return _LIB
 

@@ -155,6 +155,107 @@ __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint1
     for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(acc[e] / L);
 }
 
+// The whole attention block of a layer in one launch: CTA (kv head g, chunk
+// j), a warp per query head of the group. Each warp norms and rotates its q
+// head from the fused q|k|v row; the CTA whose chunk holds *pos also norms
+// and rotates k and writes k and v into row *pos of the caches first; every
+// CTA then runs its chunk of the split attention; the last CTA of kv head g
+// to finish (a counter that it resets) combines the chunks for the group.
+__global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const uint16_t *kn, const float *cosv,
+                                  const float *sinv, const int64_t *pos, uint16_t *kc, uint16_t *vc, float *part,
+                                  unsigned int *count, uint16_t *out, int nh, int nkv, int hd, int nchunks, float eps,
+                                  float scale) {
+    pdl_launch_dependents();
+    __shared__ int last;
+    const int g = blockIdx.x, j = blockIdx.y, lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
+    const int grp = nh / nkv, half = hd / 2, per = hd / 32;
+    const int64_t p = *pos, live = p + 1;
+    // rotate-half pairs: lane l holds elements l*per .. l*per+3; the partner
+    // of element e is e +- hd/2, held by lane (l +- 16)
+    auto norm_rope = [&](const uint16_t *src, const uint16_t *wn, float v[4]) {
+        // the sum of squares in qk_norm_rope_cache_kernel's order (lane l
+        // adds elements l, l + 32, ...), so that the bits match it
+        float ss = 0.f;
+        for (int i = lane; i < hd; i += 32) {
+            const float x = bf(src[i]);
+            ss += x * x;
+        }
+        for (int e = 0; e < per; ++e) v[e] = bf(src[lane * per + e]);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(ss / (float)hd + eps);
+        for (int e = 0; e < per; ++e) v[e] = bf(to_bf(bf(to_bf(v[e] * r)) * bf(wn[lane * per + e])));
+        // rotate-half: the partner of element e (lane l) sits in lane l ^ 16
+        float o4[4];
+        for (int e = 0; e < per; ++e) {
+            const int idx = lane * per + e;
+            const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            const int i = idx < half ? idx : idx - half;
+            const float c = cosv[p * half + i], sn = sinv[p * half + i];
+            o4[e] = idx < half ? v[e] * c - partner * sn : v[e] * c + partner * sn;
+        }
+        for (int e = 0; e < per; ++e) v[e] = bf(to_bf(o4[e]));
+    };
+    const int head = g * grp + wq;
+    float qv[4];
+    norm_rope(qkv + (int64_t)head * hd, qn, qv);
+    const int64_t r0 = (int64_t)j * kAttnChunk, r1 = min(live, r0 + kAttnChunk);
+    if (p >= r0 && p < r0 + kAttnChunk && wq == 0) {  // this chunk holds the new row
+        float kv4[4];
+        norm_rope(qkv + (int64_t)(nh + g) * hd, kn, kv4);
+        uint16_t *kd = kc + (p * nkv + g) * hd, *vd = vc + (p * nkv + g) * hd;
+        const uint16_t *vs = qkv + (int64_t)(nh + nkv + g) * hd;
+        for (int e = 0; e < per; ++e) {
+            kd[lane * per + e] = to_bf(kv4[e]);
+            vd[lane * per + e] = vs[lane * per + e];
+        }
+    }
+    __syncthreads();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, m = -INFINITY, l = 0.f;
+    for (int e = 0; e < per; ++e) qv[e] *= scale;
+    for (int64_t r = r0; r < r1; ++r) {
+        const uint16_t *kr = kc + (r * nkv + g) * hd + lane * per;
+        float sc = 0.f;
+        for (int e = 0; e < per; ++e) sc += qv[e] * bf(kr[e]);
+        for (int o = 16; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        const float mn = fmaxf(m, sc);
+        const float a = __expf(m - mn), b = __expf(sc - mn);
+        const uint16_t *vr = vc + (r * nkv + g) * hd + lane * per;
+        for (int e = 0; e < per; ++e) acc[e] = acc[e] * a + b * bf(vr[e]);
+        l = l * a + b;
+        m = mn;
+    }
+    float *pp = part + ((int64_t)head * nchunks + j) * (hd + 2);
+    if (lane == 0) {
+        pp[0] = m;
+        pp[1] = l;
+    }
+    for (int e = 0; e < per; ++e) pp[2 + lane * per + e] = acc[e];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int old = atomicAdd(count + g, 1u);
+        last = old == (unsigned int)(nchunks - 1);
+        if (last) count[g] = 0u;  // for the next launch
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int used = (int)min((int64_t)nchunks, (p + kAttnChunk) / kAttnChunk);
+    const float *ph = part + (int64_t)head * nchunks * (hd + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < used; ++c) M = fmaxf(M, __ldcg(ph + c * (hd + 2)));
+    float o4[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+    for (int c = 0; c < used; ++c) {
+        const float *pc = ph + c * (hd + 2);
+        const float lc = __ldcg(pc + 1);
+        if (lc == 0.f) continue;
+        const float a = __expf(__ldcg(pc) - M);
+        L += a * lc;
+        for (int e = 0; e < per; ++e) o4[e] += a * __ldcg(pc + 2 + lane * per + e);
+    }
+    for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(o4[e] / L);
+}
+
 __global__ void silu_mul_kernel(const uint16_t *gu, uint16_t *out, int n) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -227,6 +328,33 @@ extern "C" int dm_step_attention(const void *q, const void *kcache, const void *
     dm::attn_combine_kernel<<<nh, 32, 0, s>>>(work, pos, (uint16_t *)out, nh, hd, nchunks);
     std::string msg;
     int rc = dm::launched("attention kernels", msg);
+    if (rc) dm::set_error(err, err_len, msg);
+    return rc;
+}
+
+extern "C" int64_t dm_step_attention_block_workspace_bytes(int32_t nh, int32_t nkv, int32_t hd, int64_t max_len) {
+    return (dm_step_attention_workspace_bytes(nh, hd, max_len) + 255) / 256 * 256 + (int64_t)nkv * 4;
+}
+
+extern "C" int dm_step_attention_block(const void *qkv, const void *qn, const void *kn, const float *cos_table,
+                                       const float *sin_table, const int64_t *pos, void *kcache, void *vcache,
+                                       int64_t max_len, void *out, void *work, int32_t nh, int32_t nkv, int32_t hd,
+                                       float eps, void *stream, char *err, size_t err_len) {
+    if (!qkv || !qn || !kn || !cos_table || !sin_table || !pos || !kcache || !vcache || !out || !work || nh < 1 ||
+        nkv < 1 || nh % nkv || hd != 128 || nh / nkv > 32 || max_len < 1) {
+        dm::set_error(err, err_len, "dm_step_attention_block: bad arguments (head_dim 128, up to 32 heads per kv head)");
+        return DM_EINVAL;
+    }
+    const int nchunks = (int)((max_len + dm::kAttnChunk - 1) / dm::kAttnChunk);
+    float *part = reinterpret_cast<float *>(work);
+    unsigned int *count = reinterpret_cast<unsigned int *>(
+        reinterpret_cast<uint8_t *>(work) + (dm_step_attention_workspace_bytes(nh, hd, max_len) + 255) / 256 * 256);
+    dm::attn_block_kernel<<<dim3(nkv, nchunks), 32 * (nh / nkv), 0, (cudaStream_t)stream>>>(
+        (const uint16_t *)qkv, (const uint16_t *)qn, (const uint16_t *)kn, cos_table, sin_table, pos,
+        (uint16_t *)kcache, (uint16_t *)vcache, part, count, (uint16_t *)out, nh, nkv, hd, nchunks, eps,
+        1.0f / sqrtf((float)hd));
+    std::string msg;
+    int rc = dm::launched("attn_block_kernel", msg);
     if (rc) dm::set_error(err, err_len, msg);
     return rc;
 }

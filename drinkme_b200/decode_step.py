@@ -18,8 +18,9 @@ decodes token after token with no host work.
 
 The Linears are the hot path (the sip GEMV, the raw lm_head GEMV); the
 operations between them are this package's small fused kernels (csrc/
-step_ops.cu: residual add + RMSNorm, q/k RMSNorm + rotary + KV-cache write,
-split-K decode attention, SiLU * up) — nine launches per layer; the
+step_ops.cu: residual add + RMSNorm; the attention block — q/k RMSNorm,
+rotary, KV-cache write, split-K decode attention and its combine — in one
+launch; SiLU * up) — eight launches per layer; the
 reference runs transformers' own modules there. The embedding lookup, the
 greedy argmax and the position counter are torch operations. Weights are synthetic (random N(0, 0.02),
 packed sip by this package's encoder); `reference_logits` recomputes one
@@ -105,7 +106,7 @@ class DecodeStack:
         self.h = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
         self.x = torch.empty(1, H, dtype=torch.bfloat16, device=dev)  # the normed input of the next Linear
         self.q = torch.empty(nh, hd, dtype=torch.bfloat16, device=dev)
-        self.work = torch.empty(int(_lib.lib().dm_step_attention_workspace_bytes(nh, hd, max_len)) // 4 + 1,
+        self.work = torch.zeros(int(_lib.lib().dm_step_attention_block_workspace_bytes(nh, nkv, hd, max_len)) // 4 + 1,
                                 dtype=torch.float32, device=dev)
         self.qkv = torch.empty(1, (nh + 2 * nkv) * hd, dtype=torch.bfloat16, device=dev)
         self.attn = torch.empty(1, nh * hd, dtype=torch.bfloat16, device=dev)
@@ -131,11 +132,9 @@ class DecodeStack:
             _lib.call("dm_step_add_rmsnorm", ptr(self.h), ptr(delta) if delta is not None else P(0), ptr(lay["ln1"]),
                       ptr(self.x), H, ct.c_float(EPS), st)
             radix_ops.gemv_into(lay["qkv"], self.x, None, self.qkv)
-            _lib.call("dm_step_qk_rope_cache", ptr(self.qkv), ptr(lay["qn"]), ptr(lay["kn"]), ptr(self.cos),
-                      ptr(self.sin), ptr(self.pos), ptr(self.q), ptr(self.kcache[li]), ptr(self.vcache[li]),
-                      nh, nkv, hd, ct.c_float(EPS), st)
-            _lib.call("dm_step_attention", ptr(self.q), ptr(self.kcache[li]), ptr(self.vcache[li]), ptr(self.pos),
-                      self.max_len, ptr(self.attn), ptr(self.work), nh, nkv, hd, st)
+            _lib.call("dm_step_attention_block", ptr(self.qkv), ptr(lay["qn"]), ptr(lay["kn"]), ptr(self.cos),
+                      ptr(self.sin), ptr(self.pos), ptr(self.kcache[li]), ptr(self.vcache[li]), self.max_len,
+                      ptr(self.attn), ptr(self.work), nh, nkv, hd, ct.c_float(EPS), st)
             radix_ops.gemv_into(lay["o"], self.attn, None, self.o)
             _lib.call("dm_step_add_rmsnorm", ptr(self.h), ptr(self.o), ptr(lay["ln2"]), ptr(self.x), H,
                       ct.c_float(EPS), st)

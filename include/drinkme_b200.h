@@ -344,6 +344,16 @@ int dm_step_attention(const void *q, const void *kcache, const void *vcache, con
                       void *out, float *work, int32_t nh, int32_t nkv, int32_t head_dim, void *stream, char *err,
                       size_t err_len);
 int dm_step_silu_mul(const void *gu, void *out, int64_t n, void *stream, char *err, size_t err_len);
+/* dm_step_qk_rope_cache and dm_step_attention in one launch: the q/k norms,
+ * rotary and cache write of row *pos, the split attention and its combine
+ * (the last CTA of each kv head combines, then resets its counter). `work`
+ * holds dm_step_attention_block_workspace_bytes bytes, zeroed before the
+ * first call. Same result bits as the two entry points. */
+int64_t dm_step_attention_block_workspace_bytes(int32_t nh, int32_t nkv, int32_t head_dim, int64_t max_len);
+int dm_step_attention_block(const void *qkv, const void *qn, const void *kn, const float *cos_table,
+                            const float *sin_table, const int64_t *pos, void *kcache, void *vcache, int64_t max_len,
+                            void *out, void *work, int32_t nh, int32_t nkv, int32_t head_dim, float eps, void *stream,
+                            char *err, size_t err_len);
 
 /* Reads and clears the tensor's device error word (a kernel's bounded
  * wait that gave up writes it). Synchronises the tensor's device. */
