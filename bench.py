@@ -74,6 +74,10 @@ def parse():
     ap.add_argument("--no-fuse", action="store_true", help="one launch per linear instead of q|k|v and gate|up")
     ap.add_argument("--gather", choices=("peer", "nccl"), default="peer",
                     help="N > 1: the output gather fused into the GEMV over NVLink (peer), or NCCL all-gather")
+    ap.add_argument("--launch", choices=("auto", "chain", "linear"), default="auto",
+                    help="the step as one persistent launch over every linear (dm_chain_run), or one launch per "
+                         "linear (the per-linear plugin route); auto: per-linear on one GPU, the chain on more "
+                         "(the faster of the two measured at each); the other is timed beside it")
     ap.add_argument("--variants", type=int, default=2,
                     help="distinct random tensors per shape; every layer still gets its own HBM copy")
     ap.add_argument("--no-secondary", action="store_true", help="skip the qwen3-8b chain beside the headline")
@@ -204,7 +208,7 @@ class Chain:
     """One decode token's linear stack with static buffers, for graph capture:
     per layer, one launch per group (q|k|v, o, gate|up, down when fused)."""
 
-    def __init__(self, wl, layers, rank, world, device, head_weight=None, fuse=True, gather="peer"):
+    def __init__(self, wl, layers, rank, world, device, head_weight=None, fuse=True, gather="peer", launch="linear"):
         import torch
 
         from drinkme_b200 import shard
@@ -240,6 +244,22 @@ class Chain:
         self.last = None
         self.gather = gather if world > 1 else None
         self.plan = None
+        self.persistent = None
+        if launch == "chain":
+            # every linear of the step in one persistent launch; link k waits
+            # for link k - 1 (the previous launch's last for link 0), as each
+            # linear of a decode step waits for its predecessor's output
+            from drinkme_b200 import shard as _shard
+
+            if any(rt is None for row in layers for rt in row):
+                raise ValueError("the chain needs rows of every linear on every rank")
+            G = len(self.groups)
+            n = len(layers) * G
+            self.plan = _shard.PeerGather([self.slot[i % G] if world > 1 else layers[i // G][i % G]["R"]
+                                           for i in range(n)], 1, torch.bfloat16, rank, world, device)
+            self.persistent = self.plan.chain([(layers[k // G][k % G], self.inputs(k % G), k, (k - 1) % n, None)
+                                               for k in range(n)])
+            return
         if self.gather == "peer":
             from drinkme_b200 import shard as _shard
 
@@ -250,6 +270,9 @@ class Chain:
                                           rank, world, device)
 
     def close(self):
+        if self.persistent is not None:
+            self.persistent.close()
+            self.persistent = None
         if self.plan is not None:
             self.plan.close()
             self.plan = None
@@ -259,7 +282,7 @@ class Chain:
         return self.x_hidden if name in HIDDEN_INPUT else self.x_other[C]
 
     def launches_per_step(self):
-        n = sum(1 for row in self.layers for rt in row if rt is not None)
+        n = 1 if self.persistent is not None else sum(1 for row in self.layers for rt in row if rt is not None)
         return n + (1 if self.head is not None else 0)
 
     def step(self):
@@ -273,6 +296,13 @@ class Chain:
 
         G = len(self.groups)
         n = len(self.layers) * G
+        if self.persistent is not None:
+            self.persistent.run()
+            self.last = self.plan.output(n - 1)
+            if self.head is not None:
+                self.head_out = radix_ops.gemv_raw(self.head, self.x_hidden, None, torch.bfloat16)
+                self.last = self.head_out
+            return self.last
         for li, row in enumerate(self.layers):
             for gi, rt in enumerate(row):
                 if self.plan is not None:
@@ -785,13 +815,23 @@ def main():
 
     fuse = not a.no_fuse
     layers, stats = build_stack(a.workload, rank, world, device, a.variants, log, fuse)
-    chain = Chain(a.workload, layers, rank, world, device, fuse=fuse, gather=a.gather)
+    if a.launch == "auto":
+        a.launch = "linear" if world == 1 or a.gather != "peer" else "chain"
+    chain = Chain(a.workload, layers, rank, world, device, fuse=fuse, gather=a.gather, launch=a.launch)
     clocks = ClockSampler(local)
     clocks.start()
     ms, _ = time_graph(chain, a.steps, a.warmup, world, rank, device)
     clk = clocks.stop()
     ms_e2e, io = time_graph(chain, a.steps, max(3, a.warmup), world, rank, device, h2d=True)
     per_kernel, tot_bytes, tot_ms, launches = kernel_times(chain, device)
+    # the same step in the other launch mode
+    other = "linear" if a.launch == "chain" else ("chain" if world == 1 or a.gather == "peer" else None)
+    ms_other = None
+    if other is not None:
+        alt = Chain(a.workload, layers, rank, world, device, fuse=fuse, gather=a.gather, launch=other)
+        ms_other, _ = time_graph(alt, a.steps, a.warmup, world, rank, device)
+        alt.close()
+        del alt
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -800,7 +840,10 @@ def main():
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    # the dominant kernel: the chain launch (the whole step) or the
+    # per-linear launches (their device time summed)
+    k_ms = ms if a.launch == "chain" else tot_ms
+    achieved = tot_bytes / (k_ms * 1e-3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
     if os.path.exists(tpath):
@@ -821,12 +864,20 @@ def main():
             "config": base_config,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "sip_gemv_kernel", "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
-                         "bytes_per_step_algorithmic": int(tot_bytes), "kernel_ms_per_step": round(tot_ms, 4)},
+                         "kernel": "sip_chain_kernel" if a.launch == "chain" else "sip_gemv_kernel",
+                         "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
+                         "bytes_per_step_algorithmic": int(tot_bytes), "kernel_ms_per_step": round(k_ms, 4)},
+            "launch": ("one persistent launch per step over every linear (dm_chain_run; link k waits for link "
+                       "k - 1's flags)" if a.launch == "chain" else "one launch per linear (dm_gemv / "
+                       "dm_gemv_gather)"),
             "per_linear": per_kernel,
             "e2e": {"value": round(1e3 / ms_e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": io[0],
                     "d2h_bytes_per_step": io[1]},
             "gpu_launches": chain.launches_per_step() * a.steps,
+            "other_launch": None if ms_other is None else {
+                "launch": other, "tokens_per_s": round(1e3 / ms_other, 3), "ms_per_step": round(ms_other, 4),
+                "note": "the same step and bits in the other launch mode (chain: one sip_chain_kernel launch; "
+                        "linear: one sip_gemv_kernel launch per linear)"},
             "clocks": clk,
             "pack": {"variants_per_shape": a.variants, "bpw_mean": round(
                 sum(v["bpw"] for v in stats.values()) / len(stats), 4), "distinct_words": words},
@@ -840,8 +891,12 @@ def main():
             l8, _ = build_stack("qwen3-8b", 0, 1, device, a.variants, log, fuse)
             g = torch.Generator(device=device).manual_seed(3)
             head = (torch.randn(WORKLOADS["qwen3-8b"]["head"], generator=g, device=device) * 0.02).to(torch.bfloat16)
-            c8 = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head, fuse=fuse)
+            c8 = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head, fuse=fuse, launch=a.launch)
             ms8, _ = time_graph(c8, a.steps, a.warmup, 1, 0, device)
+            c8o = Chain("qwen3-8b", l8, 0, 1, device, head_weight=head, fuse=fuse, launch=other)
+            ms8_other, _ = time_graph(c8o, a.steps, a.warmup, 1, 0, device)
+            c8o.close()
+            del c8o
             pk8, b8, t8, _ = kernel_times(c8, device)
             # the raw bf16 lm_head alone: this package's raw GEMV and cuBLAS
             from drinkme_b200 import radix_ops
@@ -851,6 +906,9 @@ def main():
             h_cublas = _graph_us(lambda: torch.nn.functional.linear(xh, head), device)
             result["qwen3_8b_chain"] = {"config": "BASELINE configs[1]: 36 layers + raw lm_head 151936x4096",
                                         "tokens_per_s": round(1e3 / ms8, 3), "ms_per_step": round(ms8, 4),
+                                        "launch": a.launch,
+                                        "other_launch": {"launch": other,
+                                                         "tokens_per_s": round(1e3 / ms8_other, 3)},
                                         "fused_gemv_gbs": round(b8 / (t8 * 1e-3) / 1e9, 1),
                                         "frac_of_peak": round(b8 / (t8 * 1e-3) / 1e9 / peak, 4),
                                         "per_linear": pk8,

@@ -19,7 +19,8 @@ DM_MAX_RANKS = 8
 EXPORTS = ("dm_version", "dm_tensor_create", "dm_tensor_create_multi", "dm_tensor_clone", "dm_tensor_destroy", "dm_tensor_get_info", "dm_gemv",
            "dm_gemv_noalloc", "dm_decode",
            "dm_prepare_schedule", "dm_gemv_raw", "dm_pack_plan", "dm_pack_encode", "dm_pack_plan_device", "dm_pack_encode_device", "dm_decode_pack", "dm_step_add_rmsnorm", "dm_step_qk_rope_cache", "dm_step_attention_workspace_bytes", "dm_step_attention", "dm_step_silu_mul", "dm_step_attention_block_workspace_bytes", "dm_step_attention_block", "dm_tensor_check",
-           "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_tensor_set_launch", "dm_gemv_plan", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free")
+           "dm_prefill", "dm_prefill_workspace_bytes", "dm_gemv_gather", "dm_tensor_set_launch", "dm_gemv_plan", "dm_ipc_handle", "dm_ipc_open", "dm_ipc_close", "dm_device_alloc", "dm_device_free",
+           "dm_chain_create", "dm_chain_run", "dm_chain_destroy")
 
 
 class DrinkmeError(RuntimeError):
@@ -48,7 +49,8 @@ class PackPart(ct.Structure):
 
 class Launch(ct.Structure):
     """dm_launch: a sip tensor's launch knobs."""
-    _fields_ = [("slots", ct.c_int32), ("split", ct.c_int32), ("skew", ct.c_int32), ("resident", ct.c_int32)]
+    _fields_ = [("slots", ct.c_int32), ("split", ct.c_int32), ("skew", ct.c_int32), ("resident", ct.c_int32),
+                ("prefetch", ct.c_int32)]
 
 
 class LaunchPlan(ct.Structure):
@@ -63,6 +65,11 @@ class Gather(ct.Structure):
                 ("peer_out", ct.c_void_p * DM_MAX_RANKS), ("peer_flags", ct.c_void_p * DM_MAX_RANKS),
                 ("gen", ct.c_void_p), ("done", ct.c_void_p), ("wait_flags", ct.c_void_p), ("wait_gen", ct.c_void_p),
                 ("abort", ct.c_void_p), ("wait_polls", ct.c_uint32)]
+
+
+class ChainLink(ct.Structure):
+    """dm_chain_link: one linear of a persistent chain launch."""
+    _fields_ = [("t", ct.c_void_p), ("x", ct.c_void_p), ("bias", ct.c_void_p), ("g", Gather), ("wait", ct.c_int32)]
 
 
 _LIB = None
@@ -110,6 +117,9 @@ def lib():
         L.dm_ipc_close.argtypes = [p, cp, sz]
         L.dm_device_alloc.argtypes = [i32, sz, ct.POINTER(p), cp, sz]
         L.dm_device_free.argtypes = [p, cp, sz]
+        L.dm_chain_create.argtypes = [ct.POINTER(ChainLink), i32, i64, i32, ct.POINTER(p), cp, sz]
+        L.dm_chain_run.argtypes = [p, p, cp, sz]
+        L.dm_chain_destroy.argtypes = [p, cp, sz]
         L.dm_tensor_set_launch.argtypes = [p, ct.POINTER(Launch), cp, sz]
         L.dm_gemv_plan.argtypes = [p, i64, i32, ct.POINTER(LaunchPlan), cp, sz]
         for name in EXPORTS:

@@ -351,7 +351,10 @@ extern "C" int dm_tensor_set_launch(dm_tensor *t, const dm_launch *l, char *err,
     t->K.slots = l->slots;
     t->K.split = l->split;
     t->K.skew = l->skew;
+    if (l->prefetch < -1 || l->prefetch > 32)
+        return fail(err, err_len, DM_EINVAL, "dm_tensor_set_launch: prefetch must be -1 (default) or 0..32");
     t->K.resident = l->resident;
+    t->K.prefetch = l->prefetch;
     return DM_OK;
 }
 

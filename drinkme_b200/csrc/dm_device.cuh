@@ -104,6 +104,21 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 __device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Asks `bytes` (a multiple of 16, from a 16-byte aligned address) into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Retires an mbarrier so that its shared memory can be initialised again or
+// reused for data (no thread waits on it and no copy completes on it).
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 
 // Orders generic-proxy accesses of global memory (e.g. another GPU's stores
 // made visible by an acquire) before this thread's later bulk copies.

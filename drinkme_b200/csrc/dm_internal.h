@@ -79,6 +79,7 @@ struct LaunchKnobs {
     int32_t split = kSplitAuto;
     int32_t skew = -1;      // stream-K: units fewer than the average for the last CTA (-1: 4)
     int32_t resident = -1;  // most block columns with resident activations (-1: 16; 0: never)
+    int32_t prefetch = -1;  // units each CTA asks into L2 before its dependency wait (-1: 0, none)
 };
 
 struct Scratch {
@@ -151,7 +152,7 @@ int launch_prepare_schedule(const uint32_t *data, size_t nwords, const uint32_t 
 int launch_gemv_raw(const void *w, int64_t R, int64_t C, const void *x, int x_f32, int64_t M, const uint16_t *bias,
                     void *out, int out_f32, void *stream, std::string &msg);
 int sip_shared_bytes(const dm_tensor *t, int Mv, int slots, int max_res, int *slot_bytes, int *nslots,
-                     int *xres_bytes, int dir_cap);
+                     int *xres_bytes, int dir_cap, int reserve = 0);
 int gemv_plan(const dm_tensor *t, int Mv, dm_launch_plan *out, std::string &msg);
 int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
                          const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,

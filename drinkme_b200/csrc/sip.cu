@@ -54,6 +54,7 @@
 #include <algorithm>
 #include <atomic>
 #include <string>
+#include <vector>
 
 #include "dm_device.cuh"
 #include "dm_internal.h"
@@ -62,7 +63,7 @@ namespace dm {
 
 constexpr int kMaxGrid = 256;  // CTAs of one launch, at most (one per SM)
 
-struct SipArgs {
+struct alignas(16) SipArgs {
     const uint8_t *data;
     const uint32_t *unit16;
     int64_t units, rows, NB;
@@ -92,6 +93,13 @@ struct SipArgs {
     const uint32_t *wait_flags, *wait_gen;
     uint32_t *abort;
     uint32_t wait_polls;  // polls of one flag wait before it gives up
+    int32_t grid;         // CTAs of this linear (a chain launch may have more)
+    int32_t wait_prev;    // chain: the awaited flags are the previous launch's (the link waits on a later link)
+    int32_t prefetch;     // units after the staged ones asked into L2 before the dependency wait
+    // a one-rank chain: the awaited link's CTA count (never reset: grid per
+    // launch) and its grid, polled directly instead of a flag
+    const uint32_t *wait_done;
+    int32_t wait_grid;
 };
 
 // A GROUP of kGroupWarps consumer warps shares each staged unit: warp w of
@@ -110,6 +118,12 @@ constexpr int kSipThreads = 32 * (2 + kGroups * kGroupWarps);
 constexpr int kMaxSlots = 6;
 // Units fewer than the average that the last stream-K worker gets (part_sum).
 constexpr double kSkewUnits = 4.0;
+// Units past the first staged ones whose weights a CTA asks into L2 before it
+// waits for its activations. Off by default: measured on the Qwen3 8B and
+// 32B stacks, 4, 8 and 16 units each made the step 3-9 % slower, per-linear
+// launches and chains alike (the extra requests compete with the previous
+// linear's tail instead of filling it).
+constexpr int kPrefetchUnits = 0;
 
 // The stream-K split: worker b's share of the U units is proportional to
 // wt(b) = 4096 for b <= b0 and 4096 - r (b - b0) after. CTAs are dispatched
@@ -220,13 +234,33 @@ __device__ __forceinline__ void store_output(const SipArgs &a, int64_t tile, int
 
 // The wait for the flags of the linear this launch's input depends on: each
 // rank's flag word reaches this rank's own launch count of that linear
-// (bounded; gives up with an error code).
-__device__ __forceinline__ void wait_inputs(const SipArgs &a) {
-    if (a.world <= 0 || a.wait_flags == nullptr) return;
-    const uint32_t want = ld_acquire_gpu(a.wait_gen);
+// (bounded; gives up with an error code). In a chain launch (E > 0: the
+// chain's launch count after this launch) the target is E for a link earlier
+// in the chain and E - 1 for a later one (its output of the previous launch).
+// One rank: the flags never leave this GPU, GPU scope suffices.
+__device__ __forceinline__ void wait_inputs(const SipArgs &a, uint32_t E) {
+    if (a.world <= 0) return;
+    if (E && a.wait_done) {
+        // one rank: the awaited link is done when all its CTAs have counted
+        // themselves for this launch (E - 1 for the previous launch's)
+        const uint32_t want = (a.wait_prev ? E - 1u : E) * (uint32_t)a.wait_grid;
+        uint32_t i = 0;
+        while ((int32_t)(ld_acquire_gpu(a.wait_done) - want) < 0)
+            if (++i > a.wait_polls || (i % 64 == 0 && ld_acquire_gpu(a.abort) != 0u)) {
+                atomicExch(a.err, kErrWaitPeer);
+                atomicExch(a.abort, 1u);
+                return;
+            }
+        fence_proxy_async_global();
+        return;
+    }
+    if (a.wait_flags == nullptr) return;
+    const uint32_t want = E ? (a.wait_prev ? E - 1u : E) : ld_acquire_gpu(a.wait_gen);
+    if (want == 0u) return;  // a chain's first launch: no earlier output to wait for
     for (int r = 0; r < a.world; ++r) {
         uint32_t i = 0;
-        while ((int32_t)(ld_acquire_sys(a.wait_flags + r) - want) < 0) {
+        while ((int32_t)((a.world == 1 ? ld_acquire_gpu(a.wait_flags + r) : ld_acquire_sys(a.wait_flags + r)) -
+                         want) < 0) {
             // a rank gave up before: do not wait again
             if (++i > a.wait_polls || (i % 64 == 0 && ld_acquire_gpu(a.abort) != 0u)) {
                 atomicExch(a.err, kErrWaitPeer);
@@ -241,15 +275,26 @@ __device__ __forceinline__ void wait_inputs(const SipArgs &a) {
 // After this CTA's last output (called by one lane, after a __syncwarp of
 // the warp that stored them): the CTA count of the launch; the last CTA,
 // having acquired every count, raises every rank's flag of this linear to
-// the new launch count behind one system-scope fence.
-__device__ __forceinline__ void signal_outputs(const SipArgs &a) {
+// the new launch count (E in a chain launch) behind one fence.
+__device__ __forceinline__ void signal_outputs(const SipArgs &a, uint32_t E) {
     if (a.world <= 0) return;
+    if (E && a.world == 1) {
+        // a one-rank chain: the count itself is what later links poll; it
+        // grows by the grid every launch (never reset)
+        if (atom_add_acq_rel_gpu(a.done, 1u) + 1u == E * (uint32_t)a.grid) *a.gen = E;
+        return;
+    }
     // the count needs GPU scope only: the last CTA's system-scope fence
     // below carries every CTA's stores (ordered before it here) to the peers
-    if (atom_add_acq_rel_gpu(a.done, 1u) + 1u != gridDim.x) return;
+    if (atom_add_acq_rel_gpu(a.done, 1u) + 1u != (uint32_t)a.grid) return;
     *a.done = 0u;
-    const uint32_t g = *a.gen + 1u;
+    const uint32_t g = E ? E : *a.gen + 1u;
     *a.gen = g;
+    if (a.world == 1) {
+        fence_acq_rel_gpu();
+        st_relaxed_gpu(a.peer_flags[0] + a.rank, g);
+        return;
+    }
     // one system-scope fence releases every flag store after it (a release
     // store per rank would wait for the outstanding NVLink stores each time)
     fence_acq_rel_sys();
@@ -321,11 +366,18 @@ struct Seq {
     }
 };
 
+// The barriers of a linear's shared-memory plan: full [L][S], empty [S],
+// tfull and tempty [kTileRing], x_ready [kMaxResidentCols], contiguous.
+__device__ __forceinline__ uint64_t *sip_barriers(const SipArgs &a, uint8_t *smem) {
+    return reinterpret_cast<uint64_t *>(smem + (size_t)a.nslots * a.slot_bytes + a.xres_bytes);
+}
+
+// One linear's GEMV by this CTA (the kernel body; every role returns here).
 // RES: the activations of every block column are resident in shared memory
-// (loaded once per launch) instead of staged with each unit.
+// (loaded once per launch) instead of staged with each unit. E: 0 for a
+// launch of its own, else the chain's launch count after this launch.
 template <int MV, bool RES>
-__global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__device__ __forceinline__ void sip_run(const SipArgs &a, uint8_t *smem, uint32_t E) {
     constexpr int kP = 16 * MV;  // floats of one tile partial [MV][16]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.nslots;
@@ -341,7 +393,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     float *tslot = pwb + kGroups * 2 * kGroupWarps * kP;          // [kTileRing][kGroups][kP]
     float *ebuf = tslot + kTileRing * kGroups * kP;               // [kP] the epilogue's tile sum
     uint32_t *dir = reinterpret_cast<uint32_t *>(ebuf + kP);     // this CTA's unit starts
-    const int64_t U = a.units, W = gridDim.x, NB = a.NB;
+    const int64_t U = a.units, W = a.grid, NB = a.NB;
     const int64_t T = (U + NB - 1) / NB;
     const int64_t cu0 = a.starts[blockIdx.x], cu1 = a.starts[blockIdx.x + 1];
     const bool dir_in_smem = (cu1 - cu0 + 1) <= a.dir_cap;
@@ -407,9 +459,17 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                     if (p > 0) advance(p, u, col);
                     stage_w(u, p, &full[p]);
                 }
+                // the next units' weights into L2 meanwhile
+                const int32_t pf = std::min<int32_t>(q.n, first + a.prefetch);
+                for (int32_t p = first; p < pf; ++p) {
+                    advance(p, u, col);
+                    const uint32_t q0 = dir_in_smem ? dir[u - cu0] : a.unit16[u];
+                    const uint32_t q1 = dir_in_smem ? dir[u + 1 - cu0] : a.unit16[u + 1];
+                    bulk_prefetch_l2(a.data + (size_t)q0 * 16, (q1 - q0) * 16u);
+                }
             }
             pdl_wait();
-            wait_inputs(a);
+            wait_inputs(a, E);
             if constexpr (RES) {
                 // the block columns this CTA's units touch (its units are
                 // consecutive: min(n, NB) columns from A's first), each once
@@ -525,7 +585,7 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
                 }
             }
             __syncwarp();
-            if (lane == 0) signal_outputs(a);
+            if (lane == 0) signal_outputs(a, E);
             return;
         }
     }
@@ -771,6 +831,70 @@ __global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(SipArgs a) {
     }
 }
 
+template <int MV, bool RES>
+__global__ void __launch_bounds__(kSipThreads, 1) sip_gemv_kernel(const __grid_constant__ SipArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    sip_run<MV, RES>(a, smem, 0u);
+}
+
+// A CHAIN: a sequence of GEMVs (links) in one persistent launch, one CTA per
+// SM. Each CTA runs its share of link 0, then of link 1, ...: the link's
+// arguments are copied into shared memory behind the largest link's plan,
+// its barriers set up, the body run, its barriers retired. A link whose
+// activations are another link's output waits (bounded) on that link's flags
+// before staging them, exactly as a launch of its own waits on its
+// predecessor; its first units' weights are staged before the wait, under the
+// previous link's tail. words[0] counts the chain's launches (each link's
+// flags are raised to it), words[1] the CTAs that have left this launch: the
+// last one raises words[0], after every CTA has read it. Needs every CTA
+// resident at once (a cooperative launch).
+// A link's arguments global -> shared, 16 bytes per thread, asynchronously
+// (LDGSTS): the next link's copy lands while this one runs.
+__device__ __forceinline__ void chain_args_prefetch(const SipArgs *src, SipArgs *dst) {
+    const uint8_t *s = reinterpret_cast<const uint8_t *>(src);
+    uint8_t *d = reinterpret_cast<uint8_t *>(dst);
+    for (int k = threadIdx.x; k < (int)(sizeof(SipArgs) / 16); k += kSipThreads)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(d + 16 * k)), "l"(s + 16 * k)
+                     : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int MV>
+__global__ void __launch_bounds__(kSipThreads, 1) sip_chain_kernel(const SipArgs *links, int32_t n, uint32_t *words,
+                                                                   int32_t args_off) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    SipArgs *buf = reinterpret_cast<SipArgs *>(smem + args_off);  // [2]: this link's and the next one's
+    uint32_t *launches = reinterpret_cast<uint32_t *>(buf + 2);
+    if (threadIdx.x == 0) *launches = ld_acquire_gpu(words);
+    chain_args_prefetch(links, buf);
+    for (int32_t i = 0; i < n; ++i) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // link i's arguments landed; the previous link is done in this CTA
+        if (i + 1 < n) chain_args_prefetch(links + i + 1, buf + ((i + 1) & 1));
+        const SipArgs *sa = buf + (i & 1);
+        if ((int32_t)blockIdx.x >= sa->grid) continue;
+        const uint32_t E = *launches + 1u;
+        if (sa->xres_bytes > 0)
+            sip_run<MV, true>(*sa, smem, E);
+        else
+            sip_run<MV, false>(*sa, smem, E);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            // retire the link's barriers: its shared memory is the next link's
+            uint64_t *b = sip_barriers(*sa, smem);
+            const int S = sa->nslots, nb = full_sets(S) * S + S + 2 * kTileRing;
+            const int nres = sa->xres_bytes > 0 ? (int)sa->NB : 0;
+            for (int k = 0; k < nb + nres; ++k) mbar_inval(b + k);
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(words + 1, 1u) + 1u == gridDim.x) {
+        words[1] = 0u;
+        st_relaxed_gpu(words, *launches + 1u);
+    }
+}
+
 // Staging slots of a launch with resident activations: five, six at M = 1
 // for tensors of 8 or more block columns. Fewer slots than fit: on the Qwen3
 // 8B and 32B shapes 5-6 slots beat 7-8 by 3-8 % (and 4 lose up to 10 %).
@@ -785,9 +909,9 @@ inline int resident_slots(int Mv, int64_t NB) { return Mv == 1 && NB >= 8 ? 6 : 
 // part: the barriers, the groups' partial buffers, the tile ring, the
 // epilogue's sum and the directory.
 int sip_shared_bytes(const dm_tensor *t, int Mv, int slots, int max_res, int *slot_bytes, int *nslots,
-                     int *xres_bytes, int dir_cap) {
+                     int *xres_bytes, int dir_cap, int reserve) {
     const int unit = (t->L.max_unit_bytes + 127) & ~127;
-    const int budget = 227 * 1024;
+    const int budget = 227 * 1024 - reserve;
     const int kP = 16 * Mv;
     const int fixed = (3 * kMaxSlots + 2 * kTileRing + kMaxResidentCols) * 8 +
                       (kGroups * 2 * kGroupWarps + kTileRing * kGroups + 1) * kP * 4 + (dir_cap + 1) * 4 + 128;
@@ -820,7 +944,7 @@ struct SipPlan {
     int dir_cap = 0, smem = 0, slot_bytes = 0, nslots = 0, xres_bytes = 0;
 };
 
-static int plan_sip(const dm_tensor *t, int Mv, SipPlan &P, std::string &msg) {
+static int plan_sip(const dm_tensor *t, int Mv, SipPlan &P, std::string &msg, int reserve = 0) {
     const dm::TensorLayout &L = t->L;
     const LaunchKnobs &K = t->K;
     // One CTA per SM, each a stream-K worker owning at least one unit; or,
@@ -853,7 +977,7 @@ static int plan_sip(const dm_tensor *t, int Mv, SipPlan &P, std::string &msg) {
                                 : perA);
     P.dir_cap = (int)std::min<int64_t>(4096, P.per_cta + 2);
     P.smem = sip_shared_bytes(t, Mv, K.slots, K.resident >= 0 ? K.resident : kMaxResidentCols, &P.slot_bytes,
-                              &P.nslots, &P.xres_bytes, P.dir_cap);
+                              &P.nslots, &P.xres_bytes, P.dir_cap, reserve);
     if (P.smem < 0) {
         msg = "sip kernel: a unit does not fit in shared memory";
         return DM_EINVAL;
@@ -923,56 +1047,27 @@ int gemv_sip_rows(const dm_tensor *t, const void *x, int x_f32, int64_t M, const
     return rc;
 }
 
-// The launch with caller-supplied scratch (partials for `max_workers`
-// CTAs, per-tile counters that are zero on entry, the error word):
-// dm_gemv passes the tensor's own, dm_gemv_noalloc a static device array.
-int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
-                         const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
-                         int64_t max_workers, void *stream, std::string &msg, const dm_gather *gather) {
+// The kernel arguments of one GEMV with caller-supplied scratch (partials
+// for `max_workers` CTAs, per-tile counters that are zero on entry, the error
+// word) under the tensor's launch plan. `reserve` bytes of shared memory are
+// kept out of the plan (a chain launch keeps its link arguments there).
+static int prepare_sip_args(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
+                            const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
+                            int64_t max_workers, const dm_gather *gather, SipArgs &a, SipPlan &P, std::string &msg,
+                            int reserve = 0) {
     const dm::TensorLayout &L = t->L;
     if (Mv < 0 || Mv > kMaxVirtualRows) {  // 0: decode to bf16
         msg = "sip kernel: 1..8 virtual activation rows";
         return DM_EINVAL;
     }
-    SipPlan P;
-    if (int rc = plan_sip(t, Mv, P, msg)) return rc;
+    if (int rc = plan_sip(t, Mv, P, msg, reserve)) return rc;
     const int64_t tiles = L.tiles, grid = P.grid;
-    const int tile_split = P.tile_split;
-    const int32_t part_b0 = P.part_b0, part_r = P.part_r;
     if (grid > max_workers || grid > kMaxGrid) {
         msg = "sip kernel: " + std::to_string(grid) + " stream-K workers exceed the scratch's " +
               std::to_string(max_workers) + " (or the launch's " + std::to_string(kMaxGrid) + ")";
         return DM_EINVAL;
     }
-    const int dir_cap = P.dir_cap, smem = P.smem, slot_bytes = P.slot_bytes, nslots = P.nslots,
-              xres_bytes = P.xres_bytes;
-    using Kern = void (*)(SipArgs);
-    static const Kern kernels[2][kMaxVirtualRows + 1] = {
-        {sip_gemv_kernel<0, false>, sip_gemv_kernel<1, false>, sip_gemv_kernel<2, false>, sip_gemv_kernel<3, false>,
-         sip_gemv_kernel<4, false>, sip_gemv_kernel<5, false>, sip_gemv_kernel<6, false>, sip_gemv_kernel<7, false>,
-         sip_gemv_kernel<8, false>},
-        {nullptr, sip_gemv_kernel<1, true>, sip_gemv_kernel<2, true>, sip_gemv_kernel<3, true>,
-         sip_gemv_kernel<4, true>, sip_gemv_kernel<5, true>, sip_gemv_kernel<6, true>, sip_gemv_kernel<7, true>,
-         sip_gemv_kernel<8, true>}};
-    // the shared-memory limit is a per-device attribute of each kernel: one
-    // bit per device (devices 64 and up set it on every launch)
-    static std::atomic<uint64_t> attr_set[2][kMaxVirtualRows + 1];
-    const int res = xres_bytes > 0 ? 1 : 0;
-    const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
-    const Kern kern = kernels[res][Mv];
-    if (kern == nullptr) {
-        msg = "sip kernel: no resident-activation kernel without activations";
-        return DM_EINVAL;
-    }
-    if (!dev_bit || !(attr_set[res][Mv].load() & dev_bit)) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) {
-            msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-            return DM_ECUDA;
-        }
-        attr_set[res][Mv].fetch_or(dev_bit);
-    }
-    SipArgs a{};
+    a = SipArgs{};
     a.data = t->d_data;
     a.unit16 = t->d_unit16;
     a.units = L.units;
@@ -989,15 +1084,18 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     a.partials = partials;
     a.counters = counters;
     a.err = err;
-    a.slot_bytes = slot_bytes;
-    a.xres_bytes = xres_bytes;
+    a.slot_bytes = P.slot_bytes;
+    a.xres_bytes = P.xres_bytes;
     a.x_off = (L.max_unit_bytes + 127) & ~127;
-    a.nslots = nslots;
-    a.dir_cap = dir_cap;
-    a.tile_split = tile_split;
+    a.nslots = P.nslots;
+    a.dir_cap = P.dir_cap;
+    a.tile_split = P.tile_split;
+    a.grid = (int32_t)grid;
+    a.prefetch = Mv > 0 ? (t->K.prefetch >= 0 ? t->K.prefetch : kPrefetchUnits) : 0;
     for (int64_t w = 0; w <= grid; ++w)
-        a.starts[w] = (int32_t)(tile_split ? (w * tiles / grid) * L.NB
-                                           : L.units * part_sum(w, part_b0, part_r) / part_sum(grid, part_b0, part_r));
+        a.starts[w] = (int32_t)(P.tile_split ? (w * tiles / grid) * L.NB
+                                             : L.units * part_sum(w, P.part_b0, P.part_r) /
+                                                   part_sum(grid, P.part_b0, P.part_r));
     if (gather) {
         a.world = gather->world;
         a.rank = gather->rank;
@@ -1013,10 +1111,49 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
         a.abort = gather->abort;
         a.wait_polls = gather->wait_polls ? gather->wait_polls : kPeerPolls;
     }
+    return DM_OK;
+}
+
+// The launch with caller-supplied scratch: dm_gemv passes the tensor's own,
+// dm_gemv_noalloc a static device array.
+int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_stride, int Mv, int nsplit, int M_out,
+                         const uint16_t *bias, void *out, int out_f32, float *partials, int *counters, int *err,
+                         int64_t max_workers, void *stream, std::string &msg, const dm_gather *gather) {
+    SipArgs a;
+    SipPlan P;
+    if (int rc = prepare_sip_args(t, xv, x_stride, Mv, nsplit, M_out, bias, out, out_f32, partials, counters, err,
+                                  max_workers, gather, a, P, msg))
+        return rc;
+    using Kern = void (*)(SipArgs);
+    static const Kern kernels[2][kMaxVirtualRows + 1] = {
+        {sip_gemv_kernel<0, false>, sip_gemv_kernel<1, false>, sip_gemv_kernel<2, false>, sip_gemv_kernel<3, false>,
+         sip_gemv_kernel<4, false>, sip_gemv_kernel<5, false>, sip_gemv_kernel<6, false>, sip_gemv_kernel<7, false>,
+         sip_gemv_kernel<8, false>},
+        {nullptr, sip_gemv_kernel<1, true>, sip_gemv_kernel<2, true>, sip_gemv_kernel<3, true>,
+         sip_gemv_kernel<4, true>, sip_gemv_kernel<5, true>, sip_gemv_kernel<6, true>, sip_gemv_kernel<7, true>,
+         sip_gemv_kernel<8, true>}};
+    // the shared-memory limit is a per-device attribute of each kernel: one
+    // bit per device (devices 64 and up set it on every launch)
+    static std::atomic<uint64_t> attr_set[2][kMaxVirtualRows + 1];
+    const int res = P.xres_bytes > 0 ? 1 : 0;
+    const uint64_t dev_bit = t->device >= 0 && t->device < 64 ? 1ull << t->device : 0ull;
+    const Kern kern = kernels[res][Mv];
+    if (kern == nullptr) {
+        msg = "sip kernel: no resident-activation kernel without activations";
+        return DM_EINVAL;
+    }
+    if (!dev_bit || !(attr_set[res][Mv].load() & dev_bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) {
+            msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+            return DM_ECUDA;
+        }
+        attr_set[res][Mv].fetch_or(dev_bit);
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = dim3((unsigned)P.grid);
     cfg.blockDim = dim3(kSipThreads);
-    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.dynamicSmemBytes = (size_t)P.smem;
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1026,6 +1163,123 @@ int launch_gemv_sip_with(const dm_tensor *t, const uint16_t *xv, int64_t x_strid
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {
         msg = std::string("sip_gemv_kernel: ") + cudaGetErrorString(e);
+        return DM_ECUDA;
+    }
+    return DM_OK;
+}
+
+// Room behind a chain's largest plan: two links' arguments (this one's and
+// the next one's) and the launch count read at entry.
+constexpr int kChainArgsBytes = (2 * (int)sizeof(SipArgs) + 16 + 127) & ~127;
+
+int chain_prepare(const dm_chain_link *links, int32_t n, int64_t M, int32_t out_f32, std::vector<SipArgs> &args,
+                  int *grid, int *smem, std::string &msg) {
+    args.resize((size_t)n);
+    *grid = 0;
+    *smem = 0;
+    for (int32_t i = 0; i < n; ++i) {
+        const dm_chain_link &k = links[i];
+        const std::string at = "dm_chain_create: link " + std::to_string(i) + ": ";
+        if (!k.t || !k.x) {
+            msg = at + "null tensor or activations";
+            return DM_EINVAL;
+        }
+        if (!k.t->L.fast_sip) {
+            msg = at + "needs a sip tensor (the fast path)";
+            return DM_EINVAL;
+        }
+        if (k.t->device != links[0].t->device) {
+            msg = at + "tensors on different devices";
+            return DM_EINVAL;
+        }
+        if ((reinterpret_cast<uintptr_t>(k.x) & 15) != 0) {
+            msg = at + "activations must be 16-byte aligned";
+            return DM_EINVAL;
+        }
+        const dm_gather &g = k.g;
+        if (g.world < 1 || g.world > DM_MAX_RANKS || g.rank < 0 || g.rank >= g.world) {
+            msg = at + "rank outside a world of 1.." + std::to_string(DM_MAX_RANKS);
+            return DM_EINVAL;
+        }
+        if (g.slot < k.t->L.rows) {
+            msg = at + "slot smaller than this rank's rows";
+            return DM_EINVAL;
+        }
+        for (int r = 0; r < g.world; ++r)
+            if (!g.peer_out[r] || !g.peer_flags[r]) {
+                msg = at + "null peer pointer";
+                return DM_EINVAL;
+            }
+        if (!g.gen || !g.done || !g.abort) {
+            msg = at + "counters incomplete";
+            return DM_EINVAL;
+        }
+        if (k.wait < -1 || k.wait >= n) {
+            msg = at + "wait index outside -1.." + std::to_string(n - 1);
+            return DM_EINVAL;
+        }
+        if (k.wait >= 0 && (links[k.wait].g.world != g.world || links[k.wait].g.rank != g.rank)) {
+            msg = at + "waits on a link of another world";
+            return DM_EINVAL;
+        }
+        dm_gather gg = g;
+        gg.wait_flags = k.wait >= 0 ? links[k.wait].g.peer_flags[g.rank] : nullptr;
+        gg.wait_gen = nullptr;
+        SipPlan P;
+        if (int rc = prepare_sip_args(k.t, reinterpret_cast<const uint16_t *>(k.x), k.t->L.C, (int)M, 1, (int)M,
+                                      reinterpret_cast<const uint16_t *>(k.bias), nullptr, out_f32, k.t->S.partials,
+                                      k.t->S.counters, k.t->S.err, k.t->S.max_workers, &gg, args[(size_t)i], P, msg,
+                                      kChainArgsBytes)) {
+            msg = at + msg;
+            return rc;
+        }
+        args[(size_t)i].wait_prev = k.wait >= i ? 1 : 0;
+        *grid = std::max<int>(*grid, (int)P.grid);
+        *smem = std::max<int>(*smem, (P.smem + 127) & ~127);
+    }
+    // one rank: a link polls its predecessor's CTA count itself
+    for (int32_t i = 0; i < n; ++i)
+        if (links[i].wait >= 0 && links[i].g.world == 1) {
+            args[(size_t)i].wait_done = links[links[i].wait].g.done;
+            args[(size_t)i].wait_grid = args[(size_t)links[i].wait].grid;
+        }
+    return DM_OK;
+}
+
+int launch_chain(const SipArgs *d_links, int32_t n, int Mv, int grid, int smem, uint32_t *words, int device,
+                 void *stream, std::string &msg) {
+    using Kern = void (*)(const SipArgs *, int32_t, uint32_t *, int32_t);
+    static const Kern kernels[kMaxVirtualRows + 1] = {
+        nullptr, sip_chain_kernel<1>, sip_chain_kernel<2>, sip_chain_kernel<3>, sip_chain_kernel<4>,
+        sip_chain_kernel<5>, sip_chain_kernel<6>, sip_chain_kernel<7>, sip_chain_kernel<8>};
+    static std::atomic<uint64_t> attr_set[kMaxVirtualRows + 1];
+    if (Mv < 1 || Mv > kMaxVirtualRows) {
+        msg = "dm_chain: 1..8 activation rows";
+        return DM_EINVAL;
+    }
+    const Kern kern = kernels[Mv];
+    const uint64_t dev_bit = device >= 0 && device < 64 ? 1ull << device : 0ull;
+    if (!dev_bit || !(attr_set[Mv].load() & dev_bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) {
+            msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+            return DM_ECUDA;
+        }
+        attr_set[Mv].fetch_or(dev_bit);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kSipThreads);
+    cfg.dynamicSmemBytes = (size_t)smem + kChainArgsBytes;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the links wait on one another's CTAs
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, d_links, n, words, (int32_t)smem);
+    if (e != cudaSuccess) {
+        msg = std::string("sip_chain_kernel: ") + cudaGetErrorString(e);
         return DM_ECUDA;
     }
     return DM_OK;
@@ -1048,3 +1302,91 @@ int launch_decode_sip(const dm_tensor *t, uint16_t *out, void *stream, std::stri
 }
 
 }  // namespace dm
+
+// ------------------------------------------------------------ the chain --
+
+struct dm_chain {
+    int32_t device = 0, n = 0, Mv = 0, grid = 0, smem = 0;
+    dm::SipArgs *d_links = nullptr;
+    uint32_t *d_words = nullptr;  // [0] the chain's launch count, [1] CTAs that have left the running launch
+    void *d_alloc = nullptr;
+};
+
+namespace {
+
+struct ChainDevice {
+    int prev = -1;
+    explicit ChainDevice(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~ChainDevice() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int chain_fail(char *err, size_t len, int code, const std::string &msg) {
+    dm::set_error(err, len, msg);
+    return code;
+}
+
+}  // namespace
+
+extern "C" int dm_chain_create(const dm_chain_link *links, int32_t n, int64_t M, int32_t out_dtype, dm_chain **out,
+                               char *err, size_t err_len) {
+    if (!links || !out || n < 1) return chain_fail(err, err_len, DM_EINVAL, "dm_chain_create: no links");
+    *out = nullptr;
+    if (M < 1 || M > DM_MC_MAX)
+        return chain_fail(err, err_len, DM_EINVAL,
+                          "radix gemv_mc: M=" + std::to_string(M) + " outside 1.." + std::to_string(DM_MC_MAX));
+    if (out_dtype != DM_BF16 && out_dtype != DM_F32)
+        return chain_fail(err, err_len, DM_EINVAL, "dm_chain_create: dtype must be DM_BF16 or DM_F32");
+    if (!links[0].t) return chain_fail(err, err_len, DM_EINVAL, "dm_chain_create: link 0: null tensor or activations");
+    std::vector<dm::SipArgs> args;
+    int grid = 0, smem = 0;
+    std::string msg;
+    if (int rc = dm::chain_prepare(links, n, M, out_dtype == DM_F32, args, &grid, &smem, msg))
+        return chain_fail(err, err_len, rc, msg);
+    auto *c = new dm_chain;
+    c->device = links[0].t->device;
+    c->n = n;
+    c->Mv = (int32_t)M;
+    c->grid = grid;
+    c->smem = smem;
+    ChainDevice g(c->device);
+    const size_t abytes = ((size_t)n * sizeof(dm::SipArgs) + 255) & ~(size_t)255;
+    cudaError_t e = cudaMalloc(&c->d_alloc, abytes + 256);
+    if (e == cudaSuccess) {
+        c->d_links = reinterpret_cast<dm::SipArgs *>(c->d_alloc);
+        c->d_words = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(c->d_alloc) + abytes);
+        e = cudaMemcpy(c->d_links, args.data(), (size_t)n * sizeof(dm::SipArgs), cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaMemset(c->d_words, 0, 256);
+    if (e != cudaSuccess) {
+        if (c->d_alloc) cudaFree(c->d_alloc);
+        delete c;
+        return chain_fail(err, err_len, e == cudaErrorMemoryAllocation ? DM_ENOMEM : DM_ECUDA,
+                          std::string("dm_chain_create: ") + cudaGetErrorString(e));
+    }
+    *out = c;
+    return DM_OK;
+}
+
+extern "C" int dm_chain_run(const dm_chain *c, void *stream, char *err, size_t err_len) {
+    if (!c) return chain_fail(err, err_len, DM_EINVAL, "dm_chain_run: null chain");
+    ChainDevice g(c->device);
+    std::string msg;
+    if (int rc = dm::launch_chain(c->d_links, c->n, c->Mv, c->grid, c->smem, c->d_words, c->device, stream, msg))
+        return chain_fail(err, err_len, rc, msg);
+    return DM_OK;
+}
+
+extern "C" int dm_chain_destroy(dm_chain *c, char *err, size_t err_len) {
+    if (!c) return chain_fail(err, err_len, DM_EINVAL, "dm_chain_destroy: null chain");
+    ChainDevice g(c->device);
+    cudaError_t e = cudaFree(c->d_alloc);
+    delete c;
+    if (e != cudaSuccess) return chain_fail(err, err_len, DM_ECUDA, std::string("dm_chain_destroy: ") + cudaGetErrorString(e));
+    return DM_OK;
+}

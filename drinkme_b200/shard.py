@@ -226,6 +226,36 @@ class PeerGather:
                   else _lib.DM_BF16, ct.byref(self.desc(i, wait, wait_polls)),
                   ct.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
 
+    def chain(self, links) -> "GatherChain":
+        """One persistent launch over a sequence of this gather's linears
+        (dm_chain_create): `links` = [(rt, x, i, wait, bias), ...] — linear i
+        of this plan computed from activations x (contiguous bf16 [M, C],
+        16-byte aligned, e.g. another linear's output(j)[:, :C]), first
+        waiting for linear `wait`'s flags (an index into `links`: an earlier
+        link's output of this launch, or a later link's of the previous one;
+        None: no wait). Same result bits as calling gemv() link by link. The
+        plan's flags then belong to the chain: no per-linear gemv() calls."""
+        import ctypes as ct
+
+        from . import _lib
+
+        arr = (_lib.ChainLink * len(links))()
+        keep = []
+        for k, (rt, x, i, wait, bias) in enumerate(links):
+            if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.shape[0] != self.M:
+                raise ValueError(f"PeerGather.chain: link {k}: activations must be contiguous bf16 [M, C]")
+            b = bias.to(device=x.device, dtype=torch.bfloat16).contiguous() if bias is not None else None
+            keep.append((rt, x, b))
+            arr[k].t = rt["rx_handle"].ptr.value
+            arr[k].x = x.data_ptr()
+            arr[k].bias = b.data_ptr() if b is not None else None
+            arr[k].g = self.desc(i)
+            arr[k].wait = -1 if wait is None else int(wait)
+        out = ct.c_void_p()
+        _lib.call("dm_chain_create", arr, len(links), self.M,
+                  _lib.DM_F32 if self.dtype == torch.float32 else _lib.DM_BF16, ct.byref(out))
+        return GatherChain(out.value, self.device, keep)
+
     def close(self) -> None:
         """Collective: every rank stops using the others' memory, then unmaps."""
         import ctypes as ct
@@ -244,3 +274,36 @@ class PeerGather:
                 _lib.call("dm_ipc_close", ct.c_void_p(p))
         _lib.call("dm_device_free", ct.c_void_p(self.base))
         self.base = None
+
+
+class GatherChain:
+    """A chain of row-sharded linears in one persistent launch (dm_chain_run):
+    run() enqueues it on the current stream (capturable in a CUDA graph).
+    Holds the activations and biases it was built over."""
+
+    def __init__(self, handle: int, device, keep):
+        self.handle, self.device, self._keep = handle, device, keep
+
+    def run(self, stream=None) -> None:
+        import ctypes as ct
+
+        from . import _lib
+
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _lib.call("dm_chain_run", ct.c_void_p(self.handle), ct.c_void_p(s.cuda_stream))
+
+    def close(self) -> None:
+        import ctypes as ct
+
+        from . import _lib
+
+        if self.handle:
+            torch.cuda.synchronize(self.device)
+            _lib.call("dm_chain_destroy", ct.c_void_p(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -109,10 +109,11 @@ class RadixTensor:
         _lib.call("dm_tensor_clone", self.ptr, ct.byref(h))
         return RadixTensor._wrap(h, self)
 
-    def set_launch(self, slots: int = 0, split: int = 0, skew: int = -1, resident: int = -1) -> None:
+    def set_launch(self, slots: int = 0, split: int = 0, skew: int = -1, resident: int = -1,
+                   prefetch: int = -1) -> None:
         """The sip kernels' launch knobs for this tensor (dm_tensor_set_launch;
         radix_schedule.Launch.knobs() gives them from the schedule table)."""
-        _lib.call("dm_tensor_set_launch", self.ptr, ct.byref(_lib.Launch(slots, split, skew, resident)))
+        _lib.call("dm_tensor_set_launch", self.ptr, ct.byref(_lib.Launch(slots, split, skew, resident, prefetch)))
 
     def plan(self, M: int = 1, dtype=torch.bfloat16) -> dict:
         """What a GEMV of M rows would launch (dm_gemv_plan): grid, split

@@ -183,6 +183,8 @@ int dm_gemv_noalloc(const dm_tensor *t, const void *x, int32_t x_dtype, int64_t 
  * dm_decode; DM_EINVAL outside the ranges. */
 typedef struct dm_launch {
     int32_t slots, split, skew, resident;
+    int32_t prefetch; /* units past the staged ones whose weights each CTA asks into L2 before it waits for the
+                         activations (-1: the default, none; 0: none; at most 32) */
 } dm_launch;
 int dm_tensor_set_launch(dm_tensor *t, const dm_launch *launch, char *err, size_t err_len);
 
@@ -241,6 +243,36 @@ typedef struct dm_gather {
  * another: run one rank per GPU. */
 int dm_gemv_gather(const dm_tensor *t, const void *x, int64_t M, const void *bias, int32_t out_dtype,
                    const dm_gather *g, void *stream, char *err, size_t err_len);
+
+/* A sequence of dm_gemv_gather calls in ONE persistent launch (a chain):
+ * the reference runs one module call per linear (src/drinkme/codec/
+ * swap.py:426-456) and has no counterpart for the sequence; this is the
+ * per-linear route with the launches, and their start and drain, taken out.
+ * Link i computes this rank's rows of its tensor from `x` into every rank's
+ * gathered buffer (g, as dm_gemv_gather; g.wait_flags / g.wait_gen are not
+ * read) and raises its flags to the chain's launch count. With wait = j it
+ * first waits, bounded, for link j's flags: this launch's output of link j
+ * when j < i, the previous launch's when j >= i (none on the first launch).
+ * Same result bits as the per-linear calls. A tensor may serve two links
+ * only when the later one waits (directly or through others) on the earlier.
+ * A PeerGather's flags serve either one chain or per-linear calls, not both.
+ * bf16 activations, 16-byte aligned, 1 <= M <= 8, sip tensors on one device.
+ * dm_chain_create copies the links' kernel arguments to the device (one
+ * allocation; the chain's launch count starts at zero); dm_chain_run is one
+ * cooperative kernel launch, no host synchronisation (CUDA-graph
+ * capturable); every rank runs its chain the same number of times. */
+typedef struct dm_chain dm_chain;
+typedef struct dm_chain_link {
+    const dm_tensor *t;
+    const void *x;    /* bf16 [M][C] */
+    const void *bias; /* bf16 [rows] or NULL */
+    dm_gather g;
+    int32_t wait;     /* -1: none */
+} dm_chain_link;
+int dm_chain_create(const dm_chain_link *links, int32_t n, int64_t M, int32_t out_dtype, dm_chain **out, char *err,
+                    size_t err_len);
+int dm_chain_run(const dm_chain *c, void *stream, char *err, size_t err_len);
+int dm_chain_destroy(dm_chain *c, char *err, size_t err_len);
 
 /* CUDA IPC of a device allocation (plain peer mappings; no multicast):
  * the 64-byte handle of `dptr` (the start of a cudaMalloc block), and the

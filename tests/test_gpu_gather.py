@@ -62,7 +62,7 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, use_chain=False):
     import datetime
 
     import torch.distributed as dist
@@ -79,9 +79,18 @@ def _rank(rank, world, port, q):
         slot = sum(shard.shard_rows_padded(W.shape[0], world) for W in Ws)
         x = torch.randn(2, 4096, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(dev)
         plan = shard.PeerGather([slot, slot], 2, torch.bfloat16, rank, world, dev)
-        for step in range(4):
-            plan.gemv(rt, x, 0, wait=1)
-            plan.gemv(rt, x, 1, wait=0)
+        if use_chain:
+            # both linears in one persistent launch per step, the same waits
+            chain = plan.chain([(rt, x, 0, 1, None), (rt, x, 1, 0, None)])
+            for step in range(4):
+                chain.run()
+            torch.cuda.synchronize()
+            assert int(plan.launch_count(1)) == 4
+            chain.close()
+        else:
+            for step in range(4):
+                plan.gemv(rt, x, 0, wait=1)
+                plan.gemv(rt, x, 1, wait=0)
         torch.cuda.synchronize()
         got = plan.output(1).cpu()
         err = rt["rx_handle"].device_error()
@@ -93,12 +102,13 @@ def _rank(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_gather_two_gpus_equals_one_gpu():
+@pytest.mark.parametrize("use_chain", [False, True], ids=["per-linear", "chain"])
+def test_gather_two_gpus_equals_one_gpu(use_chain):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, use_chain)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda t: t[0])
