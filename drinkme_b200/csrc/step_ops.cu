@@ -5,10 +5,11 @@
 // rotary embedding + KV-cache write, grouped-query decode attention over
 // the cache (split over the sequence, then combined) and SiLU(gate) * up.
 // Every launch reads the position from device memory, so a captured graph
-// serves every step. bf16 storage, fp32 arithmetic. Each kernel lets the
-// launch after it start early (programmatic dependent launch): a sip GEMV
-// stages its first weights while these run and waits for them to finish
-// before it reads their output.
+// serves every step. bf16 storage, fp32 arithmetic. Every launch is a
+// programmatic dependent launch both ways: each kernel is scheduled while its
+// predecessor finishes and waits for it on the device before reading, and
+// lets its own successor start early (a sip GEMV stages its first weights
+// while these run and waits for them before it reads their output).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -41,6 +42,7 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 __global__ void add_rmsnorm_kernel(uint16_t *h, const uint16_t *delta, const uint16_t *w, uint16_t *out, int n,
                                    float eps) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     __shared__ float red[32];
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -64,6 +66,7 @@ __global__ void qk_norm_rope_cache_kernel(const uint16_t *qkv, const uint16_t *q
                                           const float *cosv, const float *sinv, const int64_t *pos, uint16_t *q_out,
                                           uint16_t *kc, uint16_t *vc, int nh, int nkv, int hd, float eps) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (head >= nh + 2 * nkv) return;
     const int64_t p = *pos;
@@ -101,6 +104,7 @@ __global__ void qk_norm_rope_cache_kernel(const uint16_t *qkv, const uint16_t *q
 __global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
                                   float *part, int nh, int nkv, int hd, int nchunks, float scale) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     const int g = blockIdx.x, j = blockIdx.y, lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
     const int grp = nh / nkv;
     if (wq >= grp) return;
@@ -138,6 +142,7 @@ __global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const u
 __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint16_t *out, int nh, int hd,
                                     int nchunks) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     const int head = blockIdx.x, lane = threadIdx.x;
     const int used = (int)min((int64_t)nchunks, (*pos + kAttnChunk) / kAttnChunk);
     const float *p = part + (int64_t)head * nchunks * (hd + 2);
@@ -166,6 +171,7 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
                                   unsigned int *count, uint16_t *out, int nh, int nkv, int hd, int nchunks, float eps,
                                   float scale) {
     pdl_launch_dependents();
+    pdl_wait();
     __shared__ int last;
     const int g = blockIdx.x, j = blockIdx.y, lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
     const int grp = nh / nkv, half = hd / 2, per = hd / 32;
@@ -258,6 +264,7 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
 
 __global__ void silu_mul_kernel(const uint16_t *gu, uint16_t *out, int n) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
+    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float g = bf(gu[i]), u = bf(gu[n + i]);
@@ -271,6 +278,23 @@ int launched(const char *what, std::string &msg) {
     return DM_ECUDA;
 }
 
+// Every launch here lets the kernel start while its predecessor finishes
+// (programmatic dependent launch; the kernel waits for it on the device
+// before reading anything).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, void *stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 }  // namespace
 }  // namespace dm
 
@@ -280,8 +304,8 @@ extern "C" int dm_step_add_rmsnorm(void *h, const void *delta, const void *w, vo
         dm::set_error(err, err_len, "dm_step_add_rmsnorm: bad arguments");
         return DM_EINVAL;
     }
-    dm::add_rmsnorm_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(
-        (uint16_t *)h, (const uint16_t *)delta, (const uint16_t *)w, (uint16_t *)out, (int)n, eps);
+    dm::launch_pdl(dm::add_rmsnorm_kernel, dim3(1), dim3(1024), stream, (uint16_t *)h, (const uint16_t *)delta,
+                   (const uint16_t *)w, (uint16_t *)out, (int)n, eps);
     std::string msg;
     int rc = dm::launched("add_rmsnorm_kernel", msg);
     if (rc) dm::set_error(err, err_len, msg);
@@ -298,9 +322,9 @@ extern "C" int dm_step_qk_rope_cache(const void *qkv, const void *qn, const void
         return DM_EINVAL;
     }
     const int heads = nh + 2 * nkv, per = 4;
-    dm::qk_norm_rope_cache_kernel<<<(heads + per - 1) / per, 32 * per, 0, (cudaStream_t)stream>>>(
-        (const uint16_t *)qkv, (const uint16_t *)qn, (const uint16_t *)kn, cosv, sinv, pos, (uint16_t *)q_out,
-        (uint16_t *)kcache, (uint16_t *)vcache, nh, nkv, hd, eps);
+    dm::launch_pdl(dm::qk_norm_rope_cache_kernel, dim3((heads + per - 1) / per), dim3(32 * per), stream,
+                   (const uint16_t *)qkv, (const uint16_t *)qn, (const uint16_t *)kn, cosv, sinv, pos,
+                   (uint16_t *)q_out, (uint16_t *)kcache, (uint16_t *)vcache, nh, nkv, hd, eps);
     std::string msg;
     int rc = dm::launched("qk_norm_rope_cache_kernel", msg);
     if (rc) dm::set_error(err, err_len, msg);
@@ -322,10 +346,11 @@ extern "C" int dm_step_attention(const void *q, const void *kcache, const void *
     }
     const int nchunks = (int)((max_len + dm::kAttnChunk - 1) / dm::kAttnChunk);
     cudaStream_t s = (cudaStream_t)stream;
-    dm::attn_split_kernel<<<dim3(nkv, nchunks), 32 * (nh / nkv), 0, s>>>(
-        (const uint16_t *)q, (const uint16_t *)kcache, (const uint16_t *)vcache, pos, work, nh, nkv, hd, nchunks,
-        1.0f / sqrtf((float)hd));
-    dm::attn_combine_kernel<<<nh, 32, 0, s>>>(work, pos, (uint16_t *)out, nh, hd, nchunks);
+    dm::launch_pdl(dm::attn_split_kernel, dim3(nkv, nchunks), dim3(32 * (nh / nkv)), s, (const uint16_t *)q,
+                   (const uint16_t *)kcache, (const uint16_t *)vcache, pos, work, nh, nkv, hd, nchunks,
+                   1.0f / sqrtf((float)hd));
+    dm::launch_pdl(dm::attn_combine_kernel, dim3(nh), dim3(32), s, (const float *)work, pos, (uint16_t *)out, nh,
+                   hd, nchunks);
     std::string msg;
     int rc = dm::launched("attention kernels", msg);
     if (rc) dm::set_error(err, err_len, msg);
@@ -349,10 +374,10 @@ extern "C" int dm_step_attention_block(const void *qkv, const void *qn, const vo
     float *part = reinterpret_cast<float *>(work);
     unsigned int *count = reinterpret_cast<unsigned int *>(
         reinterpret_cast<uint8_t *>(work) + (dm_step_attention_workspace_bytes(nh, hd, max_len) + 255) / 256 * 256);
-    dm::attn_block_kernel<<<dim3(nkv, nchunks), 32 * (nh / nkv), 0, (cudaStream_t)stream>>>(
-        (const uint16_t *)qkv, (const uint16_t *)qn, (const uint16_t *)kn, cos_table, sin_table, pos,
-        (uint16_t *)kcache, (uint16_t *)vcache, part, count, (uint16_t *)out, nh, nkv, hd, nchunks, eps,
-        1.0f / sqrtf((float)hd));
+    dm::launch_pdl(dm::attn_block_kernel, dim3(nkv, nchunks), dim3(32 * (nh / nkv)), stream, (const uint16_t *)qkv,
+                   (const uint16_t *)qn, (const uint16_t *)kn, cos_table, sin_table, pos, (uint16_t *)kcache,
+                   (uint16_t *)vcache, part, count, (uint16_t *)out, nh, nkv, hd, nchunks, eps,
+                   1.0f / sqrtf((float)hd));
     std::string msg;
     int rc = dm::launched("attn_block_kernel", msg);
     if (rc) dm::set_error(err, err_len, msg);
@@ -364,8 +389,8 @@ extern "C" int dm_step_silu_mul(const void *gu, void *out, int64_t n, void *stre
         dm::set_error(err, err_len, "dm_step_silu_mul: bad arguments");
         return DM_EINVAL;
     }
-    dm::silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t *)gu,
-                                                                                       (uint16_t *)out, (int)n);
+    dm::launch_pdl(dm::silu_mul_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), stream, (const uint16_t *)gu,
+                   (uint16_t *)out, (int)n);
     std::string msg;
     int rc = dm::launched("silu_mul_kernel", msg);
     if (rc) dm::set_error(err, err_len, msg);
