@@ -275,3 +275,24 @@ def test_eligible_and_in_place_adoption():
     assert not swap.codec_tree(m)
     assert swap.install_stock_gemv(m, "cpu", "b200") == 0
     assert swap.install_narrow(m, "cpu") == []
+
+
+def test_chain_create_refuses_bad_arguments_without_a_gpu():
+    """dm_chain_create checks its arguments before it touches a device: no
+    links, M outside 1..8 (the reference's gemv_mc ValueError) and an output
+    dtype other than bf16 / fp32 are refused with named errors."""
+    import ctypes as ct
+
+    arr = (_lib.ChainLink * 1)()
+    out = ct.c_void_p()
+    with pytest.raises(ValueError, match="no links"):
+        _lib.call("dm_chain_create", arr, 0, 1, _lib.DM_BF16, ct.byref(out))
+    with pytest.raises(ValueError, match="outside 1..8"):
+        _lib.call("dm_chain_create", arr, 1, 9, _lib.DM_BF16, ct.byref(out))
+    with pytest.raises(ValueError, match="dtype"):
+        _lib.call("dm_chain_create", arr, 1, 1, 7, ct.byref(out))
+    with pytest.raises(ValueError, match="null tensor"):
+        _lib.call("dm_chain_create", arr, 1, 1, _lib.DM_BF16, ct.byref(out))
+    with pytest.raises(ValueError, match="null chain"):
+        _lib.call("dm_chain_run", None, None)
+    assert ct.sizeof(_lib.ChainLink) == 224  # t, x, bias, dm_gather (192), wait: the header's layout
