@@ -226,7 +226,7 @@ class PeerGather:
                   else _lib.DM_BF16, ct.byref(self.desc(i, wait, wait_polls)),
                   ct.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
 
-    def chain(self, links) -> "GatherChain":
+    def chain(self, links, wait_polls: int = 0) -> "GatherChain":
         """One persistent launch over a sequence of this gather's linears
         (dm_chain_create): `links` = [(rt, x, i, wait, bias), ...] — linear i
         of this plan computed from activations x (contiguous bf16 [M, C],
@@ -234,7 +234,9 @@ class PeerGather:
         waiting for linear `wait`'s flags (an index into `links`: an earlier
         link's output of this launch, or a later link's of the previous one;
         None: no wait). Same result bits as calling gemv() link by link. The
-        plan's flags then belong to the chain: no per-linear gemv() calls."""
+        plan's flags then belong to the chain: no per-linear gemv() calls.
+        A wait gives up after `wait_polls` polls (0: the library's bound),
+        recording kErrWaitPeer in the waiting link's tensor and the abort word."""
         import ctypes as ct
 
         from . import _lib
@@ -249,7 +251,7 @@ class PeerGather:
             arr[k].t = rt["rx_handle"].ptr.value
             arr[k].x = x.data_ptr()
             arr[k].bias = b.data_ptr() if b is not None else None
-            arr[k].g = self.desc(i)
+            arr[k].g = self.desc(i, None, wait_polls)
             arr[k].wait = -1 if wait is None else int(wait)
         out = ct.c_void_p()
         _lib.call("dm_chain_create", arr, len(links), self.M,

@@ -99,3 +99,37 @@ def test_chain_refuses_bad_links():
             plan.chain([(rts[0], buf[:, 1:], 0, None, None)])
     finally:
         plan.close()
+
+
+def test_chain_wait_that_never_completes_returns_with_an_error():
+    """A link whose predecessor's CTA count never reaches this run's target
+    (reset by hand after the first run) gives up after its poll bound,
+    records kErrWaitPeer (4) in its tensor's error word and sets the abort
+    word; the launch still ends and the GPU stays usable (a plain GEMV
+    afterwards equals the first run's output)."""
+    from drinkme_b200.tensor import device_view
+
+    rts = _tensors()[:2]
+    x = torch.randn(1, SHAPES[0][1], generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(DEV)
+    plan = shard.PeerGather([R for R, _ in SHAPES[:2]], 1, torch.bfloat16, 0, 1, DEV)
+    chain = None
+    try:
+        chain = plan.chain([(rts[0], x, 0, None, None), (rts[1], plan.output(0)[:, :SHAPES[1][1]], 1, 0, None)],
+                           wait_polls=1 << 12)
+        chain.run()
+        torch.cuda.synchronize()
+        want = plan.output(1)[:, :SHAPES[1][0]].clone()
+        assert rts[1]["rx_handle"].device_error() == 0 and int(plan.abort_word()) == 0
+        # link 0's CTA count (the word after its launch count) back to zero:
+        # the next run's link 1 waits for a count it never sees
+        device_view(plan.base + plan.cnt_off + 4, (1,), torch.int32, DEV).fill_(0)
+        chain.run()
+        torch.cuda.synchronize()
+        assert rts[1]["rx_handle"].device_error() == 4  # kErrWaitPeer
+        assert int(plan.abort_word()) != 0
+        y = radix_ops.gemv_mc_fused(rts[1], plan.output(0)[:, :SHAPES[1][1]].contiguous(), None, torch.bfloat16)
+        assert torch.equal(y, want)
+    finally:
+        if chain is not None:
+            chain.close()
+        plan.close()
