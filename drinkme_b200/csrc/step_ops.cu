@@ -21,7 +21,10 @@
 namespace dm {
 namespace {
 
-constexpr int kAttnChunk = 128;  // cache rows per attention CTA
+// Cache rows per attention CTA: a warp walks its chunk's rows in order, so
+// the chunk bounds the serial work (32: at position 896 the 8B step took
+// 6.77 ms with 128-row chunks).
+constexpr int kAttnChunk = 32;
 
 __device__ __forceinline__ float bf(uint16_t b) { return bf16_bits_to_f32(b); }
 __device__ __forceinline__ uint16_t to_bf(float f) { return f32_to_bf16_bits(f); }
@@ -97,8 +100,43 @@ __global__ void qk_norm_rope_cache_kernel(const uint16_t *qkv, const uint16_t *q
     }
 }
 
+// The online softmax of one query head (this warp; lane l holds elements
+// 4l .. 4l + 3 of q, already scaled) over cache rows [r0, r1) of kv head g:
+// the rows are taken in order, one at a time, as a plain loop would, but
+// the keys and values of eight rows are loaded before their arithmetic (the
+// rows were just written: each load is an L2 round trip, which a row-by-row
+// loop would wait for once per row).
+__device__ __forceinline__ void attend_rows(const float qv[4], const uint16_t *kc, const uint16_t *vc, int64_t r0,
+                                            int64_t r1, int nkv, int g, int hd, int lane, float &m, float &l,
+                                            float acc[4]) {
+    constexpr int kAhead = 8;
+    for (int64_t rb = r0; rb < r1; rb += kAhead) {
+        uint2 kk[kAhead], vv[kAhead];
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+            const int64_t r = rb + u < r1 ? rb + u : r1 - 1;  // in bounds; unused past r1
+            kk[u] = *reinterpret_cast<const uint2 *>(kc + (r * nkv + g) * hd + lane * 4);
+            vv[u] = *reinterpret_cast<const uint2 *>(vc + (r * nkv + g) * hd + lane * 4);
+        }
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+            if (rb + u >= r1) break;
+            const float k4[4] = {bf(kk[u].x & 0xffffu), bf(kk[u].x >> 16), bf(kk[u].y & 0xffffu), bf(kk[u].y >> 16)};
+            const float v4[4] = {bf(vv[u].x & 0xffffu), bf(vv[u].x >> 16), bf(vv[u].y & 0xffffu), bf(vv[u].y >> 16)};
+            float s = 0.f;
+            for (int e = 0; e < 4; ++e) s += qv[e] * k4[e];
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const float mn = fmaxf(m, s);
+            const float a = __expf(m - mn), b = __expf(s - mn);
+            for (int e = 0; e < 4; ++e) acc[e] = acc[e] * a + b * v4[e];
+            l = l * a + b;
+            m = mn;
+        }
+    }
+}
+
 // Split decode attention: CTA (kv head g, chunk j) covers cache rows
-// [128 j, 128 j + 128) below *pos + 1; a warp per query head of the group
+// [32 j, 32 j + 32) below *pos + 1; a warp per query head of the group
 // keeps a running max, sum and weighted value sum, written to
 // part[head][j] = {m, l, acc[hd]}.
 __global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
@@ -118,18 +156,7 @@ __global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const u
         acc[e] = 0.f;
     }
     float m = -INFINITY, l = 0.f;
-    for (int64_t r = r0; r < r1; ++r) {
-        const uint16_t *kr = kc + (r * nkv + g) * hd + lane * per;
-        float s = 0.f;
-        for (int e = 0; e < per; ++e) s += qv[e] * bf(kr[e]);
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float mn = fmaxf(m, s);
-        const float a = __expf(m - mn), b = __expf(s - mn);
-        const uint16_t *vr = vc + (r * nkv + g) * hd + lane * per;
-        for (int e = 0; e < per; ++e) acc[e] = acc[e] * a + b * bf(vr[e]);
-        l = l * a + b;
-        m = mn;
-    }
+    attend_rows(qv, kc, vc, r0, r1, nkv, g, hd, lane, m, l, acc);
     float *out = part + ((int64_t)head * nchunks + j) * (hd + 2);
     if (lane == 0) {
         out[0] = m;
@@ -147,9 +174,11 @@ __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint1
     const int used = (int)min((int64_t)nchunks, (*pos + kAttnChunk) / kAttnChunk);
     const float *p = part + (int64_t)head * nchunks * (hd + 2);
     float M = -INFINITY;
+#pragma unroll 8
     for (int j = 0; j < used; ++j) M = fmaxf(M, p[j * (hd + 2)]);
     const int per = hd / 32;
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+#pragma unroll 8
     for (int j = 0; j < used; ++j) {
         const float *pj = p + j * (hd + 2);
         if (pj[1] == 0.f) continue;
@@ -218,18 +247,7 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     __syncthreads();
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, m = -INFINITY, l = 0.f;
     for (int e = 0; e < per; ++e) qv[e] *= scale;
-    for (int64_t r = r0; r < r1; ++r) {
-        const uint16_t *kr = kc + (r * nkv + g) * hd + lane * per;
-        float sc = 0.f;
-        for (int e = 0; e < per; ++e) sc += qv[e] * bf(kr[e]);
-        for (int o = 16; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-        const float mn = fmaxf(m, sc);
-        const float a = __expf(m - mn), b = __expf(sc - mn);
-        const uint16_t *vr = vc + (r * nkv + g) * hd + lane * per;
-        for (int e = 0; e < per; ++e) acc[e] = acc[e] * a + b * bf(vr[e]);
-        l = l * a + b;
-        m = mn;
-    }
+    attend_rows(qv, kc, vc, r0, r1, nkv, g, hd, lane, m, l, acc);
     float *pp = part + ((int64_t)head * nchunks + j) * (hd + 2);
     if (lane == 0) {
         pp[0] = m;
@@ -249,8 +267,10 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     const int used = (int)min((int64_t)nchunks, (p + kAttnChunk) / kAttnChunk);
     const float *ph = part + (int64_t)head * nchunks * (hd + 2);
     float M = -INFINITY;
+#pragma unroll 8
     for (int c = 0; c < used; ++c) M = fmaxf(M, __ldcg(ph + c * (hd + 2)));
     float o4[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+#pragma unroll 8
     for (int c = 0; c < used; ++c) {
         const float *pc = ph + c * (hd + 2);
         const float lc = __ldcg(pc + 1);

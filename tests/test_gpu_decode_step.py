@@ -66,7 +66,7 @@ def test_attention_block_equals_two_launches(nh, nkv):
     def ptr(t):
         return P(t.data_ptr())
 
-    for p in (0, 1, 127, 128, 129, 255, 256, 399):
+    for p in (0, 1, 31, 32, 33, 127, 128, 129, 255, 256, 399):
         qkv = rnd(1, (nh + 2 * nkv) * hd)
         pos = torch.tensor([p], dtype=torch.int64, device=DEV)
         q = torch.empty(nh, hd, dtype=torch.bfloat16, device=DEV)
