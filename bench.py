@@ -76,8 +76,8 @@ def parse():
                     help="N > 1: the output gather fused into the GEMV over NVLink (peer), or NCCL all-gather")
     ap.add_argument("--launch", choices=("auto", "chain", "linear"), default="auto",
                     help="the step as one persistent launch over every linear (dm_chain_run), or one launch per "
-                         "linear (the per-linear plugin route); auto: per-linear on one GPU, the chain on more "
-                         "(the faster of the two measured at each); the other is timed beside it")
+                         "linear (the per-linear plugin route); auto: per-linear (measured faster at N = 1 and 4, "
+                         "2.4 %% slower at N = 2); the other is timed beside it")
     ap.add_argument("--variants", type=int, default=2,
                     help="distinct random tensors per shape; every layer still gets its own HBM copy")
     ap.add_argument("--no-secondary", action="store_true", help="skip the qwen3-8b chain beside the headline")
@@ -829,7 +829,7 @@ def main():
     fuse = not a.no_fuse
     layers, stats = build_stack(a.workload, rank, world, device, a.variants, log, fuse)
     if a.launch == "auto":
-        a.launch = "linear" if world == 1 or a.gather != "peer" else "chain"
+        a.launch = "linear"
     chain = Chain(a.workload, layers, rank, world, device, fuse=fuse, gather=a.gather, launch=a.launch)
     clocks = ClockSampler(local)
     clocks.start()
