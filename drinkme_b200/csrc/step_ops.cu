@@ -42,23 +42,63 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 
 // h <- h + delta (rounded to bf16, as an in-place bf16 add), then
 // out = h * rsqrt(mean(h^2) + eps) * w; one CTA, one row.
+// Rows of up to kNormReg * blockDim elements keep each thread's elements in
+// registers, all of a thread's loads in flight at once (each is an L2 round
+// trip), the norm weights fetched before the wait for the predecessor; the
+// sum runs in the same element order either way.
+constexpr int kNormReg = 8;
 __global__ void add_rmsnorm_kernel(uint16_t *h, const uint16_t *delta, const uint16_t *w, uint16_t *out, int n,
                                    float eps) {
     pdl_launch_dependents();  // the next GEMV may stage its weights meanwhile
-    pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     __shared__ float red[32];
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float x = bf(h[i]);
-        if (delta) {
-            x = bf(to_bf(x + bf(delta[i])));
-            h[i] = to_bf(x);
+    const int bd = blockDim.x, t = threadIdx.x;
+    const bool regs = n <= kNormReg * bd;
+    uint16_t wv[kNormReg];
+    if (regs) {
+#pragma unroll
+        for (int k = 0; k < kNormReg; ++k)
+            if (t + k * bd < n) wv[k] = w[t + k * bd];  // a constant: no need to wait for it
+    }
+    pdl_wait();  // launched early: the producer of this kernel's inputs has finished
+    float ss = 0.f, xs[kNormReg];
+    if (regs) {
+        uint16_t hv[kNormReg], dv[kNormReg];
+#pragma unroll
+        for (int k = 0; k < kNormReg; ++k)
+            if (t + k * bd < n) {
+                hv[k] = h[t + k * bd];
+                if (delta) dv[k] = delta[t + k * bd];
+            }
+#pragma unroll
+        for (int k = 0; k < kNormReg; ++k)
+            if (t + k * bd < n) {
+                float x = bf(hv[k]);
+                if (delta) {
+                    x = bf(to_bf(x + bf(dv[k])));
+                    h[t + k * bd] = to_bf(x);
+                }
+                xs[k] = x;
+                ss += x * x;
+            }
+    } else {
+        for (int i = t; i < n; i += bd) {
+            float x = bf(h[i]);
+            if (delta) {
+                x = bf(to_bf(x + bf(delta[i])));
+                h[i] = to_bf(x);
+            }
+            ss += x * x;
         }
-        ss += x * x;
     }
     const float r = rsqrtf(block_sum(ss, red) / (float)n + eps);
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = to_bf(bf(to_bf(bf(h[i]) * r)) * bf(w[i]));
+    if (regs) {
+#pragma unroll
+        for (int k = 0; k < kNormReg; ++k)
+            if (t + k * bd < n) out[t + k * bd] = to_bf(bf(to_bf(xs[k] * r)) * bf(wv[k]));
+    } else {
+        for (int i = t; i < n; i += bd) out[i] = to_bf(bf(to_bf(bf(h[i]) * r)) * bf(w[i]));
+    }
 }
 
 // A warp per head of the fused q|k|v row: q and k heads get RMSNorm over
@@ -200,14 +240,26 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
                                   unsigned int *count, uint16_t *out, int nh, int nkv, int hd, int nchunks, float eps,
                                   float scale) {
     pdl_launch_dependents();
-    pdl_wait();
     __shared__ int last;
     const int g = blockIdx.x, j = blockIdx.y, lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
     const int grp = nh / nkv, half = hd / 2, per = hd / 32;
+    // what does not depend on the kernel before this one, fetched before the
+    // wait for it: the position (advanced between steps, before the step's
+    // first kernel), the norm weights and the rotary row of this lane's
+    // elements
     const int64_t p = *pos, live = p + 1;
+    float wq4[4], wk4[4], c4[4], s4[4];
+    for (int e = 0; e < per; ++e) {
+        const int idx = lane * per + e, i = idx < half ? idx : idx - half;
+        wq4[e] = bf(qn[idx]);
+        wk4[e] = bf(kn[idx]);
+        c4[e] = cosv[p * half + i];
+        s4[e] = sinv[p * half + i];
+    }
+    pdl_wait();
     // rotate-half pairs: lane l holds elements l*per .. l*per+3; the partner
     // of element e is e +- hd/2, held by lane (l +- 16)
-    auto norm_rope = [&](const uint16_t *src, const uint16_t *wn, float v[4]) {
+    auto norm_rope = [&](const uint16_t *src, const float wn[4], float v[4]) {
         // the sum of squares in qk_norm_rope_cache_kernel's order (lane l
         // adds elements l, l + 32, ...), so that the bits match it
         float ss = 0.f;
@@ -218,25 +270,24 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
         for (int e = 0; e < per; ++e) v[e] = bf(src[lane * per + e]);
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float r = rsqrtf(ss / (float)hd + eps);
-        for (int e = 0; e < per; ++e) v[e] = bf(to_bf(bf(to_bf(v[e] * r)) * bf(wn[lane * per + e])));
+        for (int e = 0; e < per; ++e) v[e] = bf(to_bf(bf(to_bf(v[e] * r)) * wn[e]));
         // rotate-half: the partner of element e (lane l) sits in lane l ^ 16
         float o4[4];
         for (int e = 0; e < per; ++e) {
             const int idx = lane * per + e;
             const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-            const int i = idx < half ? idx : idx - half;
-            const float c = cosv[p * half + i], sn = sinv[p * half + i];
+            const float c = c4[e], sn = s4[e];
             o4[e] = idx < half ? v[e] * c - partner * sn : v[e] * c + partner * sn;
         }
         for (int e = 0; e < per; ++e) v[e] = bf(to_bf(o4[e]));
     };
     const int head = g * grp + wq;
     float qv[4];
-    norm_rope(qkv + (int64_t)head * hd, qn, qv);
+    norm_rope(qkv + (int64_t)head * hd, wq4, qv);
     const int64_t r0 = (int64_t)j * kAttnChunk, r1 = min(live, r0 + kAttnChunk);
     if (p >= r0 && p < r0 + kAttnChunk && wq == 0) {  // this chunk holds the new row
         float kv4[4];
-        norm_rope(qkv + (int64_t)(nh + g) * hd, kn, kv4);
+        norm_rope(qkv + (int64_t)(nh + g) * hd, wk4, kv4);
         uint16_t *kd = kc + (p * nkv + g) * hd, *vd = vc + (p * nkv + g) * hd;
         const uint16_t *vs = qkv + (int64_t)(nh + nkv + g) * hd;
         for (int e = 0; e < per; ++e) {

@@ -217,3 +217,40 @@ class DecodeStack:
                 h = h + (torch.nn.functional.silu(gu[:, : s["inter"]]) * gu[:, s["inter"]:]) @ W[li]["down"].T
             logits = rms(h, self.norm) @ self.head.float().T
         return logits
+
+
+def main(argv=None) -> int:
+    """`python -m drinkme_b200.decode_step`: device time per token of the
+    graphed Qwen3-8B-shaped step (synthetic weights), at positions from
+    `--position` on."""
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shape", choices=tuple(QWEN3), default="qwen3-8b")
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--position", type=int, default=0)
+    ap.add_argument("--max-len", type=int, default=1024)
+    a = ap.parse_args(argv)
+    st = DecodeStack(QWEN3[a.shape], "cuda:0", max_len=a.max_len, seed=11)
+    st.reset(token=1)
+    st.capture()
+    st.pos.fill_(a.position)
+    for _ in range(a.warmup):
+        st.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.steps):
+        st.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / a.steps
+    print(json.dumps({"shape": a.shape, "position": a.position, "steps": a.steps, "ms_per_step": round(ms, 4),
+                      "tokens_per_s": round(1e3 / ms, 2)}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
