@@ -233,8 +233,10 @@ __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint1
 // j), a warp per query head of the group. Each warp norms and rotates its q
 // head from the fused q|k|v row; the CTA whose chunk holds *pos also norms
 // and rotates k and writes k and v into row *pos of the caches first; every
-// CTA then runs its chunk of the split attention; the last CTA of kv head g
-// to finish (a counter that it resets) combines the chunks for the group.
+// CTA with live rows then runs its chunk of the split attention; the last
+// CTA of kv head g to finish (a counter of the live chunks, which it resets)
+// combines the chunks for the group. With one live chunk (*pos < 32) that
+// chunk's CTA writes the result itself.
 __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const uint16_t *kn, const float *cosv,
                                   const float *sinv, const int64_t *pos, uint16_t *kc, uint16_t *vc, float *part,
                                   unsigned int *count, uint16_t *out, int nh, int nkv, int hd, int nchunks, float eps,
@@ -248,6 +250,10 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     // first kernel), the norm weights and the rotary row of this lane's
     // elements
     const int64_t p = *pos, live = p + 1;
+    // chunks past the live rows have nothing to do: they leave at once and
+    // are not counted (the count below waits for the live chunks)
+    const int used = (int)min((int64_t)nchunks, (p + kAttnChunk) / kAttnChunk);
+    if (j >= used) return;
     float wq4[4], wk4[4], c4[4], s4[4];
     for (int e = 0; e < per; ++e) {
         const int idx = lane * per + e, i = idx < half ? idx : idx - half;
@@ -299,6 +305,17 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, m = -INFINITY, l = 0.f;
     for (int e = 0; e < per; ++e) qv[e] *= scale;
     attend_rows(qv, kc, vc, r0, r1, nkv, g, hd, lane, m, l, acc);
+    if (used == 1) {
+        // one live chunk: its softmax is the result — the combine's
+        // arithmetic over one chunk, written directly (same bits), with no
+        // partials, fence, count or combine
+        const float a = __expf(m - fmaxf(-INFINITY, m));
+        float o4[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+        L += a * l;
+        for (int e = 0; e < per; ++e) o4[e] += a * acc[e];
+        for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(o4[e] / L);
+        return;
+    }
     float *pp = part + ((int64_t)head * nchunks + j) * (hd + 2);
     if (lane == 0) {
         pp[0] = m;
@@ -309,13 +326,12 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int old = atomicAdd(count + g, 1u);
-        last = old == (unsigned int)(nchunks - 1);
+        last = old == (unsigned int)(used - 1);
         if (last) count[g] = 0u;  // for the next launch
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const int used = (int)min((int64_t)nchunks, (p + kAttnChunk) / kAttnChunk);
     const float *ph = part + (int64_t)head * nchunks * (hd + 2);
     float M = -INFINITY;
 #pragma unroll 8
