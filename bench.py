@@ -115,10 +115,18 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait for its first sample, so
+        # that a short timed region (20 steps of a few ms at N = 8) is covered
+        t0 = time.time()
+        while time.time() - t0 < 10 and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:
