@@ -143,13 +143,13 @@ __global__ void qk_norm_rope_cache_kernel(const uint16_t *qkv, const uint16_t *q
 // The online softmax of one query head (this warp; lane l holds elements
 // 4l .. 4l + 3 of q, already scaled) over cache rows [r0, r1) of kv head g:
 // the rows are taken in order, one at a time, as a plain loop would, but
-// the keys and values of eight rows are loaded before their arithmetic (the
+// the keys and values of sixteen rows are loaded before their arithmetic (the
 // rows were just written: each load is an L2 round trip, which a row-by-row
 // loop would wait for once per row).
 __device__ __forceinline__ void attend_rows(const float qv[4], const uint16_t *kc, const uint16_t *vc, int64_t r0,
                                             int64_t r1, int nkv, int g, int hd, int lane, float &m, float &l,
                                             float acc[4]) {
-    constexpr int kAhead = 8;
+    constexpr int kAhead = 16;
     for (int64_t rb = r0; rb < r1; rb += kAhead) {
         uint2 kk[kAhead], vv[kAhead];
 #pragma unroll
@@ -205,6 +205,37 @@ __global__ void attn_split_kernel(const uint16_t *q, const uint16_t *kc, const u
     for (int e = 0; e < per; ++e) out[2 + lane * per + e] = acc[e];
 }
 
+// The partial softmaxes {m, l, acc[hd]} of chunks [0, used) of one head
+// combined by one warp (lane l owns elements 4l .. 4l + 3) into the head's
+// bf16 output: the chunks folded in order with a running maximum, the
+// partials of eight chunks loaded at once (L2 round trips). Both attention
+// routes combine through this function, so their results are the same bits.
+__device__ __forceinline__ void combine_chunks(const float *ph, int used, int hd, int lane, uint16_t *outp) {
+    float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c0 = 0; c0 < used; c0 += 8) {
+        float mc[8], lc[8], ac[8][4];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (c0 + u < used) {
+                const float *pc = ph + (int64_t)(c0 + u) * (hd + 2);
+                mc[u] = __ldcg(pc);
+                lc[u] = __ldcg(pc + 1);
+                for (int e = 0; e < 4; ++e) ac[u][e] = __ldcg(pc + 2 + lane * 4 + e);
+            }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (c0 + u >= used) break;
+            if (lc[u] == 0.f) continue;
+            const float Mn = fmaxf(M, mc[u]);
+            const float so = __expf(M - Mn), sn = __expf(mc[u] - Mn);
+            L = L * so + lc[u] * sn;
+            for (int e = 0; e < 4; ++e) o[e] = o[e] * so + ac[u][e] * sn;
+            M = Mn;
+        }
+    }
+    for (int e = 0; e < 4; ++e) outp[lane * 4 + e] = to_bf(o[e] / L);
+}
+
 // A warp per query head: the chunks' partial softmaxes combined.
 __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint16_t *out, int nh, int hd,
                                     int nchunks) {
@@ -212,21 +243,7 @@ __global__ void attn_combine_kernel(const float *part, const int64_t *pos, uint1
     pdl_wait();               // launched early: the producer of this kernel's inputs has finished
     const int head = blockIdx.x, lane = threadIdx.x;
     const int used = (int)min((int64_t)nchunks, (*pos + kAttnChunk) / kAttnChunk);
-    const float *p = part + (int64_t)head * nchunks * (hd + 2);
-    float M = -INFINITY;
-#pragma unroll 8
-    for (int j = 0; j < used; ++j) M = fmaxf(M, p[j * (hd + 2)]);
-    const int per = hd / 32;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < used; ++j) {
-        const float *pj = p + j * (hd + 2);
-        if (pj[1] == 0.f) continue;
-        const float a = __expf(pj[0] - M);
-        L += a * pj[1];
-        for (int e = 0; e < per; ++e) acc[e] += a * pj[2 + lane * per + e];
-    }
-    for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(acc[e] / L);
+    combine_chunks(part + (int64_t)head * nchunks * (hd + 2), used, hd, lane, out + (int64_t)head * hd);
 }
 
 // The whole attention block of a layer in one launch: CTA (kv head g, chunk
@@ -332,21 +349,7 @@ __global__ void attn_block_kernel(const uint16_t *qkv, const uint16_t *qn, const
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const float *ph = part + (int64_t)head * nchunks * (hd + 2);
-    float M = -INFINITY;
-#pragma unroll 8
-    for (int c = 0; c < used; ++c) M = fmaxf(M, __ldcg(ph + c * (hd + 2)));
-    float o4[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < used; ++c) {
-        const float *pc = ph + c * (hd + 2);
-        const float lc = __ldcg(pc + 1);
-        if (lc == 0.f) continue;
-        const float a = __expf(__ldcg(pc) - M);
-        L += a * lc;
-        for (int e = 0; e < per; ++e) o4[e] += a * __ldcg(pc + 2 + lane * per + e);
-    }
-    for (int e = 0; e < per; ++e) out[(int64_t)head * hd + lane * per + e] = to_bf(o4[e] / L);
+    combine_chunks(part + (int64_t)head * nchunks * (hd + 2), used, hd, lane, out + (int64_t)head * hd);
 }
 
 __global__ void silu_mul_kernel(const uint16_t *gu, uint16_t *out, int n) {
